@@ -1,0 +1,384 @@
+#!/usr/bin/env python
+"""Throughput benchmark: embeddings/sec of 512-token Q8_0 sequences.
+
+One process per GPU (``torchrun --nproc-per-node N bench.py --gpus N``); each rank embeds its
+own shard of sequences on its own GPU (weak scaling, no data-path collective;
+torch.distributed only provides the barrier and the max-over-ranks timing).  Rank 0 prints
+one JSON line.
+
+  value        device-resident inputs (ids already in HBM), glp_embed_packed_device on the
+               rank's stream, CUDA events around exactly --steps steps, max over ranks
+  e2e          the public host API glp_embed_tokens (host ids in, host embeddings out: H2D of
+               the ids and D2H of the embeddings inside the timed region), max over ranks
+  roofline     the dominant kernel's algorithmic FLOP (or byte) rate from CUDA events on the
+               launching stream during the timed region, against MEASURED_PEAKS.json
+  cpu_baseline the C++ restatement of glypr's CPU path (oracle/, candle-faithful mode) on a
+               bounded sample of the same workload, all host threads (rank 0, N=1 only)
+
+``--impl reference`` times that CPU path alone on this host (rank 0; other ranks exit).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from glypr_b200 import synth  # noqa: E402
+
+METRIC = "embeddings/sec @512 tok Q8_0 at 1/2/4/8 B200; Q8_0 GEMM % of roofline"
+UNIT = "embeddings/s"
+MODEL_DESC = ("EmbeddingGemma-style encoder, 24 layers, hidden 768, 3 Q heads / 1 KV head x 256, "
+              "GeGLU 1152, dense head 768-3072-768, vocab 262144, Q8_0, synthetic random init")
+
+
+def parse_args(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["glypr_b200", "reference"], default="glypr_b200")
+    ap.add_argument("--seqs-per-gpu", type=int, default=8192,
+                    help="sequences per GPU per step (8 x 8192 = the 65,536-sequence box batch)")
+    ap.add_argument("--seq-len", type=int, default=512)
+    ap.add_argument("--max-batch-tokens", type=int, default=0, help="launch-chunk size (0 = library default)")
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
+    ap.add_argument("--model-dir", default=os.environ.get("GLYPR_BENCH_DIR",
+                                                          os.path.join(tempfile.gettempdir(), "glypr_b200_bench")))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args(argv)
+
+
+# ------------------------------------------------------------------------------ distributed
+def dist_env():
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")),
+            int(os.environ.get("LOCAL_RANK", "0")))
+
+
+def shard_range(n_total: int, world: int, rank: int):
+    """Contiguous shard [lo, hi) of n_total units for `rank` (sizes differ by at most 1)."""
+    base, rem = divmod(n_total, world)
+    lo = rank * base + min(rank, rem)
+    return lo, lo + base + (1 if rank < rem else 0)
+
+
+def max_over_ranks(value: float, world: int, device=None) -> float:
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int, device=None) -> None:
+    if world > 1:
+        import torch.distributed as dist
+        if device is not None and dist.get_backend() == "nccl":
+            dist.barrier(device_ids=[device.index])
+        else:
+            dist.barrier()
+
+
+# ------------------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi clock/throttle sampling during the timed region (200 ms period)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,utilization.gpu,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(prefix="glypr_clocks_", suffix=".csv")
+            os.close(fd)
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.fh, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self) -> dict:
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.fh.close()
+        rows = []
+        with open(self.path) as fh:
+            for line in fh:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 10:
+                    rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+        load = [r for r in rows if (num(r[4]) or 0) >= 50] or rows
+        sm = [num(r[1]) for r in load if num(r[1]) is not None]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in load for i in range(4) if r[6 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": num(rows[0][2]),
+                "power_w_max": max((num(r[3]) or 0) for r in rows), "samples": len(rows),
+                "samples_under_load": len(load), "reasons": reasons}
+
+
+# ------------------------------------------------------------------------------ peaks
+def measured_peaks() -> dict:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as fh:
+            p = json.load(fh)
+        return {"hbm_gbs": p["hbm_gbs"], "bf16_tflops": p["bf16_tflops"],
+                "bf16_tflops_sustained": p.get("bf16_tflops_sustained", p["bf16_tflops"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def ncu_traffic(kernel: str):
+    """dram bytes per launch for `kernel` from the committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    if not os.path.exists(path):
+        return None
+    with open(path) as fh:
+        data = json.load(fh)
+    return data.get(kernel)
+
+
+GEMM_KINDS = ("gemm_qkv_norm_rope", "gemm_o", "gemm_gate_up_geglu", "gemm_down", "gemm_head")
+TENSOR_KINDS = GEMM_KINDS + ("flash_attention",)
+
+
+def roofline(prof: dict, peaks: dict) -> tuple:
+    kinds = {k: v for k, v in prof.items() if not k.startswith("_") and v["launches"] > 0}
+    total = sum(v["ms"] for v in kinds.values()) or 1.0
+    dom = max(kinds, key=lambda k: kinds[k]["ms"])
+    table = {}
+    for k, v in kinds.items():
+        ms_per = v["ms"] / v["launches"] if v["launches"] else 0.0
+        entry = {"launches": v["launches"], "ms_total": round(v["ms"], 3), "share": round(v["ms"] / total, 4),
+                 "ms_per_launch": round(ms_per, 5)}
+        if v["ms"] > 0:
+            if k in TENSOR_KINDS:
+                entry["tflops"] = round(v["flops"] / (v["ms"] * 1e-3) / 1e12, 1)
+            entry["gbs"] = round(v["bytes"] / (v["ms"] * 1e-3) / 1e9, 1)
+        table[k] = entry
+    # the Q8_0 GEMM family as one roofline figure too (the metric's second half)
+    g_ms = sum(kinds[k]["ms"] for k in GEMM_KINDS if k in kinds)
+    g_fl = sum(kinds[k]["flops"] for k in GEMM_KINDS if k in kinds)
+    peak_t = peaks["bf16_tflops_sustained"]
+    v = kinds[dom]
+    if dom in TENSOR_KINDS:
+        ach = v["flops"] / v["launches"] / (v["ms"] / v["launches"] * 1e-3) / 1e12
+        rl = {"kernel": dom, "bound": "tensor", "achieved": round(ach, 1), "peak": peak_t, "unit": "TFLOP/s",
+              "frac": round(ach / peak_t, 4), "peak_source": f"{peaks['source']} bf16_tflops_sustained"}
+    else:
+        ach = v["bytes"] / v["launches"] / (v["ms"] / v["launches"] * 1e-3) / 1e9
+        rl = {"kernel": dom, "bound": "hbm", "achieved": round(ach, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+              "frac": round(ach / peaks["hbm_gbs"], 4), "peak_source": f"{peaks['source']} hbm_gbs"}
+    tr = ncu_traffic(dom)
+    rl["traffic"] = tr
+    rl["algorithmic_per_launch"] = round((v["flops"] if dom in TENSOR_KINDS else v["bytes"]) / v["launches"], 1)
+    if g_ms > 0:
+        ach_g = g_fl / (g_ms * 1e-3) / 1e12
+        rl["q8_0_gemm_family"] = {"achieved": round(ach_g, 1), "unit": "TFLOP/s", "frac": round(ach_g / peak_t, 4)}
+    return rl, table
+
+
+# ------------------------------------------------------------------------------ CPU baseline
+def cpu_baseline(model_path: str, seq_len: int, budget_s: float) -> dict:
+    import oracle
+    threads = os.cpu_count() or 1
+    oracle.set_threads(threads)
+    m = oracle.OracleModel(model_path)
+    ids, lens = synth.make_batch(64, seq_len, m.vocab, seed=synth.MASTER_SEED + 777)
+    t0 = time.perf_counter()
+    done = 0
+    while done < len(lens):
+        m.embed(ids[done:done + 1], lens[done:done + 1], oracle.M1_CANDLE)
+        done += 1
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": round(done / dt, 4), "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{done} x {seq_len}-token sequence(s), same synthetic GGUF, oracle M1 (candle-faithful "
+                      f"Q8_0) C++ restatement of glypr's CPU path, {dt:.1f} s wall"}
+
+
+# ------------------------------------------------------------------------------ arms
+def run_reference(args) -> None:
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    import oracle
+    os.makedirs(args.model_dir, exist_ok=True)
+    path = synth.ensure_gguf(os.path.join(args.model_dir, "baseline_q8_0.gguf"), synth.BASELINE)
+    threads = os.cpu_count() or 1
+    oracle.set_threads(threads)
+    m = oracle.OracleModel(path)
+    n = args.warmup + args.steps
+    ids, lens = synth.make_batch(n, args.seq_len, m.vocab, seed=synth.MASTER_SEED + 4242)
+    times = []
+    for i in range(n):
+        t0 = time.perf_counter()
+        m.embed(ids[i:i + 1], lens[i:i + 1], oracle.M1_CANDLE)
+        if i >= args.warmup:
+            times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = len(times) / total
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * total / len(times), 2),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (int8 Q8_0 dot products)",
+        "data": "synthetic",
+        "config": {"workload": f"config5 sample: 1 x {args.seq_len}-token sequence per step", "model": MODEL_DESC,
+                   "seq_len": args.seq_len, "parallelism": "host threads"},
+        "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"1 x {args.seq_len}-token sequence per step, C++ restatement of glypr's CPU "
+                                   "path (oracle/, candle-faithful Q8_0 mode), Rust reference not buildable here"},
+        "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args) -> None:
+    import torch
+    rank, world, local_rank = dist_env()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+    from glypr_b200.api import GlyprEmbedder
+
+    os.makedirs(args.model_dir, exist_ok=True)
+    path = os.path.join(args.model_dir, "baseline_q8_0.gguf")
+    if rank == 0:
+        synth.ensure_gguf(path, synth.BASELINE)
+    barrier(world, device)
+    emb = GlyprEmbedder.load_gguf(path, [local_rank], max_batch_tokens=args.max_batch_tokens)
+    seqs, L = args.seqs_per_gpu, args.seq_len
+    # this rank's shard of the box batch: distinct sequences per rank, all exactly L tokens
+    ids, lens = synth.make_batch(seqs, L, emb.info.vocab, seed=synth.MASTER_SEED + 1000 + rank)
+    h_cu = np.arange(0, (seqs + 1) * L, L, dtype=np.int32)
+    d_ids = torch.from_numpy(ids.reshape(-1).copy()).to(device)
+    d_cu = torch.from_numpy(h_cu).to(device)
+    d_out = torch.empty((seqs, emb.embedding_dim), dtype=torch.float32, device=device)
+    stream = torch.cuda.current_stream(device)
+
+    def step():
+        emb.embed_packed_device(d_ids.data_ptr(), d_cu.data_ptr(), h_cu, seqs, emb.embedding_dim,
+                                d_out.data_ptr(), stream.cuda_stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(device)
+    if emb.device_status() != 0:
+        raise SystemExit("device status word set during warm-up")
+
+    emb.profile_enable(True)
+    clocks = ClockSampler(local_rank)
+    barrier(world, device)
+    torch.cuda.synchronize(device)
+    clocks.start()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    barrier(world, device)
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1)
+    prof = emb.profile_read()
+    emb.profile_enable(False)
+    launches = prof["_total_launches"]
+    assert emb.device_status() == 0, "device status word set in the timed region"
+    ms_max = max_over_ranks(ms, world, device)
+    value = world * seqs * args.steps / (ms_max * 1e-3)
+
+    # e2e through the public host API (host ids -> host embeddings)
+    emb.embed_tokens(ids, lens)  # warm the host staging buffers
+    barrier(world, device)
+    t0 = time.perf_counter()
+    for _ in range(args.e2e_steps):
+        out = emb.embed_tokens(ids, lens)
+    t_e2e = time.perf_counter() - t0
+    t_e2e = max_over_ranks(t_e2e, world, device)
+    e2e_value = world * seqs * args.e2e_steps / t_e2e
+    # sanity of the e2e result against the device-resident result of the same inputs
+    same = bool(np.array_equal(out, d_out.cpu().numpy()))
+
+    peaks = measured_peaks()
+    rl, table = roofline(prof, peaks)
+    result = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded random-init GGUF weights, uniform token ids)",
+        "config": {"workload": f"config5: {L}-token Q8_0 sequences, {seqs} per GPU per step "
+                               f"({8 * seqs} = the box batch at 8 GPUs)",
+                   "model": MODEL_DESC, "seqs_per_gpu": seqs, "global_batch": world * seqs, "seq_len": L,
+                   "parallelism": f"dp{world} (contiguous sequence shards, replicated weights, no collective)",
+                   "l2": "inputs larger than L2 (per launch chunk the activations are ~3 GB)",
+                   "compute": "bf16 tcgen05 GEMMs on dequantised Q8_0 weights, f16 attention, f32 norms/residual"},
+        "tokens_per_s": round(value * L, 1),
+        "roofline": rl,
+        "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": int(seqs * L * 4 + (seqs + 1) * 4),
+                "d2h_bytes_per_step": int(seqs * emb.embedding_dim * 4), "steps": args.e2e_steps,
+                "matches_device_path": same},
+        "gpu_launches": launches,
+        "clocks": clk,
+        "kernels": table,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(path, L, args.cpu_seconds)
+    emb.close()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        barrier(world, device)
+        dist.destroy_process_group()
+
+
+def main(argv=None) -> None:
+    args = parse_args(argv)
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

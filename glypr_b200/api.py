@@ -1,0 +1,292 @@
+"""Host-side mirror of glypr-core's embedder API over ``libglypr_cuda.so`` (ctypes).
+
+Names and behaviour follow the reference facade (crates/glypr-core/src/lib.rs):
+``GlyprEmbedder.load_gguf`` / ``load_gguf_q8`` (lib.rs:176-229), ``embed_batch`` on token-id
+inputs (lib.rs:731-952), ``truncate_mrl`` / ``l2_normalize`` / ``cosine_similarity``
+(util.rs:6-41).  Errors surface as :class:`GlyprError` carrying the library's message (the
+reference's ``anyhow`` errors, e.g. "exceeds model max_position_embeddings",
+model.rs:500-506).
+
+There is no CPU fallback: if the CUDA library cannot be loaded or no GPU is visible, the
+calls fail loudly.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from typing import List, Optional, Sequence, Union
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_NAME = "libglypr_cuda.so"
+
+GLP_OK = 0
+GLP_ERR_INVALID_ARG = 1
+GLP_ERR_IO = 2
+GLP_ERR_FORMAT = 3
+GLP_ERR_UNSUPPORTED = 4
+GLP_ERR_CUDA = 5
+GLP_ERR_OOM = 6
+GLP_ERR_DEVICE = 7
+GLP_ERR_CONTEXT_LIMIT = 8
+GLP_MAX_DEVICES = 16
+
+GLP_PROFILE_KINDS = 12
+
+# Every symbol include/glypr_cuda.h declares (checked by the CPU test suite).
+EXPORTED_SYMBOLS = (
+    "glp_open", "glp_close", "glp_last_error", "glp_model_info", "glp_embed_tokens",
+    "glp_embed_packed_device", "glp_device_status", "glp_profile_enable", "glp_profile_read",
+    "glp_q8_0_dequant", "glp_q8_0_gemm", "glp_bf16_gemm", "glp_flash_attention",
+)
+
+
+class GlyprError(RuntimeError):
+    def __init__(self, code: int, message: str):
+        super().__init__(f"[glp error {code}] {message}")
+        self.code = code
+        self.message = message
+
+
+class GlpOptions(ctypes.Structure):
+    _fields_ = [("max_batch_tokens", ctypes.c_int64), ("max_batch_seqs", ctypes.c_int),
+                ("reserved", ctypes.c_int * 6)]
+
+
+class GlpModelInfo(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int) for n in (
+        "n_layers", "hidden", "ffn", "n_heads", "n_kv_heads", "head_dim", "vocab", "embedding_dim",
+        "max_position", "sliding_window", "weight_type", "n_devices")]
+
+
+class GlpTiming(ctypes.Structure):
+    _fields_ = [("n_devices", ctypes.c_int), ("device_ms", ctypes.c_float * GLP_MAX_DEVICES)]
+
+
+class GlpProfile(ctypes.Structure):
+    _fields_ = [("n_kinds", ctypes.c_int), ("names", ctypes.c_char_p * GLP_PROFILE_KINDS),
+                ("launches", ctypes.c_int64 * GLP_PROFILE_KINDS),
+                ("total_ms", ctypes.c_double * GLP_PROFILE_KINDS),
+                ("flops", ctypes.c_double * GLP_PROFILE_KINDS),
+                ("bytes", ctypes.c_double * GLP_PROFILE_KINDS),
+                ("total_launches", ctypes.c_int64)]
+
+    def as_dict(self) -> dict:
+        return {self.names[k].decode(): {"launches": int(self.launches[k]), "ms": float(self.total_ms[k]),
+                                         "flops": float(self.flops[k]), "bytes": float(self.bytes[k])}
+                for k in range(self.n_kinds)}
+
+
+_lib = None
+_lib_lock = threading.Lock()
+
+
+def library_path() -> str:
+    return os.path.join(_HERE, _LIB_NAME)
+
+
+def load_library(path: Optional[str] = None) -> ctypes.CDLL:
+    """Load (once) the CUDA library; raises if it has not been built."""
+    global _lib
+    with _lib_lock:
+        if _lib is not None:
+            return _lib
+        p = path or library_path()
+        if not os.path.exists(p):
+            raise GlyprError(GLP_ERR_IO, f"{p} not built (run glypr_b200/build.py)")
+        L = ctypes.CDLL(p)
+        P, I, I64 = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64
+        L.glp_last_error.restype = ctypes.c_char_p
+        L.glp_open.argtypes = [ctypes.c_char_p, P, I, P, ctypes.POINTER(P)]
+        L.glp_close.argtypes = [P]
+        L.glp_close.restype = None
+        L.glp_model_info.argtypes = [P, P]
+        L.glp_embed_tokens.argtypes = [P, P, P, I, I, I, P, P]
+        L.glp_embed_packed_device.argtypes = [P, I, P, P, P, I, I, P, P]
+        L.glp_device_status.argtypes = [P, I, P]
+        L.glp_profile_enable.argtypes = [P, I, I]
+        L.glp_profile_read.argtypes = [P, I, P]
+        L.glp_q8_0_dequant.argtypes = [P, I64, P, P]
+        L.glp_q8_0_gemm.argtypes = [P, I, I, P, I, P, I, P]
+        L.glp_bf16_gemm.argtypes = [P, I, I, P, I, P, I, P]
+        L.glp_flash_attention.argtypes = [P, P, I, I, I, I, I, I, P, P]
+        _lib = L
+        return L
+
+
+def check(rc: int) -> None:
+    if rc != GLP_OK:
+        msg = load_library().glp_last_error().decode(errors="replace")
+        raise GlyprError(rc, msg)
+
+
+def _ptr(a: np.ndarray):
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+# ---------------------------------------------------------------------------------------
+# util.rs equivalents (host side, f32)
+# ---------------------------------------------------------------------------------------
+
+def l2_normalize(v: np.ndarray) -> np.ndarray:
+    """util.rs:22-29 (a zero vector is returned unchanged)."""
+    v = np.asarray(v, dtype=np.float32)
+    n = np.float32(np.sqrt(np.sum(v * v, dtype=np.float32)))
+    return v.copy() if n == 0 else (v / n).astype(np.float32)
+
+
+def truncate_mrl(embedding: np.ndarray, target_dim: int) -> np.ndarray:
+    """util.rs:6-19: first ``target_dim`` values, L2-renormalised."""
+    embedding = np.asarray(embedding, dtype=np.float32)
+    if target_dim == 0:
+        raise ValueError("Target Matryoshka dimension cannot be 0")
+    if target_dim > embedding.shape[-1]:
+        raise ValueError(f"Target dimension {target_dim} exceeds embedding dimension {embedding.shape[-1]}")
+    return l2_normalize(embedding[..., :target_dim])
+
+
+def cosine_similarity(a: np.ndarray, b: np.ndarray) -> float:
+    """util.rs:32-41."""
+    a = np.asarray(a, dtype=np.float32)
+    b = np.asarray(b, dtype=np.float32)
+    na, nb = float(np.sqrt((a * a).sum())), float(np.sqrt((b * b).sum()))
+    if na == 0 or nb == 0:
+        return 0.0
+    return float(np.clip((a * b).sum() / (na * nb), -1.0, 1.0))
+
+
+# ---------------------------------------------------------------------------------------
+# the embedder
+# ---------------------------------------------------------------------------------------
+
+class GlyprEmbedder:
+    """A loaded model replicated on one or more GPUs (one weight copy per device)."""
+
+    def __init__(self, handle: int, path: str, devices: Sequence[int]):
+        self._h = ctypes.c_void_p(handle)
+        self.path = path
+        self.devices = list(devices)
+        info = GlpModelInfo()
+        check(load_library().glp_model_info(self._h, ctypes.byref(info)))
+        self.info = info
+
+    # reference: GlyprEmbedder::load_gguf(path, device) / load_gguf_q8 (lib.rs:176-229)
+    @classmethod
+    def load_gguf(cls, path: str, devices: Optional[Sequence[int]] = None,
+                  max_batch_tokens: int = 0, max_batch_seqs: int = 0) -> "GlyprEmbedder":
+        L = load_library()
+        devs = list(devices) if devices is not None else []
+        arr = (ctypes.c_int * max(1, len(devs)))(*devs) if devs else None
+        opt = GlpOptions(max_batch_tokens=max_batch_tokens, max_batch_seqs=max_batch_seqs)
+        out = ctypes.c_void_p()
+        check(L.glp_open(path.encode(), arr, len(devs), ctypes.byref(opt), ctypes.byref(out)))
+        return cls(out.value, path, devs or [-1])
+
+    load_gguf_q8 = load_gguf
+
+    def close(self) -> None:
+        if self._h and self._h.value:
+            load_library().glp_close(self._h)
+            self._h = ctypes.c_void_p(None)
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def embedding_dim(self) -> int:
+        return self.info.embedding_dim
+
+    @property
+    def max_position(self) -> int:
+        return self.info.max_position
+
+    def embed_tokens(self, ids: np.ndarray, lengths: np.ndarray, out_dim: Optional[int] = None,
+                     timing: Optional[GlpTiming] = None) -> np.ndarray:
+        """Right-padded ids [n_seq, max_len] + lengths -> L2-normalised [n_seq, out_dim] f32."""
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        if ids.ndim != 2:
+            raise ValueError("ids must be [n_seq, max_len]")
+        lengths = np.ascontiguousarray(lengths, dtype=np.int32)
+        n, s = ids.shape
+        od = int(out_dim or self.embedding_dim)
+        out = np.empty((n, od), dtype=np.float32)
+        check(load_library().glp_embed_tokens(self._h, _ptr(ids), _ptr(lengths), n, s, od, _ptr(out),
+                                              ctypes.byref(timing) if timing is not None else None))
+        return out
+
+    # reference: embed_batch(inputs, truncate_dim) -> Vec<Vec<f32>> (lib.rs:731-952), here on
+    # token-id lists (the tokenizer is outside this backend's boundary)
+    def embed_batch(self, token_ids: Sequence[Sequence[int]], truncate_dim: Optional[int] = None
+                    ) -> List[np.ndarray]:
+        if len(token_ids) == 0:
+            return []
+        lens = np.array([len(t) for t in token_ids], dtype=np.int32)
+        s = int(lens.max()) if len(lens) else 0
+        ids = np.zeros((len(token_ids), max(s, 1)), dtype=np.int32)
+        for i, t in enumerate(token_ids):
+            ids[i, :len(t)] = np.asarray(t, dtype=np.int32)
+        emb = self.embed_tokens(ids[:, :max(s, 1)] if s else ids, lens, truncate_dim)
+        return [e for e in emb]
+
+    def embed_text_ids(self, ids: Sequence[int], truncate_dim: Optional[int] = None) -> np.ndarray:
+        return self.embed_batch([ids], truncate_dim)[0]
+
+    # device-resident path (stream-ordered; pointers are raw device addresses)
+    def embed_packed_device(self, d_ids: int, d_cu: int, h_cu: np.ndarray, n_seq: int, out_dim: int,
+                            d_out: int, stream: int = 0, dev_index: int = 0) -> None:
+        h_cu = np.ascontiguousarray(h_cu, dtype=np.int32)
+        check(load_library().glp_embed_packed_device(self._h, dev_index, ctypes.c_void_p(d_ids),
+                                                     ctypes.c_void_p(d_cu), _ptr(h_cu), n_seq, out_dim,
+                                                     ctypes.c_void_p(d_out), ctypes.c_void_p(stream)))
+
+    def profile_enable(self, enable: bool = True, dev_index: int = 0) -> None:
+        check(load_library().glp_profile_enable(self._h, dev_index, int(enable)))
+
+    def profile_read(self, dev_index: int = 0) -> dict:
+        prof = GlpProfile()
+        check(load_library().glp_profile_read(self._h, dev_index, ctypes.byref(prof)))
+        out = prof.as_dict()
+        out["_total_launches"] = int(prof.total_launches)
+        return out
+
+    def device_status(self, dev_index: int = 0) -> int:
+        st = ctypes.c_int(0)
+        check(load_library().glp_device_status(self._h, dev_index, ctypes.byref(st)))
+        return st.value
+
+
+# ---------------------------------------------------------------------------------------
+# kernel-level entry points (raw device pointers)
+# ---------------------------------------------------------------------------------------
+
+def q8_0_dequant(d_blocks: int, n_blocks: int, d_out: int, stream: int = 0) -> None:
+    check(load_library().glp_q8_0_dequant(ctypes.c_void_p(d_blocks), n_blocks, ctypes.c_void_p(d_out),
+                                          ctypes.c_void_p(stream)))
+
+
+def q8_0_gemm(d_w: int, n: int, k: int, d_x: int, m: int, d_y: int, y_is_f32: bool, stream: int = 0) -> None:
+    check(load_library().glp_q8_0_gemm(ctypes.c_void_p(d_w), n, k, ctypes.c_void_p(d_x), m, ctypes.c_void_p(d_y),
+                                       int(y_is_f32), ctypes.c_void_p(stream)))
+
+
+def bf16_gemm(d_w: int, n: int, k: int, d_x: int, m: int, d_y: int, y_is_f32: bool, stream: int = 0) -> None:
+    check(load_library().glp_bf16_gemm(ctypes.c_void_p(d_w), n, k, ctypes.c_void_p(d_x), m, ctypes.c_void_p(d_y),
+                                       int(y_is_f32), ctypes.c_void_p(stream)))
+
+
+def flash_attention(d_qkv: int, d_cu: int, n_seq: int, max_len: int, n_q_heads: int, n_kv_heads: int,
+                    head_dim: int, window: int, d_out: int, stream: int = 0) -> None:
+    check(load_library().glp_flash_attention(ctypes.c_void_p(d_qkv), ctypes.c_void_p(d_cu), n_seq, max_len,
+                                             n_q_heads, n_kv_heads, head_dim, window, ctypes.c_void_p(d_out),
+                                             ctypes.c_void_p(stream)))

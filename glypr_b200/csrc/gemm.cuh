@@ -1,0 +1,339 @@
+// Persistent tcgen05 GEMM for sm_100a:  C[M, N] = A[M, K] * B[N, K]^T
+//
+//   A  activations, bf16, row-major (K contiguous)        -> TMA, 128B swizzle
+//   B  weights (dequantised Q8_0 or bf16), row-major [N,K] -> TMA, 128B swizzle
+//   accumulator f32 in tensor memory (TMEM), two buffers of BN columns
+//
+// Roles (192 threads): warp 0 = TMA producer, warp 1 = MMA issuer (+ TMEM owner),
+// warps 2..5 = epilogue (warp w reads TMEM lanes 32*(w%4)..+31, one output row per thread).
+// Tiles are 128 x BN, K is consumed 64 elements (one 128-byte swizzle row) per stage.
+// Tile order is M-major over N so consecutive CTAs share the same A rows (read from HBM
+// once, then from L2) while the weights stay L2-resident.
+//
+// Epilogues (fused so the activations make one trip through HBM):
+//   kEpiBf16    store bf16
+//   kEpiF32     store f32
+//   kEpiQkv     per-head RMSNorm (q/k with gain, v without), NeoX RoPE on q/k, store f16.
+//               One 256-column tile == one head (attention/mod.rs:166-188, rope.rs:90-106).
+//   kEpiGeglu   B rows interleaved [gate 128 | up 128] per tile; out = gelu_tanh(g)*u, bf16
+//               (cpu_simd/geglu.rs:6-18, with its +-10 clamp).
+#pragma once
+#include "common.cuh"
+
+namespace glp {
+
+enum EpiKind : int { kEpiBf16 = 0, kEpiF32 = 1, kEpiQkv = 2, kEpiGeglu = 3 };
+
+struct GemmParams {
+  int M, N, K;
+  int m_tiles, n_tiles, k_blocks;
+  void* C;      // output base
+  int ldc;      // output row stride in elements
+  // kEpiQkv
+  const float* q_gain;    // [head_dim]
+  const float* k_gain;    // [head_dim]
+  const float* rope_cos;  // [max_pos, head_dim/2] (cos of freqs; the table's halves are equal)
+  const float* rope_sin;  // [max_pos, head_dim/2]
+  const int* pos;         // [M] position of each row inside its sequence
+  int n_q_heads, n_kv_heads;
+  float eps;
+  int* status;  // device status word (error codes above)
+};
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int BM = 128;
+  static constexpr int BK = 64;
+  static constexpr int STAGES = BN == 256 ? 4 : 6;
+  static constexpr uint32_t A_BYTES = BM * BK * 2;
+  static constexpr uint32_t B_BYTES = BN * BK * 2;
+  static constexpr uint32_t TMEM_COLS = 2 * BN;  // double-buffered accumulator
+  static constexpr size_t SMEM = 1024 + STAGES * (A_BYTES + B_BYTES) + 256;
+};
+
+__device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float* v) {
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint4 u;
+    u.x = pack_bf16(v[8 * q + 0], v[8 * q + 1]);
+    u.y = pack_bf16(v[8 * q + 2], v[8 * q + 3]);
+    u.z = pack_bf16(v[8 * q + 4], v[8 * q + 5]);
+    u.w = pack_bf16(v[8 * q + 6], v[8 * q + 7]);
+    d[q] = u;
+  }
+}
+
+__device__ __forceinline__ void store_f16x32(__half* dst, const float* v) {
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint4 u;
+    u.x = pack_f16(v[8 * q + 0], v[8 * q + 1]);
+    u.y = pack_f16(v[8 * q + 2], v[8 * q + 3]);
+    u.z = pack_f16(v[8 * q + 4], v[8 * q + 5]);
+    u.w = pack_f16(v[8 * q + 6], v[8 * q + 7]);
+    d[q] = u;
+  }
+}
+
+// gelu_tanh(g) * u with the reference's clamp (cpu_simd/geglu.rs:6-18).  Uses the identity
+// 0.5 * (1 + tanh(z)) = 1 / (1 + exp(-2 z)).
+__device__ __forceinline__ float geglu_f(float g, float u) {
+  if (g <= -10.0f) return 0.0f;
+  if (g >= 10.0f) return g * u;
+  const float z = 0.7978846f * (g + 0.044715f * g * g * g);
+  return __fdividef(g, 1.0f + __expf(-2.0f * z)) * u;
+}
+
+template <int BN, int EPI>
+__device__ __forceinline__ void gemm_epilogue_tile(const GemmParams& p, uint32_t tacc, int m_blk, int n_blk,
+                                                   int row_in_tile) {
+  const int row = m_blk * 128 + row_in_tile;
+  const bool live = row < p.M;
+  uint32_t r[32];
+  if constexpr (EPI == kEpiBf16 || EPI == kEpiF32) {
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      tmem_ld32(tacc + c * 32, r);
+      tmem_ld_wait();
+      float v[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = u2f(r[j]);
+      if (live) {
+        const size_t off = static_cast<size_t>(row) * p.ldc + static_cast<size_t>(n_blk) * BN + c * 32;
+        if constexpr (EPI == kEpiBf16) {
+          store_bf16x32(reinterpret_cast<__nv_bfloat16*>(p.C) + off, v);
+        } else {
+          float4* d = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.C) + off);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) d[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        }
+      }
+    }
+  } else if constexpr (EPI == kEpiGeglu) {
+    static_assert(BN == 256, "GeGLU tiles pair 128 gate with 128 up columns");
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      uint32_t u[32];
+      tmem_ld32(tacc + c * 32, r);
+      tmem_ld32(tacc + 128 + c * 32, u);
+      tmem_ld_wait();
+      float v[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = geglu_f(u2f(r[j]), u2f(u[j]));
+      if (live) {
+        const size_t off = static_cast<size_t>(row) * p.ldc + static_cast<size_t>(n_blk) * 128 + c * 32;
+        store_bf16x32(reinterpret_cast<__nv_bfloat16*>(p.C) + off, v);
+      }
+    }
+  } else {  // kEpiQkv
+    static_assert(BN == 256, "QKV tiles are one 256-wide head");
+    // pass 1: sum of squares over the head (cpu_simd/rmsnorm.rs:13-21)
+    float ss = 0.f;
+#pragma unroll 1
+    for (int c = 0; c < 8; ++c) {
+      tmem_ld32(tacc + c * 32, r);
+      tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) ss = fmaf(u2f(r[j]), u2f(r[j]), ss);
+    }
+    const float inv = 1.0f / sqrtf(ss / 256.0f + p.eps);
+    const bool is_q = n_blk < p.n_q_heads;
+    const bool is_k = !is_q && n_blk < p.n_q_heads + p.n_kv_heads;
+    const float* gain = is_q ? p.q_gain : (is_k ? p.k_gain : nullptr);
+    const bool rope = is_q || is_k;
+    const int pos = live ? p.pos[row] : 0;
+    const float* cs = p.rope_cos + static_cast<size_t>(pos) * 128;
+    const float* sn = p.rope_sin + static_cast<size_t>(pos) * 128;
+    __half* out = reinterpret_cast<__half*>(p.C) + static_cast<size_t>(row) * p.ldc + static_cast<size_t>(n_blk) * 256;
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      uint32_t h[32];
+      tmem_ld32(tacc + c * 32, r);        // x[i],       i = 32c + j
+      tmem_ld32(tacc + 128 + c * 32, h);  // x[i + 128]
+      tmem_ld_wait();
+      float lo[32], hi[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int i = c * 32 + j;
+        float x1 = u2f(r[j]) * inv;
+        float x2 = u2f(h[j]) * inv;
+        if (gain) {
+          x1 *= __ldg(gain + i);
+          x2 *= __ldg(gain + i + 128);
+        }
+        if (rope) {
+          const float cv = __ldg(cs + i), sv = __ldg(sn + i);
+          lo[j] = x1 * cv + (-x2) * sv;  // x*cos + rotate_half(x)*sin, rotate_half = cat(-x2, x1)
+          hi[j] = x2 * cv + x1 * sv;
+        } else {
+          lo[j] = x1;
+          hi[j] = x2;
+        }
+      }
+      if (live) {
+        store_f16x32(out + c * 32, lo);
+        store_f16x32(out + 128 + c * 32, hi);
+      }
+    }
+  }
+}
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(192, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const GemmParams p) {
+  using Cfg = GemmCfg<BN>;
+  constexpr int STAGES = Cfg::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * Cfg::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * Cfg::B_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_tiles = p.m_tiles * p.n_tiles;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ TMA producer
+      int s = 0;
+      uint32_t ph = 0;
+      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+        const int m_blk = tile / p.n_tiles, n_blk = tile % p.n_tiles;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) {
+            record_error(p.status, kErrTimeoutProducer);
+            *abort_flag = 1;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], Cfg::A_BYTES + Cfg::B_BYTES);
+          tma_load_2d(sA + s * Cfg::A_BYTES, &tmA, &full[s], kb * Cfg::BK, m_blk * Cfg::BM);
+          tma_load_2d(sB + s * Cfg::B_BYTES, &tmB, &full[s], kb * Cfg::BK, n_blk * BN);
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ MMA issuer
+      constexpr uint32_t idesc = idesc_f16(128, BN, 1);
+      int s = 0;
+      uint32_t ph = 0;
+      int ab = 0;
+      uint32_t aph = 0;
+      bool issued = false;
+      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+        if (!mbar_wait(&tempty[ab], aph ^ 1, abort_flag)) {
+          record_error(p.status, kErrTimeoutMma);
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(ab * BN);
+        bool ok = true;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&full[s], ph, abort_flag)) {
+            record_error(p.status, kErrTimeoutMma);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t adesc = desc_kmajor_sw128(smem_u32(sA + s * Cfg::A_BYTES));
+          const uint64_t bdesc = desc_kmajor_sw128(smem_u32(sB + s * Cfg::B_BYTES));
+#pragma unroll
+          for (int k = 0; k < Cfg::BK / 16; ++k) {
+            // +32 bytes along K inside the 128-byte swizzle row (descriptor address is >>4)
+            umma_f16_ss(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          issued = true;
+          umma_commit(&empty[s]);
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[ab]);
+        ab ^= 1;
+        if (ab == 0) aph ^= 1;
+      }
+      if (issued) {
+        // make sure every MMA has retired before TMEM is released
+        umma_commit(drain);
+        if (!mbar_wait(drain, 0, abort_flag) && !*abort_flag) record_error(p.status, kErrTimeoutDrain);
+      }
+    }
+  } else {
+    // -------------------------------------------------------------- epilogue warps
+    const int quad = warp & 3;
+    const int row_in_tile = quad * 32 + lane;
+    int ab = 0;
+    uint32_t aph = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      const int m_blk = tile / p.n_tiles, n_blk = tile % p.n_tiles;
+      bool ok = mbar_wait(&tfull[ab], aph, abort_flag);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) {
+        if (lane == 0) {
+          record_error(p.status, kErrTimeoutEpilogue);
+          *abort_flag = 1;
+        }
+        break;
+      }
+      tc_fence_after();
+      const uint32_t tacc = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(ab * BN);
+      gemm_epilogue_tile<BN, EPI>(p, tacc, m_blk, n_blk, row_in_tile);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[ab]);
+      ab ^= 1;
+      if (ab == 0) aph ^= 1;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+}  // namespace glp

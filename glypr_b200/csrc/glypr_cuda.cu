@@ -1,0 +1,1236 @@
+// libglypr_cuda.so: host side of the B200 embedding path and its C ABI (include/glypr_cuda.h).
+//
+// Host responsibilities (the C++ counterpart of glypr-core's Rust facade):
+//   * GGUF -> TextConfig with the reference's keys and defaults (config.rs:76-250)
+//   * weight upload: one replica per device; Q8_0 linears dequantised once on the device
+//     into fused bf16 layouts (QKV concatenated as in try_concat, linear.rs:82-148; gate/up
+//     interleaved per 128 rows for the GeGLU epilogue); token table kept as raw Q8_0 blocks
+//   * per-device forward over packed sequences in launch chunks (model.rs:498-578 +
+//     pool_and_normalize 654-705), one worker thread and stream per device, contiguous
+//     sequence shards (no collective: embeddings are copied back per device).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <array>
+#include <atomic>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "attention.cuh"
+#include "gemm.cuh"
+#include "gguf.h"
+#include "glypr_cuda.h"
+#include "rowops.cuh"
+
+using glp::GemmParams;
+
+namespace {
+
+thread_local std::string t_err;
+
+int fail(int code, const std::string& msg) {
+  t_err = msg;
+  return code;
+}
+
+#define GLP_CUDA(expr)                                                                         \
+  do {                                                                                         \
+    cudaError_t e_ = (expr);                                                                   \
+    if (e_ != cudaSuccess)                                                                     \
+      return fail(e_ == cudaErrorMemoryAllocation ? GLP_ERR_OOM : GLP_ERR_CUDA,                \
+                  std::string(#expr) + ": " + cudaGetErrorString(e_));                         \
+  } while (0)
+
+#define GLP_TRY(expr)         \
+  do {                        \
+    int rc_ = (expr);         \
+    if (rc_ != GLP_OK) return rc_; \
+  } while (0)
+
+// ------------------------------------------------------------------------------ TMA maps
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 2-D bf16 row-major [rows, cols] tensor, box = 64 columns (one 128-byte swizzle row) x
+// box_rows rows, 128B swizzle, out-of-bounds rows read as zero.
+int make_map_bf16(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int64_t ld_elems, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(GLP_ERR_CUDA, "cuTensorMapEncodeTiled unavailable (driver too old?)");
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (ld_elems * 2) % 16 || cols % 64)
+    return fail(GLP_ERR_INVALID_ARG, "TMA operand must be 16-byte aligned with K % 64 == 0");
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld_elems * 2)};
+  const cuuint32_t box[2] = {64u, static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t estr[2] = {1u, 1u};
+  const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(GLP_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string(r));
+  return GLP_OK;
+}
+
+// ------------------------------------------------------------------------------ per-device kernel setup
+std::mutex g_attr_mu;
+std::array<bool, 64> g_attr_done{};
+
+int ensure_kernel_attrs() {
+  int dev = 0;
+  GLP_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lk(g_attr_mu);
+  if (dev < 0 || dev >= 64) return fail(GLP_ERR_INVALID_ARG, "device index out of range");
+  if (g_attr_done[dev]) return GLP_OK;
+  GLP_CUDA(cudaFuncSetAttribute(glp::gemm_tc_kernel<256, glp::kEpiBf16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(glp::GemmCfg<256>::SMEM)));
+  GLP_CUDA(cudaFuncSetAttribute(glp::gemm_tc_kernel<256, glp::kEpiF32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(glp::GemmCfg<256>::SMEM)));
+  GLP_CUDA(cudaFuncSetAttribute(glp::gemm_tc_kernel<256, glp::kEpiQkv>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(glp::GemmCfg<256>::SMEM)));
+  GLP_CUDA(cudaFuncSetAttribute(glp::gemm_tc_kernel<256, glp::kEpiGeglu>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(glp::GemmCfg<256>::SMEM)));
+  GLP_CUDA(cudaFuncSetAttribute(glp::gemm_tc_kernel<128, glp::kEpiBf16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(glp::GemmCfg<128>::SMEM)));
+  GLP_CUDA(cudaFuncSetAttribute(glp::gemm_tc_kernel<128, glp::kEpiF32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(glp::GemmCfg<128>::SMEM)));
+  GLP_CUDA(cudaFuncSetAttribute(glp::flash_attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(glp::kAttnSmem)));
+  g_attr_done[dev] = true;
+  return GLP_OK;
+}
+
+int sm_count() {
+  int dev = 0, n = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+int bn_for(int n) { return n % 256 == 0 ? 256 : 128; }
+
+// Launch C = A * B^T with the given epilogue.  `ma` covers A [M, K] (box rows 128), `mb`
+// covers B [N, K] with box rows == bn.
+int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, int bn, int epi, GemmParams p, cudaStream_t st) {
+  p.m_tiles = (p.M + 127) / 128;
+  p.n_tiles = p.N / bn;
+  p.k_blocks = p.K / 64;
+  if (p.M <= 0) return GLP_OK;
+  if (p.K % 64 || p.N % bn || p.K <= 0) return fail(GLP_ERR_INVALID_ARG, "GEMM needs K % 64 == 0 and N % tile == 0");
+  const int tiles = p.m_tiles * p.n_tiles;
+  const int grid = std::min(tiles, sm_count());
+  if (bn == 256) {
+    const size_t smem = glp::GemmCfg<256>::SMEM;
+    switch (epi) {
+      case glp::kEpiBf16: glp::gemm_tc_kernel<256, glp::kEpiBf16><<<grid, 192, smem, st>>>(ma, mb, p); break;
+      case glp::kEpiF32: glp::gemm_tc_kernel<256, glp::kEpiF32><<<grid, 192, smem, st>>>(ma, mb, p); break;
+      case glp::kEpiQkv: glp::gemm_tc_kernel<256, glp::kEpiQkv><<<grid, 192, smem, st>>>(ma, mb, p); break;
+      case glp::kEpiGeglu: glp::gemm_tc_kernel<256, glp::kEpiGeglu><<<grid, 192, smem, st>>>(ma, mb, p); break;
+      default: return fail(GLP_ERR_INVALID_ARG, "bad epilogue");
+    }
+  } else {
+    const size_t smem = glp::GemmCfg<128>::SMEM;
+    switch (epi) {
+      case glp::kEpiBf16: glp::gemm_tc_kernel<128, glp::kEpiBf16><<<grid, 192, smem, st>>>(ma, mb, p); break;
+      case glp::kEpiF32: glp::gemm_tc_kernel<128, glp::kEpiF32><<<grid, 192, smem, st>>>(ma, mb, p); break;
+      default: return fail(GLP_ERR_INVALID_ARG, "fused epilogues need 256-wide tiles");
+    }
+  }
+  GLP_CUDA(cudaGetLastError());
+  return GLP_OK;
+}
+
+// ------------------------------------------------------------------------------ model config
+struct Config {
+  int n_layers = 0, hidden = 0, ffn = 0, n_heads = 0, n_kv = 0, head_dim = 0, vocab = 0;
+  int emb_out = 768, max_pos = 262144, window = 512;
+  double eps = 1e-6, theta_swa = 1e4, theta_full = 1e6;
+  std::vector<bool> sliding;
+  uint32_t linear_type = glp::kGgmlQ8_0;
+};
+
+int parse_config(const glp::GgufFile& g, Config* c) {
+  const std::string a = "gemma-embedding2.";
+  uint32_t u = 0;
+  if (!g.get_u32(a + "block_count", &u)) return fail(GLP_ERR_FORMAT, "Missing gemma-embedding2.block_count");
+  c->n_layers = static_cast<int>(u);
+  if (!g.get_u32(a + "embedding_length", &u)) return fail(GLP_ERR_FORMAT, "Missing gemma-embedding2.embedding_length");
+  c->hidden = static_cast<int>(u);
+  if (!g.get_u32(a + "feed_forward_length", &u))
+    return fail(GLP_ERR_FORMAT, "Missing gemma-embedding2.feed_forward_length");
+  c->ffn = static_cast<int>(u);
+  if (!g.get_u32(a + "attention.head_count", &u))
+    return fail(GLP_ERR_FORMAT, "Missing gemma-embedding2.attention.head_count");
+  c->n_heads = static_cast<int>(u);
+  uint32_t hd_swa = 256, hd_full = 512;
+  g.get_u32(a + "attention.key_length_swa", &hd_swa);
+  g.get_u32(a + "attention.key_length", &hd_full);
+  if (g.get_u32(a + "embedding_length_out", &u)) c->emb_out = static_cast<int>(u);
+  if (g.get_u32(a + "context_length", &u)) c->max_pos = static_cast<int>(u);
+  g.get_f64(a + "attention.layer_norm_rms_epsilon", &c->eps);
+  g.get_f64(a + "rope.freq_base_swa", &c->theta_swa);
+  g.get_f64(a + "rope.freq_base", &c->theta_full);
+  const glp::GgufValue* toks = g.find("tokenizer.ggml.tokens");
+  c->vocab = toks && toks->type == 9 ? static_cast<int>(toks->arr_len) : 262144;
+  const glp::GgufValue* pat = g.find(a + "attention.sliding_window_pattern");
+  c->sliding.resize(c->n_layers);
+  for (int i = 0; i < c->n_layers; ++i) {
+    if (pat && pat->type == 9) {
+      if (pat->arr_type != 7 || i >= static_cast<int>(pat->arr.size()))
+        return fail(GLP_ERR_FORMAT, "Invalid boolean in sliding_window_pattern");
+      c->sliding[i] = pat->arr[i] != 0;
+    } else {
+      c->sliding[i] = (i + 1) % 6 != 0;
+    }
+  }
+  const glp::GgufValue* kv = g.find(a + "attention.head_count_kv");
+  c->n_kv = kv && kv->type == 9 && !kv->arr.empty() ? static_cast<int>(kv->arr[0]) : 2;
+  for (int i = 0; i < c->n_layers; ++i) {
+    int kvi = c->n_kv;
+    if (!c->sliding[i]) kvi = kv && kv->type == 9 && i < static_cast<int>(kv->arr.size()) ? static_cast<int>(kv->arr[i]) : 1;
+    const int hd = c->sliding[i] ? static_cast<int>(hd_swa) : static_cast<int>(hd_full);
+    if (kvi != c->n_kv || hd != static_cast<int>(hd_swa))
+      return fail(GLP_ERR_UNSUPPORTED,
+                  "per-layer head_dim / kv-head overrides are not supported (all layers must share head_dim and kv heads)");
+  }
+  c->head_dim = static_cast<int>(hd_swa);
+  if (c->hidden != glp::kHidden) return fail(GLP_ERR_UNSUPPORTED, "hidden size must be 768");
+  if (c->head_dim != 256) return fail(GLP_ERR_UNSUPPORTED, "head_dim must be 256");
+  if (c->n_kv <= 0 || c->n_heads % c->n_kv) return fail(GLP_ERR_FORMAT, "head_count must be a multiple of head_count_kv");
+  if (c->ffn % 128) return fail(GLP_ERR_UNSUPPORTED, "feed_forward_length must be a multiple of 128");
+  if ((c->n_heads * c->head_dim) % 64) return fail(GLP_ERR_UNSUPPORTED, "attention width must be a multiple of 64");
+  return GLP_OK;
+}
+
+// Check every tensor the forward needs (names as in model.rs:251-473) before any device
+// work, so a malformed file fails without allocating.
+int validate_tensors(const glp::GgufFile& g, const Config& c) {
+  const int64_t H = c.hidden, F = c.ffn, D = c.head_dim;
+  auto need = [&](const std::string& name, std::vector<int64_t> ne, bool matrix) -> int {
+    const glp::GgufTensor* t = g.tensor(name);
+    if (!t) return fail(GLP_ERR_FORMAT, "missing tensor " + name);
+    if (t->ne != ne) return fail(GLP_ERR_FORMAT, "bad shape for " + name);
+    if (matrix && t->type != glp::kGgmlQ8_0 && t->type != glp::kGgmlBF16)
+      return fail(GLP_ERR_UNSUPPORTED, name + " must be Q8_0 or BF16");
+    if (!matrix && t->type != glp::kGgmlF32 && t->type != glp::kGgmlF16 && t->type != glp::kGgmlBF16)
+      return fail(GLP_ERR_UNSUPPORTED, name + " must be F32, F16 or BF16");
+    return GLP_OK;
+  };
+  const glp::GgufTensor* te = g.tensor("token_embd.weight");
+  if (!te) return fail(GLP_ERR_FORMAT, "missing tensor token_embd.weight");
+  if (te->ne.size() != 2 || te->ne[0] != H || te->ne[1] < c.vocab)
+    return fail(GLP_ERR_FORMAT, "bad shape for token_embd.weight");
+  if (te->type != glp::kGgmlQ8_0 && te->type != glp::kGgmlBF16)
+    return fail(GLP_ERR_UNSUPPORTED, "token_embd.weight must be Q8_0 or BF16");
+  if (g.tensor("per_layer_model_proj.weight"))
+    return fail(GLP_ERR_UNSUPPORTED, "per-layer embeddings (PLE) are not supported by this backend");
+  for (int l = 0; l < c.n_layers; ++l) {
+    const std::string p = "blk." + std::to_string(l) + ".";
+    if (g.tensor(p + "proj.weight") || g.tensor(p + "inp_gate.weight"))
+      return fail(GLP_ERR_UNSUPPORTED, "per-layer embeddings (PLE) are not supported by this backend");
+    GLP_TRY(need(p + "attn_norm.weight", {H}, false));
+    GLP_TRY(need(p + "attn_q_norm.weight", {D}, false));
+    GLP_TRY(need(p + "attn_k_norm.weight", {D}, false));
+    GLP_TRY(need(p + "post_attention_norm.weight", {H}, false));
+    GLP_TRY(need(p + "ffn_norm.weight", {H}, false));
+    GLP_TRY(need(p + "post_ffw_norm.weight", {H}, false));
+    GLP_TRY(need(p + "attn_q.weight", {H, c.n_heads * D}, true));
+    GLP_TRY(need(p + "attn_k.weight", {H, c.n_kv * D}, true));
+    GLP_TRY(need(p + "attn_v.weight", {H, c.n_kv * D}, true));
+    GLP_TRY(need(p + "attn_output.weight", {c.n_heads * D, H}, true));
+    GLP_TRY(need(p + "ffn_gate.weight", {H, F}, true));
+    GLP_TRY(need(p + "ffn_up.weight", {H, F}, true));
+    GLP_TRY(need(p + "ffn_down.weight", {F, H}, true));
+  }
+  GLP_TRY(need("output_norm.weight", {H}, false));
+  int64_t prev = H;
+  int stages = 0;
+  for (int j = 0;; ++j) {
+    const glp::GgufTensor* t = g.tensor("dense." + std::to_string(j) + ".weight");
+    if (!t) break;
+    if (t->ne.size() != 2 || t->ne[0] != prev) return fail(GLP_ERR_FORMAT, "bad shape for dense head stage " + std::to_string(j));
+    GLP_TRY(need("dense." + std::to_string(j) + ".weight", {prev, t->ne[1]}, true));
+    if (t->ne[1] % 128) return fail(GLP_ERR_UNSUPPORTED, "dense head dims must be multiples of 128");
+    prev = t->ne[1];
+    ++stages;
+  }
+  if (stages == 0) {
+    const glp::GgufTensor* t = g.tensor("output.weight");
+    if (!t) return fail(GLP_ERR_FORMAT, "missing tensor output.weight");
+    if (t->ne.size() != 2) return fail(GLP_ERR_FORMAT, "bad shape for output.weight");
+    GLP_TRY(need("output.weight", {H, t->ne[1]}, true));
+    if (t->ne[1] % 128) return fail(GLP_ERR_UNSUPPORTED, "output.weight rows must be a multiple of 128");
+    prev = t->ne[1];
+  }
+  if (prev != c.emb_out) return fail(GLP_ERR_FORMAT, "head output dim != embedding_length_out");
+  return GLP_OK;
+}
+
+// ------------------------------------------------------------------------------ device state
+struct LayerW {
+  __nv_bfloat16 *qkv = nullptr, *o = nullptr, *gu = nullptr, *down = nullptr;
+  float *attn_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr, *post_attn = nullptr, *ffn_norm = nullptr,
+        *post_ffw = nullptr;
+  float layer_scalar = 1.0f;
+  bool sliding = true;
+  CUtensorMap m_qkv, m_o, m_gu, m_down;
+};
+
+struct HeadW {
+  __nv_bfloat16* w = nullptr;
+  int n = 0, k = 0, bn = 256;
+  CUtensorMap map;
+};
+
+struct Device {
+  int dev = 0;
+  cudaStream_t stream = nullptr;
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  std::vector<void*> allocs;
+  void* table = nullptr;
+  uint32_t table_type = glp::kGgmlQ8_0;
+  std::vector<LayerW> layers;
+  float* out_norm = nullptr;
+  std::vector<HeadW> head;
+  float *cos_swa = nullptr, *sin_swa = nullptr, *cos_full = nullptr, *sin_full = nullptr;
+  int64_t cap_tokens = 0;
+  int cap_seqs = 0;
+  float* h = nullptr;
+  __nv_bfloat16* x = nullptr;
+  __half* qkv = nullptr;
+  __nv_bfloat16* attn = nullptr;
+  __nv_bfloat16* y = nullptr;
+  __nv_bfloat16* a = nullptr;
+  int* pos = nullptr;
+  __nv_bfloat16* pooled = nullptr;
+  __nv_bfloat16* mid = nullptr;
+  float* emb = nullptr;
+  int* status = nullptr;
+  // host-API staging (device + pinned host), grown on demand
+  int* d_ids = nullptr;
+  int* d_cu = nullptr;
+  float* d_out = nullptr;
+  int* h_ids = nullptr;
+  int* h_cu = nullptr;
+  float* h_out = nullptr;
+  int64_t stage_tokens = 0, stage_seqs = 0, stage_out = 0;
+  // profiling: event pairs around launches (when enabled) + launch counters (always)
+  bool prof_on = false;
+  std::vector<std::array<cudaEvent_t, 2>> prof_ev;
+  std::vector<int> prof_kind;
+  size_t prof_used = 0;
+  std::array<int64_t, GLP_PROFILE_KINDS> prof_launch{};
+  std::array<double, GLP_PROFILE_KINDS> prof_flops{}, prof_bytes{};
+
+  template <class T>
+  int alloc(T** p, size_t count) {
+    void* v = nullptr;
+    GLP_CUDA(cudaMalloc(&v, std::max<size_t>(count, 1) * sizeof(T)));
+    allocs.push_back(v);
+    *p = static_cast<T*>(v);
+    return GLP_OK;
+  }
+  void release() {
+    cudaSetDevice(dev);
+    if (stream) cudaStreamSynchronize(stream);
+    for (void* p : allocs) cudaFree(p);
+    allocs.clear();
+    if (d_ids) cudaFree(d_ids);
+    if (d_cu) cudaFree(d_cu);
+    if (d_out) cudaFree(d_out);
+    if (h_ids) cudaFreeHost(h_ids);
+    if (h_cu) cudaFreeHost(h_cu);
+    if (h_out) cudaFreeHost(h_out);
+    d_ids = d_cu = nullptr;
+    d_out = nullptr;
+    h_ids = h_cu = nullptr;
+    h_out = nullptr;
+    for (auto& e : prof_ev) {
+      cudaEventDestroy(e[0]);
+      cudaEventDestroy(e[1]);
+    }
+    prof_ev.clear();
+    if (ev0) cudaEventDestroy(ev0);
+    if (ev1) cudaEventDestroy(ev1);
+    if (stream) cudaStreamDestroy(stream);
+    stream = nullptr;
+    ev0 = ev1 = nullptr;
+  }
+};
+
+enum ProfKind : int {
+  kProfEmbed = 0,
+  kProfGemmQkv,
+  kProfAttention,
+  kProfGemmO,
+  kProfPostNorm,
+  kProfGemmGateUp,
+  kProfGemmDown,
+  kProfPool,
+  kProfHeadGemm,
+  kProfL2,
+  kProfMisc,
+  kProfKernelApi,
+};
+const char* const kProfNames[GLP_PROFILE_KINDS] = {
+    "embed_gather_norm", "gemm_qkv_norm_rope", "flash_attention", "gemm_o", "post_norm_residual",
+    "gemm_gate_up_geglu", "gemm_down", "mean_pool", "gemm_head", "l2_mrl", "positions", "kernel_api"};
+
+// Bracket one kernel launch: counts it and, when profiling is on, records an event pair on
+// the launching stream.  Returns the launch's status.
+template <class F>
+int prof_launch(Device& d, cudaStream_t st, int kind, double flops, double bytes, F&& launch) {
+  if (d.prof_on) {
+    if (d.prof_used == d.prof_ev.size()) {
+      std::array<cudaEvent_t, 2> e{};
+      GLP_CUDA(cudaEventCreate(&e[0]));
+      GLP_CUDA(cudaEventCreate(&e[1]));
+      d.prof_ev.push_back(e);
+      d.prof_kind.push_back(0);
+    }
+    GLP_CUDA(cudaEventRecord(d.prof_ev[d.prof_used][0], st));
+  }
+  const int rc = launch();
+  if (rc != GLP_OK) return rc;
+  d.prof_launch[kind] += 1;
+  d.prof_flops[kind] += flops;
+  d.prof_bytes[kind] += bytes;
+  if (d.prof_on) {
+    GLP_CUDA(cudaEventRecord(d.prof_ev[d.prof_used][1], st));
+    d.prof_kind[d.prof_used] = kind;
+    ++d.prof_used;
+  }
+  return GLP_OK;
+}
+
+// Visible (query, key) pairs of one sequence under the attention mask (|i-j| <= w when
+// w > 0): the attention kernel's algorithmic work is 4 * head_dim * heads * pairs FLOPs.
+double visible_pairs(int64_t len, int w) {
+  if (w <= 0 || len <= w + 1) return static_cast<double>(len) * len;
+  // full square minus the two corners where |i - j| > w
+  const double excl = static_cast<double>(len - w - 1) * (len - w) ;
+  return static_cast<double>(len) * len - excl;
+}
+
+}  // namespace
+
+struct glp_ctx {
+  Config cfg;
+  std::vector<std::unique_ptr<Device>> devs;
+};
+
+namespace {
+
+// ------------------------------------------------------------------------------ upload
+int upload_gain(Device& d, const glp::GgufFile& g, const std::string& name, int n, float** out) {
+  const glp::GgufTensor* t = g.tensor(name);
+  if (!t) return fail(GLP_ERR_FORMAT, "missing tensor " + name);
+  if (t->ne.size() != 1 || t->ne[0] != n) return fail(GLP_ERR_FORMAT, "bad shape for " + name);
+  std::vector<float> v(n);
+  for (int i = 0; i < n; ++i) {
+    if (t->type == glp::kGgmlF32) {
+      std::memcpy(&v[i], t->data + 4 * i, 4);
+    } else if (t->type == glp::kGgmlF16) {
+      uint16_t hbits;
+      std::memcpy(&hbits, t->data + 2 * i, 2);
+      __half_raw hr;
+      hr.x = hbits;
+      v[i] = __half2float(__half(hr));
+    } else if (t->type == glp::kGgmlBF16) {
+      uint16_t b;
+      std::memcpy(&b, t->data + 2 * i, 2);
+      const uint32_t bits = static_cast<uint32_t>(b) << 16;
+      std::memcpy(&v[i], &bits, 4);
+    } else {
+      return fail(GLP_ERR_UNSUPPORTED, "unsupported dtype for " + name);
+    }
+  }
+  GLP_TRY(d.alloc(out, n));
+  GLP_CUDA(cudaMemcpy(*out, v.data(), n * sizeof(float), cudaMemcpyHostToDevice));
+  return GLP_OK;
+}
+
+// Upload linear `name` [n, k] into rows of dst (bf16 [*, k]) with the row mapping of
+// q8_0_dequant_bf16_rows_kernel.  Uses a device staging buffer for the raw bytes.
+int upload_linear(Device& d, const glp::GgufFile& g, const std::string& name, int n, int k, __nv_bfloat16* dst,
+                  int row_base, int group, int group_stride, void* staging, size_t staging_bytes) {
+  const glp::GgufTensor* t = g.tensor(name);
+  if (!t) return fail(GLP_ERR_FORMAT, "missing tensor " + name);
+  if (t->ne.size() != 2 || t->ne[0] != k || t->ne[1] != n) return fail(GLP_ERR_FORMAT, "bad shape for " + name);
+  if (t->nbytes > staging_bytes) return fail(GLP_ERR_FORMAT, "tensor too large: " + name);
+  GLP_CUDA(cudaMemcpy(staging, t->data, t->nbytes, cudaMemcpyHostToDevice));
+  if (t->type == glp::kGgmlQ8_0) {
+    const int64_t nb = static_cast<int64_t>(n) * (k / 32);
+    glp::q8_0_dequant_bf16_rows_kernel<<<static_cast<unsigned>((nb + 255) / 256), 256>>>(
+        static_cast<const uint8_t*>(staging), n, k, dst, row_base, group, group_stride);
+  } else if (t->type == glp::kGgmlBF16) {
+    const int64_t nc = static_cast<int64_t>(n) * (k / 8);
+    glp::bf16_rows_copy_kernel<<<static_cast<unsigned>((nc + 255) / 256), 256>>>(
+        static_cast<const __nv_bfloat16*>(staging), n, k, dst, row_base, group, group_stride);
+  } else {
+    return fail(GLP_ERR_UNSUPPORTED, "linear " + name + " must be Q8_0 or BF16");
+  }
+  GLP_CUDA(cudaGetLastError());
+  GLP_CUDA(cudaDeviceSynchronize());
+  return GLP_OK;
+}
+
+// RoPE tables exactly as rope.rs:14-87: inv_freq_i = f32(1 / theta^(2i/d)) in f64, then
+// freqs = f32(pos) * inv_freq (f32), cos/sin in f32.  Only the first half is stored (the
+// reference table is cat(freqs, freqs)).
+int upload_rope(Device& d, double theta, int d_head, int max_pos, float** cs, float** sn) {
+  const int half = d_head / 2;
+  std::vector<float> inv(half), c(static_cast<size_t>(max_pos) * half), s(static_cast<size_t>(max_pos) * half);
+  for (int i = 0; i < half; ++i) inv[i] = static_cast<float>(1.0 / std::pow(theta, (2.0 * i) / d_head));
+  for (int p = 0; p < max_pos; ++p)
+    for (int i = 0; i < half; ++i) {
+      const float f = static_cast<float>(p) * inv[i];
+      c[static_cast<size_t>(p) * half + i] = std::cos(f);
+      s[static_cast<size_t>(p) * half + i] = std::sin(f);
+    }
+  GLP_TRY(d.alloc(cs, c.size()));
+  GLP_TRY(d.alloc(sn, s.size()));
+  GLP_CUDA(cudaMemcpy(*cs, c.data(), c.size() * 4, cudaMemcpyHostToDevice));
+  GLP_CUDA(cudaMemcpy(*sn, s.data(), s.size() * 4, cudaMemcpyHostToDevice));
+  return GLP_OK;
+}
+
+int setup_device(Device& d, const Config& c, const glp::GgufFile& g, int64_t cap_tokens, int cap_seqs) {
+  GLP_CUDA(cudaSetDevice(d.dev));
+  GLP_TRY(ensure_kernel_attrs());
+  GLP_CUDA(cudaStreamCreateWithFlags(&d.stream, cudaStreamNonBlocking));
+  GLP_CUDA(cudaEventCreate(&d.ev0));
+  GLP_CUDA(cudaEventCreate(&d.ev1));
+  const int H = c.hidden, F = c.ffn, D = c.head_dim;
+  const int QKV = (c.n_heads + 2 * c.n_kv) * D, AW = c.n_heads * D;
+
+  // token table: kept as raw Q8_0 (or bf16) rows, gathered per token
+  const glp::GgufTensor* te = g.tensor("token_embd.weight");
+  if (!te) return fail(GLP_ERR_FORMAT, "missing tensor token_embd.weight");
+  if (te->ne.size() != 2 || te->ne[0] != H) return fail(GLP_ERR_FORMAT, "bad shape for token_embd.weight");
+  if (te->ne[1] < c.vocab) return fail(GLP_ERR_FORMAT, "token_embd.weight has fewer rows than the vocabulary");
+  if (te->type != glp::kGgmlQ8_0 && te->type != glp::kGgmlBF16)
+    return fail(GLP_ERR_UNSUPPORTED, "token_embd.weight must be Q8_0 or BF16");
+  d.table_type = te->type;
+  uint8_t* table = nullptr;
+  GLP_TRY(d.alloc(&table, te->nbytes));
+  GLP_CUDA(cudaMemcpy(table, te->data, te->nbytes, cudaMemcpyHostToDevice));
+  d.table = table;
+
+  // staging for raw linear bytes: the largest linear
+  size_t staging_bytes = 0;
+  for (const auto* nm : {"attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up", "ffn_down"}) {
+    const glp::GgufTensor* t = g.tensor(std::string("blk.0.") + nm + ".weight");
+    if (t) staging_bytes = std::max(staging_bytes, t->nbytes);
+  }
+  for (int j = 0;; ++j) {
+    const glp::GgufTensor* t = g.tensor("dense." + std::to_string(j) + ".weight");
+    if (!t) break;
+    staging_bytes = std::max(staging_bytes, t->nbytes);
+  }
+  if (const glp::GgufTensor* t = g.tensor("output.weight")) staging_bytes = std::max(staging_bytes, t->nbytes);
+  staging_bytes = std::max(staging_bytes, static_cast<size_t>(4) * F * std::max(H, F));
+  void* staging = nullptr;
+  GLP_CUDA(cudaMalloc(&staging, staging_bytes));
+  struct Free {
+    void* p;
+    ~Free() { cudaFree(p); }
+  } free_staging{staging};
+
+  d.layers.resize(c.n_layers);
+  for (int l = 0; l < c.n_layers; ++l) {
+    LayerW& L = d.layers[l];
+    const std::string p = "blk." + std::to_string(l) + ".";
+    L.sliding = c.sliding[l];
+    if (g.tensor(p + "proj.weight") || g.tensor(p + "inp_gate.weight"))
+      return fail(GLP_ERR_UNSUPPORTED, "per-layer embeddings (PLE) are not supported by this backend");
+    GLP_TRY(upload_gain(d, g, p + "attn_norm.weight", H, &L.attn_norm));
+    GLP_TRY(upload_gain(d, g, p + "attn_q_norm.weight", D, &L.q_norm));
+    GLP_TRY(upload_gain(d, g, p + "attn_k_norm.weight", D, &L.k_norm));
+    GLP_TRY(upload_gain(d, g, p + "post_attention_norm.weight", H, &L.post_attn));
+    GLP_TRY(upload_gain(d, g, p + "ffn_norm.weight", H, &L.ffn_norm));
+    GLP_TRY(upload_gain(d, g, p + "post_ffw_norm.weight", H, &L.post_ffw));
+    if (const glp::GgufTensor* s = g.tensor(p + "layer_output_scale.weight")) {
+      if (s->type != glp::kGgmlF32 || s->numel() != 1) return fail(GLP_ERR_FORMAT, "bad layer_output_scale");
+      std::memcpy(&L.layer_scalar, s->data, 4);
+    }
+    GLP_TRY(d.alloc(&L.qkv, static_cast<size_t>(QKV) * H));
+    GLP_TRY(d.alloc(&L.o, static_cast<size_t>(H) * AW));
+    GLP_TRY(d.alloc(&L.gu, static_cast<size_t>(2 * F) * H));
+    GLP_TRY(d.alloc(&L.down, static_cast<size_t>(H) * F));
+    GLP_TRY(upload_linear(d, g, p + "attn_q.weight", c.n_heads * D, H, L.qkv, 0, 0, 0, staging, staging_bytes));
+    GLP_TRY(upload_linear(d, g, p + "attn_k.weight", c.n_kv * D, H, L.qkv, c.n_heads * D, 0, 0, staging, staging_bytes));
+    GLP_TRY(upload_linear(d, g, p + "attn_v.weight", c.n_kv * D, H, L.qkv, (c.n_heads + c.n_kv) * D, 0, 0, staging,
+                          staging_bytes));
+    GLP_TRY(upload_linear(d, g, p + "attn_output.weight", H, AW, L.o, 0, 0, 0, staging, staging_bytes));
+    GLP_TRY(upload_linear(d, g, p + "ffn_gate.weight", F, H, L.gu, 0, 128, 256, staging, staging_bytes));
+    GLP_TRY(upload_linear(d, g, p + "ffn_up.weight", F, H, L.gu, 128, 128, 256, staging, staging_bytes));
+    GLP_TRY(upload_linear(d, g, p + "ffn_down.weight", H, F, L.down, 0, 0, 0, staging, staging_bytes));
+    GLP_TRY(make_map_bf16(&L.m_qkv, L.qkv, QKV, H, H, 256));
+    GLP_TRY(make_map_bf16(&L.m_o, L.o, H, AW, AW, bn_for(H)));
+    GLP_TRY(make_map_bf16(&L.m_gu, L.gu, 2 * F, H, H, 256));
+    GLP_TRY(make_map_bf16(&L.m_down, L.down, H, F, F, bn_for(H)));
+  }
+  GLP_TRY(upload_gain(d, g, "output_norm.weight", H, &d.out_norm));
+  // dense head: dense.0 .. dense.N (BASELINE two-stage 768->3072->768), else output.weight
+  int prev = H;
+  for (int j = 0;; ++j) {
+    const std::string nm = "dense." + std::to_string(j) + ".weight";
+    const glp::GgufTensor* t = g.tensor(nm);
+    if (!t) break;
+    HeadW hw;
+    hw.n = static_cast<int>(t->ne.size() == 2 ? t->ne[1] : 0);
+    hw.k = prev;
+    if (hw.n % 128 || hw.k % 64) return fail(GLP_ERR_UNSUPPORTED, "dense head dims must be multiples of 128");
+    hw.bn = bn_for(hw.n);
+    GLP_TRY(d.alloc(&hw.w, static_cast<size_t>(hw.n) * hw.k));
+    GLP_TRY(upload_linear(d, g, nm, hw.n, hw.k, hw.w, 0, 0, 0, staging, staging_bytes));
+    GLP_TRY(make_map_bf16(&hw.map, hw.w, hw.n, hw.k, hw.k, hw.bn));
+    d.head.push_back(hw);
+    prev = hw.n;
+  }
+  if (d.head.empty()) {
+    const glp::GgufTensor* t = g.tensor("output.weight");
+    if (!t) return fail(GLP_ERR_FORMAT, "missing tensor output.weight");
+    HeadW hw;
+    hw.n = static_cast<int>(t->ne.size() == 2 ? t->ne[1] : 0);
+    hw.k = H;
+    if (hw.n % 128) return fail(GLP_ERR_UNSUPPORTED, "output.weight rows must be a multiple of 128");
+    hw.bn = bn_for(hw.n);
+    GLP_TRY(d.alloc(&hw.w, static_cast<size_t>(hw.n) * hw.k));
+    GLP_TRY(upload_linear(d, g, "output.weight", hw.n, hw.k, hw.w, 0, 0, 0, staging, staging_bytes));
+    GLP_TRY(make_map_bf16(&hw.map, hw.w, hw.n, hw.k, hw.k, hw.bn));
+    d.head.push_back(hw);
+  }
+  if (d.head.back().n != c.emb_out) return fail(GLP_ERR_FORMAT, "head output dim != embedding_length_out");
+  GLP_TRY(upload_rope(d, c.theta_swa, D, c.max_pos, &d.cos_swa, &d.sin_swa));
+  GLP_TRY(upload_rope(d, c.theta_full, D, c.max_pos, &d.cos_full, &d.sin_full));
+
+  // activations for one launch chunk
+  d.cap_tokens = cap_tokens;
+  d.cap_seqs = cap_seqs;
+  int max_head = H;
+  for (auto& hw : d.head) max_head = std::max(max_head, hw.n);
+  GLP_TRY(d.alloc(&d.h, static_cast<size_t>(cap_tokens) * H));
+  GLP_TRY(d.alloc(&d.x, static_cast<size_t>(cap_tokens) * H));
+  GLP_TRY(d.alloc(&d.qkv, static_cast<size_t>(cap_tokens) * QKV));
+  GLP_TRY(d.alloc(&d.attn, static_cast<size_t>(cap_tokens) * AW));
+  GLP_TRY(d.alloc(&d.y, static_cast<size_t>(cap_tokens) * H));
+  GLP_TRY(d.alloc(&d.a, static_cast<size_t>(cap_tokens) * F));
+  GLP_TRY(d.alloc(&d.pos, static_cast<size_t>(cap_tokens)));
+  GLP_TRY(d.alloc(&d.pooled, static_cast<size_t>(cap_seqs) * H));
+  GLP_TRY(d.alloc(&d.mid, static_cast<size_t>(cap_seqs) * max_head));
+  GLP_TRY(d.alloc(&d.emb, static_cast<size_t>(cap_seqs) * max_head));
+  GLP_TRY(d.alloc(&d.status, 1));
+  GLP_CUDA(cudaMemset(d.status, 0, sizeof(int)));
+  GLP_CUDA(cudaDeviceSynchronize());
+  return GLP_OK;
+}
+
+// ------------------------------------------------------------------------------ forward
+// One launch chunk: sequences [s0, s1) of the packed input; tokens are rows 0..T-1 of the
+// activation buffers (global packed index = row + base).  h_cu (host offsets of the chunk's
+// sequences) only feeds the profiler's algorithmic work counts.
+int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_cu_chunk, const int* h_cu_chunk,
+              int base, int n_seq, int T, int max_len, int out_dim, float* d_out, cudaStream_t st) {
+  const int H = c.hidden, F = c.ffn, D = c.head_dim;
+  const int QKV = (c.n_heads + 2 * c.n_kv) * D, AW = c.n_heads * D;
+  const float eps = static_cast<float>(c.eps);
+  const double Td = T;
+  auto gemm_flops = [&](double m, double n, double k) { return 2.0 * m * n * k; };
+  auto gemm_bytes = [&](double m, double n, double k, double out_elem) { return 2.0 * m * k + 2.0 * n * k + out_elem * m * n; };
+  if (T > 0) {
+    GLP_TRY(prof_launch(d, st, kProfMisc, 0.0, 8.0 * Td, [&] {
+      glp::positions_kernel<<<n_seq, 256, 0, st>>>(d_cu_chunk, base, n_seq, d.pos);
+      GLP_CUDA(cudaGetLastError());
+      return GLP_OK;
+    }));
+    const unsigned rows_grid = static_cast<unsigned>((T + 7) / 8);
+    const float scale = static_cast<float>(std::sqrt(static_cast<double>(H)));
+    const double row_in = d.table_type == glp::kGgmlQ8_0 ? H / 32 * 34.0 : 2.0 * H;
+    GLP_TRY(prof_launch(d, st, kProfEmbed, 0.0, Td * (4.0 + row_in + 6.0 * H), [&] {
+      if (d.table_type == glp::kGgmlQ8_0)
+        glp::embed_gather_norm_kernel<<<rows_grid, 256, 0, st>>>(static_cast<const uint8_t*>(d.table), d_ids_chunk,
+                                                                 T, scale, d.layers[0].attn_norm, eps, d.h, d.x);
+      else
+        glp::embed_gather_norm_bf16_kernel<<<rows_grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(d.table),
+                                                                      d_ids_chunk, T, scale, d.layers[0].attn_norm,
+                                                                      eps, d.h, d.x);
+      GLP_CUDA(cudaGetLastError());
+      return GLP_OK;
+    }));
+
+    CUtensorMap m_x, m_attn, m_a;
+    GLP_TRY(make_map_bf16(&m_x, d.x, T, H, H, 128));
+    GLP_TRY(make_map_bf16(&m_attn, d.attn, T, AW, AW, 128));
+    GLP_TRY(make_map_bf16(&m_a, d.a, T, F, F, 128));
+    const dim3 attn_grid(static_cast<unsigned>((max_len + glp::kAttnBQ - 1) / glp::kAttnBQ),
+                         static_cast<unsigned>(c.n_heads), static_cast<unsigned>(n_seq));
+    double pairs_local = 0, pairs_global = 0;
+    for (int b = 0; b < n_seq; ++b) {
+      const int64_t len = h_cu_chunk[b + 1] - h_cu_chunk[b];
+      pairs_local += visible_pairs(len, c.window);
+      pairs_global += visible_pairs(len, 0);
+    }
+    const double attn_bytes = 2.0 * Td * QKV + 2.0 * Td * AW;
+    const double post_bytes = Td * (2.0 * H + 8.0 * H + 2.0 * H);
+    for (int l = 0; l < c.n_layers; ++l) {
+      LayerW& L = d.layers[l];
+      GemmParams p{};
+      p.M = T;
+      p.K = H;
+      p.status = d.status;
+      // QKV projection + per-head RMSNorm + RoPE -> f16 qkv
+      p.N = QKV;
+      p.C = d.qkv;
+      p.ldc = QKV;
+      p.q_gain = L.q_norm;
+      p.k_gain = L.k_norm;
+      p.rope_cos = L.sliding ? d.cos_swa : d.cos_full;
+      p.rope_sin = L.sliding ? d.sin_swa : d.sin_full;
+      p.pos = d.pos;
+      p.n_q_heads = c.n_heads;
+      p.n_kv_heads = c.n_kv;
+      p.eps = eps;
+      GLP_TRY(prof_launch(d, st, kProfGemmQkv, gemm_flops(Td, QKV, H), gemm_bytes(Td, QKV, H, 2.0),
+                          [&] { return launch_gemm(m_x, L.m_qkv, 256, glp::kEpiQkv, p, st); }));
+      // attention
+      const double pairs = L.sliding ? pairs_local : pairs_global;
+      GLP_TRY(prof_launch(d, st, kProfAttention, 4.0 * D * c.n_heads * pairs, attn_bytes, [&] {
+        glp::flash_attn_fwd_kernel<<<attn_grid, glp::kAttnThreads, glp::kAttnSmem, st>>>(
+            d.qkv, QKV, d_cu_chunk, base, c.n_heads, c.n_kv, L.sliding ? c.window : 0, d.attn, AW);
+        GLP_CUDA(cudaGetLastError());
+        return GLP_OK;
+      }));
+      // O projection
+      GemmParams po{};
+      po.M = T;
+      po.N = H;
+      po.K = AW;
+      po.C = d.y;
+      po.ldc = H;
+      po.status = d.status;
+      GLP_TRY(prof_launch(d, st, kProfGemmO, gemm_flops(Td, H, AW), gemm_bytes(Td, H, AW, 2.0),
+                          [&] { return launch_gemm(m_attn, L.m_o, bn_for(H), glp::kEpiBf16, po, st); }));
+      GLP_TRY(prof_launch(d, st, kProfPostNorm, 0.0, post_bytes, [&] {
+        glp::post_norm_residual_kernel<false><<<rows_grid, 256, 0, st>>>(d.y, d.h, L.post_attn, 1.0f, L.ffn_norm,
+                                                                         eps, T, d.x);
+        GLP_CUDA(cudaGetLastError());
+        return GLP_OK;
+      }));
+      // gate|up + GeGLU
+      GemmParams pg{};
+      pg.M = T;
+      pg.N = 2 * F;
+      pg.K = H;
+      pg.C = d.a;
+      pg.ldc = F;
+      pg.status = d.status;
+      GLP_TRY(prof_launch(d, st, kProfGemmGateUp, gemm_flops(Td, 2.0 * F, H),
+                          2.0 * Td * H + 2.0 * 2.0 * F * H + 2.0 * Td * F,
+                          [&] { return launch_gemm(m_x, L.m_gu, 256, glp::kEpiGeglu, pg, st); }));
+      // down projection
+      GemmParams pd{};
+      pd.M = T;
+      pd.N = H;
+      pd.K = F;
+      pd.C = d.y;
+      pd.ldc = H;
+      pd.status = d.status;
+      GLP_TRY(prof_launch(d, st, kProfGemmDown, gemm_flops(Td, H, F), gemm_bytes(Td, H, F, 2.0),
+                          [&] { return launch_gemm(m_a, L.m_down, bn_for(H), glp::kEpiBf16, pd, st); }));
+      const bool last = l + 1 == c.n_layers;
+      GLP_TRY(prof_launch(d, st, kProfPostNorm, 0.0, last ? Td * 10.0 * H : post_bytes, [&] {
+        if (!last)
+          glp::post_norm_residual_kernel<false><<<rows_grid, 256, 0, st>>>(
+              d.y, d.h, L.post_ffw, L.layer_scalar, d.layers[l + 1].attn_norm, eps, T, d.x);
+        else
+          glp::post_norm_residual_kernel<true><<<rows_grid, 256, 0, st>>>(d.y, d.h, L.post_ffw, L.layer_scalar,
+                                                                          d.out_norm, eps, T, d.x);
+        GLP_CUDA(cudaGetLastError());
+        return GLP_OK;
+      }));
+    }
+  }
+  // masked mean of the final-normed rows, then the dense head on the pooled vectors
+  GLP_TRY(prof_launch(d, st, kProfPool, 0.0, 4.0 * Td * H + 2.0 * n_seq * H, [&] {
+    glp::mean_pool_kernel<<<n_seq, 192, 0, st>>>(d.h, d_cu_chunk, base, n_seq, d.pooled, nullptr);
+    GLP_CUDA(cudaGetLastError());
+    return GLP_OK;
+  }));
+  const __nv_bfloat16* cur = d.pooled;
+  int cur_k = H;
+  for (size_t j = 0; j < d.head.size(); ++j) {
+    HeadW& hw = d.head[j];
+    const bool last = j + 1 == d.head.size();
+    CUtensorMap m_in;
+    GLP_TRY(make_map_bf16(&m_in, cur, n_seq, cur_k, cur_k, 128));
+    GemmParams ph{};
+    ph.M = n_seq;
+    ph.N = hw.n;
+    ph.K = hw.k;
+    ph.C = last ? static_cast<void*>(d.emb) : static_cast<void*>(j % 2 ? d.pooled : d.mid);
+    ph.ldc = hw.n;
+    ph.status = d.status;
+    GLP_TRY(prof_launch(d, st, kProfHeadGemm, gemm_flops(n_seq, hw.n, hw.k),
+                        gemm_bytes(n_seq, hw.n, hw.k, last ? 4.0 : 2.0),
+                        [&] { return launch_gemm(m_in, hw.map, hw.bn, last ? glp::kEpiF32 : glp::kEpiBf16, ph, st); }));
+    cur = static_cast<const __nv_bfloat16*>(ph.C);
+    cur_k = hw.n;
+  }
+  GLP_TRY(prof_launch(d, st, kProfL2, 0.0, 4.0 * n_seq * (c.emb_out + out_dim), [&] {
+    glp::l2_mrl_kernel<<<static_cast<unsigned>((n_seq + 7) / 8), 256, 0, st>>>(d.emb, n_seq, c.emb_out, out_dim, d_out);
+    GLP_CUDA(cudaGetLastError());
+    return GLP_OK;
+  }));
+  return GLP_OK;
+}
+
+// Run all sequences of a packed input on one device, cutting launch chunks by token count.
+int run_packed(const Config& c, Device& d, const int* d_ids, const int* d_cu, const int* h_cu, int n_seq, int out_dim,
+               float* d_out, cudaStream_t st) {
+  // d_ids[h_cu[b] .. h_cu[b+1]) are the tokens of sequence b (offsets index d_ids)
+  int s0 = 0;
+  while (s0 < n_seq) {
+    int s1 = s0;
+    int max_len = 0;
+    while (s1 < n_seq && s1 - s0 < d.cap_seqs &&
+           static_cast<int64_t>(h_cu[s1 + 1]) - h_cu[s0] <= d.cap_tokens) {
+      max_len = std::max(max_len, h_cu[s1 + 1] - h_cu[s1]);
+      ++s1;
+    }
+    if (s1 == s0) return fail(GLP_ERR_INVALID_ARG, "sequence longer than the launch chunk (max_batch_tokens)");
+    const int base = h_cu[s0];
+    const int T = h_cu[s1] - base;
+    GLP_TRY(run_chunk(c, d, d_ids + base, d_cu + s0, h_cu + s0, base, s1 - s0, T, max_len, out_dim,
+                      d_out + static_cast<size_t>(s0) * out_dim, st));
+    s0 = s1;
+  }
+  return GLP_OK;
+}
+
+int grow_staging(Device& d, int64_t tokens, int64_t seqs, int64_t outs) {
+  if (tokens > d.stage_tokens) {
+    if (d.d_ids) cudaFree(d.d_ids);
+    if (d.h_ids) cudaFreeHost(d.h_ids);
+    d.d_ids = nullptr;
+    d.h_ids = nullptr;
+    GLP_CUDA(cudaMalloc(&d.d_ids, std::max<int64_t>(tokens, 1) * sizeof(int)));
+    GLP_CUDA(cudaHostAlloc(&d.h_ids, std::max<int64_t>(tokens, 1) * sizeof(int), cudaHostAllocDefault));
+    d.stage_tokens = tokens;
+  }
+  if (seqs > d.stage_seqs) {
+    if (d.d_cu) cudaFree(d.d_cu);
+    if (d.h_cu) cudaFreeHost(d.h_cu);
+    d.d_cu = nullptr;
+    d.h_cu = nullptr;
+    GLP_CUDA(cudaMalloc(&d.d_cu, (seqs + 1) * sizeof(int)));
+    GLP_CUDA(cudaHostAlloc(&d.h_cu, (seqs + 1) * sizeof(int), cudaHostAllocDefault));
+    d.stage_seqs = seqs;
+  }
+  if (outs > d.stage_out) {
+    if (d.d_out) cudaFree(d.d_out);
+    if (d.h_out) cudaFreeHost(d.h_out);
+    d.d_out = nullptr;
+    d.h_out = nullptr;
+    GLP_CUDA(cudaMalloc(&d.d_out, std::max<int64_t>(outs, 1) * sizeof(float)));
+    GLP_CUDA(cudaHostAlloc(&d.h_out, std::max<int64_t>(outs, 1) * sizeof(float), cudaHostAllocDefault));
+    d.stage_out = outs;
+  }
+  return GLP_OK;
+}
+
+int check_status(Device& d) {
+  int st = 0;
+  GLP_CUDA(cudaMemcpy(&st, d.status, sizeof(int), cudaMemcpyDeviceToHost));
+  if (st != 0) {
+    cudaMemset(d.status, 0, sizeof(int));
+    return fail(GLP_ERR_DEVICE, "device pipeline wait timed out (status " + std::to_string(st) + ")");
+  }
+  return GLP_OK;
+}
+
+// Host-API shard on one device: pack, H2D, forward, D2H (all on the device's stream).
+int run_shard(const Config& c, Device& d, const int32_t* ids, const int32_t* lengths, int s0, int s1, int max_len,
+              int out_dim, float* out, float* ms) {
+  GLP_CUDA(cudaSetDevice(d.dev));
+  const int n = s1 - s0;
+  int64_t tokens = 0;
+  for (int i = s0; i < s1; ++i) tokens += lengths[i];
+  GLP_TRY(grow_staging(d, tokens, n, static_cast<int64_t>(n) * out_dim));
+  int64_t off = 0;
+  d.h_cu[0] = 0;
+  for (int i = 0; i < n; ++i) {
+    const int len = lengths[s0 + i];
+    std::memcpy(d.h_ids + off, ids + static_cast<int64_t>(s0 + i) * max_len, len * sizeof(int));
+    off += len;
+    d.h_cu[i + 1] = static_cast<int>(off);
+  }
+  cudaStream_t st = d.stream;
+  GLP_CUDA(cudaEventRecord(d.ev0, st));
+  GLP_CUDA(cudaMemcpyAsync(d.d_ids, d.h_ids, tokens * sizeof(int), cudaMemcpyHostToDevice, st));
+  GLP_CUDA(cudaMemcpyAsync(d.d_cu, d.h_cu, (n + 1) * sizeof(int), cudaMemcpyHostToDevice, st));
+  GLP_TRY(run_packed(c, d, d.d_ids, d.d_cu, d.h_cu, n, out_dim, d.d_out, st));
+  GLP_CUDA(cudaMemcpyAsync(d.h_out, d.d_out, static_cast<size_t>(n) * out_dim * sizeof(float), cudaMemcpyDeviceToHost,
+                           st));
+  GLP_CUDA(cudaEventRecord(d.ev1, st));
+  GLP_CUDA(cudaStreamSynchronize(st));
+  GLP_TRY(check_status(d));
+  if (ms) cudaEventElapsedTime(ms, d.ev0, d.ev1);
+  std::memcpy(out + static_cast<size_t>(s0) * out_dim, d.h_out, static_cast<size_t>(n) * out_dim * sizeof(float));
+  return GLP_OK;
+}
+
+// ------------------------------------------------------------------------------ kernel-level scratch
+struct Scratch {
+  std::mutex mu;
+  std::array<__nv_bfloat16*, 64> w{};
+  std::array<size_t, 64> cap{};
+  std::array<int*, 64> status{};
+};
+Scratch g_scratch;
+
+int device_status_word(int dev, int** out) {
+  std::lock_guard<std::mutex> lk(g_scratch.mu);
+  if (!g_scratch.status[dev]) {
+    GLP_CUDA(cudaMalloc(&g_scratch.status[dev], sizeof(int)));
+    GLP_CUDA(cudaMemset(g_scratch.status[dev], 0, sizeof(int)));
+  }
+  *out = g_scratch.status[dev];
+  return GLP_OK;
+}
+
+int run_bf16_gemm(const __nv_bfloat16* w, int N, int K, const void* x, int M, void* y, int y_is_f32, cudaStream_t st) {
+  if (N <= 0 || K <= 0 || M < 0 || N % 128 || K % 64)
+    return fail(GLP_ERR_INVALID_ARG, "GEMM needs N % 128 == 0, K % 64 == 0, M >= 0");
+  if (!w || !x || !y) return fail(GLP_ERR_INVALID_ARG, "null pointer");
+  GLP_TRY(ensure_kernel_attrs());
+  int dev = 0;
+  GLP_CUDA(cudaGetDevice(&dev));
+  int* status = nullptr;
+  GLP_TRY(device_status_word(dev, &status));
+  if (M == 0) return GLP_OK;
+  const int bn = bn_for(N);
+  CUtensorMap ma, mb;
+  GLP_TRY(make_map_bf16(&ma, x, M, K, K, 128));
+  GLP_TRY(make_map_bf16(&mb, w, N, K, K, bn));
+  GemmParams p{};
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.C = y;
+  p.ldc = N;
+  p.status = status;
+  return launch_gemm(ma, mb, bn, y_is_f32 ? glp::kEpiF32 : glp::kEpiBf16, p, st);
+}
+
+}  // namespace
+
+// ================================================================================= C ABI
+extern "C" {
+
+const char* glp_last_error(void) { return t_err.c_str(); }
+
+int glp_open(const char* gguf_path, const int* device_ids, int n_devices, const glp_options* opt, glp_ctx** out) {
+  if (!out) return fail(GLP_ERR_INVALID_ARG, "out is NULL");
+  *out = nullptr;
+  if (!gguf_path) return fail(GLP_ERR_INVALID_ARG, "gguf_path is NULL");
+  if (n_devices < 0 || n_devices > GLP_MAX_DEVICES) return fail(GLP_ERR_INVALID_ARG, "bad device count");
+  glp::GgufFile g;
+  std::string err;
+  if (!g.open(gguf_path, &err)) return fail(err.rfind("cannot open", 0) == 0 ? GLP_ERR_IO : GLP_ERR_FORMAT, err);
+  auto ctx = std::make_unique<glp_ctx>();
+  GLP_TRY(parse_config(g, &ctx->cfg));
+  GLP_TRY(validate_tensors(g, ctx->cfg));
+  if (const glp::GgufTensor* q = g.tensor("blk.0.attn_q.weight")) ctx->cfg.linear_type = q->type;
+  int64_t cap_tokens = opt && opt->max_batch_tokens > 0 ? opt->max_batch_tokens : 262144;
+  cap_tokens = std::max<int64_t>(cap_tokens, ctx->cfg.max_pos);
+  const int cap_seqs = opt && opt->max_batch_seqs > 0 ? opt->max_batch_seqs : 4096;
+  std::vector<int> ids;
+  if (n_devices == 0 || !device_ids) {
+    int cur = 0;
+    GLP_CUDA(cudaGetDevice(&cur));
+    ids.push_back(cur);
+  } else {
+    ids.assign(device_ids, device_ids + n_devices);
+  }
+  int ndev_avail = 0;
+  GLP_CUDA(cudaGetDeviceCount(&ndev_avail));
+  for (int id : ids)
+    if (id < 0 || id >= ndev_avail) return fail(GLP_ERR_INVALID_ARG, "device id out of range");
+  int prev = 0;
+  cudaGetDevice(&prev);
+  for (int id : ids) {
+    auto d = std::make_unique<Device>();
+    d->dev = id;
+    const int rc = setup_device(*d, ctx->cfg, g, cap_tokens, cap_seqs);
+    if (rc != GLP_OK) {
+      const std::string keep = t_err;
+      d->release();
+      for (auto& e : ctx->devs) e->release();
+      cudaSetDevice(prev);
+      t_err = keep;
+      return rc;
+    }
+    ctx->devs.push_back(std::move(d));
+  }
+  cudaSetDevice(prev);
+  *out = ctx.release();
+  return GLP_OK;
+}
+
+void glp_close(glp_ctx* ctx) {
+  if (!ctx) return;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  for (auto& d : ctx->devs) d->release();
+  cudaSetDevice(prev);
+  delete ctx;
+}
+
+int glp_model_info(const glp_ctx* ctx, glp_model_info_t* info) {
+  if (!ctx || !info) return fail(GLP_ERR_INVALID_ARG, "NULL argument");
+  const Config& c = ctx->cfg;
+  info->n_layers = c.n_layers;
+  info->hidden = c.hidden;
+  info->ffn = c.ffn;
+  info->n_heads = c.n_heads;
+  info->n_kv_heads = c.n_kv;
+  info->head_dim = c.head_dim;
+  info->vocab = c.vocab;
+  info->embedding_dim = c.emb_out;
+  info->max_position = c.max_pos;
+  info->sliding_window = c.window;
+  info->weight_type = static_cast<int>(c.linear_type);
+  info->n_devices = static_cast<int>(ctx->devs.size());
+  return GLP_OK;
+}
+
+int glp_embed_tokens(glp_ctx* ctx, const int32_t* ids, const int32_t* lengths, int n_seq, int max_len, int out_dim,
+                     float* out, glp_timing* timing) {
+  if (!ctx) return fail(GLP_ERR_INVALID_ARG, "ctx is NULL");
+  const Config& c = ctx->cfg;
+  if (n_seq < 0 || max_len < 0) return fail(GLP_ERR_INVALID_ARG, "negative batch shape");
+  if (n_seq > 0 && (!ids || !lengths || !out)) return fail(GLP_ERR_INVALID_ARG, "NULL buffer");
+  if (out_dim <= 0 || out_dim > c.emb_out)
+    return fail(GLP_ERR_INVALID_ARG, "out_dim must be in (0, " + std::to_string(c.emb_out) + "]");
+  if (max_len > c.max_pos)
+    return fail(GLP_ERR_CONTEXT_LIMIT, "Input sequence length (" + std::to_string(max_len) +
+                                           ") exceeds model max_position_embeddings (" + std::to_string(c.max_pos) + ")");
+  int64_t total = 0;
+  for (int i = 0; i < n_seq; ++i) {
+    if (lengths[i] < 0 || lengths[i] > max_len) return fail(GLP_ERR_INVALID_ARG, "length out of [0, max_len]");
+    const int32_t* row = ids + static_cast<int64_t>(i) * max_len;
+    for (int j = 0; j < lengths[i]; ++j)
+      if (row[j] < 0 || row[j] >= c.vocab)
+        return fail(GLP_ERR_INVALID_ARG, "token id " + std::to_string(row[j]) + " outside the vocabulary");
+    total += lengths[i];
+  }
+  const int nd = static_cast<int>(ctx->devs.size());
+  if (timing) {
+    timing->n_devices = nd;
+    for (int i = 0; i < GLP_MAX_DEVICES; ++i) timing->device_ms[i] = 0.f;
+  }
+  if (n_seq == 0) return GLP_OK;
+  // contiguous shards balanced by token count
+  std::vector<int> bounds(nd + 1, n_seq);
+  bounds[0] = 0;
+  {
+    int64_t acc = 0;
+    int k = 1;
+    for (int i = 0; i < n_seq && k < nd; ++i) {
+      acc += lengths[i];
+      while (k < nd && acc * nd >= total * k) bounds[k++] = i + 1;
+    }
+    for (; k < nd; ++k) bounds[k] = n_seq;
+  }
+  std::vector<int> rcs(nd, GLP_OK);
+  std::vector<std::string> errs(nd);
+  std::vector<float> ms(nd, 0.f);
+  auto work = [&](int i) {
+    if (bounds[i] >= bounds[i + 1]) return;
+    rcs[i] = run_shard(c, *ctx->devs[i], ids, lengths, bounds[i], bounds[i + 1], max_len, out_dim, out, &ms[i]);
+    if (rcs[i] != GLP_OK) errs[i] = t_err;
+  };
+  if (nd == 1) {
+    int prev = 0;
+    cudaGetDevice(&prev);
+    work(0);
+    cudaSetDevice(prev);
+  } else {
+    std::vector<std::thread> th;
+    for (int i = 0; i < nd; ++i) th.emplace_back(work, i);
+    for (auto& t : th) t.join();
+  }
+  for (int i = 0; i < nd; ++i) {
+    if (timing && i < GLP_MAX_DEVICES) timing->device_ms[i] = ms[i];
+    if (rcs[i] != GLP_OK) return fail(rcs[i], "device " + std::to_string(ctx->devs[i]->dev) + ": " + errs[i]);
+  }
+  return GLP_OK;
+}
+
+int glp_embed_packed_device(glp_ctx* ctx, int dev_index, const int32_t* d_ids, const int32_t* d_cu_seqlens,
+                            const int32_t* h_cu_seqlens, int n_seq, int out_dim, float* d_out, void* stream) {
+  if (!ctx) return fail(GLP_ERR_INVALID_ARG, "ctx is NULL");
+  if (dev_index < 0 || dev_index >= static_cast<int>(ctx->devs.size())) return fail(GLP_ERR_INVALID_ARG, "bad dev_index");
+  const Config& c = ctx->cfg;
+  if (n_seq < 0 || (n_seq > 0 && (!d_ids || !d_cu_seqlens || !h_cu_seqlens || !d_out)))
+    return fail(GLP_ERR_INVALID_ARG, "NULL buffer");
+  if (out_dim <= 0 || out_dim > c.emb_out) return fail(GLP_ERR_INVALID_ARG, "bad out_dim");
+  for (int i = 0; i < n_seq; ++i) {
+    const int len = h_cu_seqlens[i + 1] - h_cu_seqlens[i];
+    if (len < 0) return fail(GLP_ERR_INVALID_ARG, "cu_seqlens must be non-decreasing");
+    if (len > c.max_pos)
+      return fail(GLP_ERR_CONTEXT_LIMIT, "Input sequence length (" + std::to_string(len) +
+                                             ") exceeds model max_position_embeddings (" + std::to_string(c.max_pos) + ")");
+  }
+  Device& d = *ctx->devs[dev_index];
+  int prev = 0;
+  cudaGetDevice(&prev);
+  GLP_CUDA(cudaSetDevice(d.dev));
+  const int rc = run_packed(c, d, d_ids, d_cu_seqlens, h_cu_seqlens, n_seq, out_dim, d_out,
+                            static_cast<cudaStream_t>(stream));
+  cudaSetDevice(prev);
+  return rc;
+}
+
+int glp_device_status(glp_ctx* ctx, int dev_index, int* status) {
+  if (!ctx || !status || dev_index < 0 || dev_index >= static_cast<int>(ctx->devs.size()))
+    return fail(GLP_ERR_INVALID_ARG, "bad argument");
+  Device& d = *ctx->devs[dev_index];
+  int prev = 0;
+  cudaGetDevice(&prev);
+  GLP_CUDA(cudaSetDevice(d.dev));
+  const cudaError_t e = cudaMemcpy(status, d.status, sizeof(int), cudaMemcpyDeviceToHost);
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) return fail(GLP_ERR_CUDA, cudaGetErrorString(e));
+  return GLP_OK;
+}
+
+int glp_profile_enable(glp_ctx* ctx, int dev_index, int enable) {
+  if (!ctx || dev_index < 0 || dev_index >= static_cast<int>(ctx->devs.size()))
+    return fail(GLP_ERR_INVALID_ARG, "bad argument");
+  Device& d = *ctx->devs[dev_index];
+  d.prof_on = enable != 0;
+  d.prof_used = 0;
+  d.prof_launch.fill(0);
+  d.prof_flops.fill(0.0);
+  d.prof_bytes.fill(0.0);
+  return GLP_OK;
+}
+
+int glp_profile_read(glp_ctx* ctx, int dev_index, glp_profile* out) {
+  if (!ctx || !out || dev_index < 0 || dev_index >= static_cast<int>(ctx->devs.size()))
+    return fail(GLP_ERR_INVALID_ARG, "bad argument");
+  Device& d = *ctx->devs[dev_index];
+  int prev = 0;
+  cudaGetDevice(&prev);
+  GLP_CUDA(cudaSetDevice(d.dev));
+  std::memset(out, 0, sizeof(*out));
+  out->n_kinds = GLP_PROFILE_KINDS;
+  for (int k = 0; k < GLP_PROFILE_KINDS; ++k) {
+    out->names[k] = kProfNames[k];
+    out->launches[k] = d.prof_launch[k];
+    out->flops[k] = d.prof_flops[k];
+    out->bytes[k] = d.prof_bytes[k];
+    out->total_launches += d.prof_launch[k];
+  }
+  for (size_t i = 0; i < d.prof_used; ++i) {
+    float ms = 0.f;
+    GLP_CUDA(cudaEventSynchronize(d.prof_ev[i][1]));
+    GLP_CUDA(cudaEventElapsedTime(&ms, d.prof_ev[i][0], d.prof_ev[i][1]));
+    out->total_ms[d.prof_kind[i]] += ms;
+  }
+  d.prof_used = 0;
+  d.prof_launch.fill(0);
+  d.prof_flops.fill(0.0);
+  d.prof_bytes.fill(0.0);
+  cudaSetDevice(prev);
+  return GLP_OK;
+}
+
+int glp_q8_0_dequant(const void* d_blocks, int64_t n_blocks, float* d_out, void* stream) {
+  if (n_blocks < 0 || (n_blocks > 0 && (!d_blocks || !d_out))) return fail(GLP_ERR_INVALID_ARG, "bad argument");
+  if (reinterpret_cast<uintptr_t>(d_out) & 15) return fail(GLP_ERR_INVALID_ARG, "output must be 16-byte aligned");
+  if (n_blocks == 0) return GLP_OK;
+  glp::q8_0_dequant_f32_kernel<<<static_cast<unsigned>((n_blocks + 255) / 256), 256, 0,
+                                  static_cast<cudaStream_t>(stream)>>>(static_cast<const uint8_t*>(d_blocks), n_blocks,
+                                                                      d_out);
+  GLP_CUDA(cudaGetLastError());
+  return GLP_OK;
+}
+
+int glp_q8_0_gemm(const void* d_q8_w, int N, int K, const void* d_x_bf16, int M, void* d_y, int y_is_f32,
+                  void* stream) {
+  if (N <= 0 || K <= 0 || N % 128 || K % 64) return fail(GLP_ERR_INVALID_ARG, "Q8_0 GEMM needs N % 128 == 0, K % 64 == 0");
+  if (!d_q8_w) return fail(GLP_ERR_INVALID_ARG, "null weight");
+  int dev = 0;
+  GLP_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(GLP_ERR_INVALID_ARG, "device index out of range");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  __nv_bfloat16* w = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_scratch.mu);
+    const size_t need = static_cast<size_t>(N) * K;
+    if (g_scratch.cap[dev] < need) {
+      if (g_scratch.w[dev]) {
+        cudaStreamSynchronize(st);
+        cudaFree(g_scratch.w[dev]);
+        g_scratch.w[dev] = nullptr;
+        g_scratch.cap[dev] = 0;
+      }
+      GLP_CUDA(cudaMalloc(&g_scratch.w[dev], need * sizeof(__nv_bfloat16)));
+      g_scratch.cap[dev] = need;
+    }
+    w = g_scratch.w[dev];
+  }
+  const int64_t nb = static_cast<int64_t>(N) * (K / 32);
+  glp::q8_0_dequant_bf16_rows_kernel<<<static_cast<unsigned>((nb + 255) / 256), 256, 0, st>>>(
+      static_cast<const uint8_t*>(d_q8_w), N, K, w, 0, 0, 0);
+  GLP_CUDA(cudaGetLastError());
+  return run_bf16_gemm(w, N, K, d_x_bf16, M, d_y, y_is_f32, st);
+}
+
+int glp_bf16_gemm(const void* d_w_bf16, int N, int K, const void* d_x_bf16, int M, void* d_y, int y_is_f32,
+                  void* stream) {
+  return run_bf16_gemm(static_cast<const __nv_bfloat16*>(d_w_bf16), N, K, d_x_bf16, M, d_y, y_is_f32,
+                       static_cast<cudaStream_t>(stream));
+}
+
+int glp_flash_attention(const void* d_qkv, const int32_t* d_cu_seqlens, int n_seq, int max_len, int n_q_heads,
+                        int n_kv_heads, int head_dim, int window, void* d_out, void* stream) {
+  if (head_dim != glp::kAttnD) return fail(GLP_ERR_UNSUPPORTED, "head_dim must be 256");
+  if (n_seq < 0 || max_len < 0 || n_q_heads <= 0 || n_kv_heads <= 0 || n_q_heads % n_kv_heads)
+    return fail(GLP_ERR_INVALID_ARG, "bad attention shape");
+  if (n_seq == 0 || max_len == 0) return GLP_OK;
+  if (!d_qkv || !d_cu_seqlens || !d_out) return fail(GLP_ERR_INVALID_ARG, "null pointer");
+  GLP_TRY(ensure_kernel_attrs());
+  const dim3 grid(static_cast<unsigned>((max_len + glp::kAttnBQ - 1) / glp::kAttnBQ), static_cast<unsigned>(n_q_heads),
+                  static_cast<unsigned>(n_seq));
+  const int ld = (n_q_heads + 2 * n_kv_heads) * head_dim;
+  glp::flash_attn_fwd_kernel<<<grid, glp::kAttnThreads, glp::kAttnSmem, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __half*>(d_qkv), ld, d_cu_seqlens, 0, n_q_heads, n_kv_heads, window,
+      static_cast<__nv_bfloat16*>(d_out), n_q_heads * head_dim);
+  GLP_CUDA(cudaGetLastError());
+  return GLP_OK;
+}
+
+}  // extern "C"

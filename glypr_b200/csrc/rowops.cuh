@@ -1,0 +1,288 @@
+// Memory-bound row kernels (one warp per token row, 128-bit vector accesses, warp-shuffle
+// reductions) and the Q8_0 dequantisation kernels.
+//
+// Residual stream h is f32 [T, H]; the GEMM inputs x are bf16 [T, H].
+#pragma once
+#include "common.cuh"
+
+namespace glp {
+
+constexpr int kHidden = 768;           // row kernels are specialised for hidden 768
+constexpr int kVecPerLane = kHidden / 256;  // 8-element chunks per lane (3)
+
+// ---------------------------------------------------------------------------- Q8_0
+// Exact dequantisation f32(d) * q (the product of an int8 and an fp16 value is exact in
+// f32, so this is bit-identical to any correct dequantiser).  One thread per 32-block.
+__global__ void q8_0_dequant_f32_kernel(const uint8_t* __restrict__ blocks, int64_t n_blocks,
+                                        float* __restrict__ out) {
+  const int64_t b = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (b >= n_blocks) return;
+  const uint8_t* src = blocks + b * 34;
+  const float d = __half2float(__ushort_as_half(static_cast<unsigned short>(src[0] | (src[1] << 8))));
+  float4* dst = reinterpret_cast<float4*>(out + b * 32);
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const int8_t* s = reinterpret_cast<const int8_t*>(src + 2 + 4 * q);
+    dst[q] = make_float4(s[0] * d, s[1] * d, s[2] * d, s[3] * d);
+  }
+}
+
+// Dequantise a Q8_0 matrix [N, K] into bf16 rows of a destination matrix.  Row n goes to
+//   dst_row = group ? (n / group) * group_stride + row_base + n % group : row_base + n
+// which builds the fused QKV weight (row_base offsets) and the gate/up interleave
+// (group = 128, group_stride = 256, row_base = 0 for gate and 128 for up).
+__global__ void q8_0_dequant_bf16_rows_kernel(const uint8_t* __restrict__ blocks, int n, int k,
+                                              __nv_bfloat16* __restrict__ dst, int row_base, int group,
+                                              int group_stride) {
+  const int nb = k / 32;
+  const int64_t b = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (b >= static_cast<int64_t>(n) * nb) return;
+  const int row = static_cast<int>(b / nb), blk = static_cast<int>(b % nb);
+  const int drow = group ? (row / group) * group_stride + row_base + row % group : row_base + row;
+  const uint8_t* src = blocks + b * 34;
+  const float d = __half2float(__ushort_as_half(static_cast<unsigned short>(src[0] | (src[1] << 8))));
+  uint4* out = reinterpret_cast<uint4*>(dst + static_cast<size_t>(drow) * k + blk * 32);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int8_t* s = reinterpret_cast<const int8_t*>(src + 2 + 8 * q);
+    uint4 u;
+    u.x = pack_bf16(s[0] * d, s[1] * d);
+    u.y = pack_bf16(s[2] * d, s[3] * d);
+    u.z = pack_bf16(s[4] * d, s[5] * d);
+    u.w = pack_bf16(s[6] * d, s[7] * d);
+    out[q] = u;
+  }
+}
+
+// bf16 [N, K] source (BF16 GGUF weights) copied into the same fused/interleaved layout.
+__global__ void bf16_rows_copy_kernel(const __nv_bfloat16* __restrict__ src, int n, int k,
+                                      __nv_bfloat16* __restrict__ dst, int row_base, int group,
+                                      int group_stride) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;  // 8-element chunks
+  const int per_row = k / 8;
+  if (i >= static_cast<int64_t>(n) * per_row) return;
+  const int row = static_cast<int>(i / per_row), c = static_cast<int>(i % per_row);
+  const int drow = group ? (row / group) * group_stride + row_base + row % group : row_base + row;
+  reinterpret_cast<uint4*>(dst + static_cast<size_t>(drow) * k)[c] =
+      reinterpret_cast<const uint4*>(src + static_cast<size_t>(row) * k)[c];
+}
+
+// ---------------------------------------------------------------------------- helpers
+__device__ __forceinline__ void load_f32x8(const float* p, float* v) {
+  const float4 a = reinterpret_cast<const float4*>(p)[0];
+  const float4 b = reinterpret_cast<const float4*>(p)[1];
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+__device__ __forceinline__ void store_f32x8(float* p, const float* v) {
+  reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+  reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+}
+__device__ __forceinline__ void load_bf16x8(const __nv_bfloat16* p, float* v) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&w[i]);
+    const float2 f = __bfloat1622float2(h);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+__device__ __forceinline__ void store_bf16x8(__nv_bfloat16* p, const float* v) {
+  uint4 u;
+  u.x = pack_bf16(v[0], v[1]);
+  u.y = pack_bf16(v[2], v[3]);
+  u.z = pack_bf16(v[4], v[5]);
+  u.w = pack_bf16(v[6], v[7]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+
+// ---------------------------------------------------------------------------- embedding
+// h[t] = dequant(E[id_t]) * f32(sqrt(H))   (model.rs:252-255, 507-508)
+// x[t] = bf16(RMSNorm(h[t]) * w)            (first layer's attn_norm, norm.rs:22-63)
+// One warp per token; lane l covers elements l, l+32, ... (coalesced byte reads of the
+// 34-byte blocks).
+__global__ void embed_gather_norm_kernel(const uint8_t* __restrict__ table, const int* __restrict__ ids,
+                                         int n_tokens, float scale, const float* __restrict__ w, float eps,
+                                         float* __restrict__ h, __nv_bfloat16* __restrict__ x) {
+  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (t >= n_tokens) return;
+  const uint8_t* row = table + static_cast<size_t>(ids[t]) * (kHidden / 32) * 34;
+  float v[kHidden / 32];
+  float ss = 0.f;
+#pragma unroll
+  for (int b = 0; b < kHidden / 32; ++b) {
+    const uint8_t* blk = row + b * 34;
+    const float d = __half2float(__ushort_as_half(static_cast<unsigned short>(blk[0] | (blk[1] << 8))));
+    const float q = static_cast<float>(static_cast<int8_t>(blk[2 + lane]));
+    v[b] = (q * d) * scale;
+    ss = fmaf(v[b], v[b], ss);
+  }
+  ss = warp_sum(ss);
+  const float inv = 1.0f / sqrtf(ss / static_cast<float>(kHidden) + eps);
+  float* hr = h + static_cast<size_t>(t) * kHidden;
+  __nv_bfloat16* xr = x + static_cast<size_t>(t) * kHidden;
+#pragma unroll
+  for (int b = 0; b < kHidden / 32; ++b) {
+    const int e = b * 32 + lane;
+    hr[e] = v[b];
+    xr[e] = __float2bfloat16_rn(v[b] * inv * __ldg(w + e));
+  }
+}
+
+// Same gather for a bf16 token table (BF16 GGUF).
+__global__ void embed_gather_norm_bf16_kernel(const __nv_bfloat16* __restrict__ table, const int* __restrict__ ids,
+                                              int n_tokens, float scale, const float* __restrict__ w, float eps,
+                                              float* __restrict__ h, __nv_bfloat16* __restrict__ x) {
+  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (t >= n_tokens) return;
+  const __nv_bfloat16* row = table + static_cast<size_t>(ids[t]) * kHidden;
+  float v[kHidden / 32];
+  float ss = 0.f;
+#pragma unroll
+  for (int b = 0; b < kHidden / 32; ++b) {
+    v[b] = __bfloat162float(row[b * 32 + lane]) * scale;
+    ss = fmaf(v[b], v[b], ss);
+  }
+  ss = warp_sum(ss);
+  const float inv = 1.0f / sqrtf(ss / static_cast<float>(kHidden) + eps);
+  float* hr = h + static_cast<size_t>(t) * kHidden;
+  __nv_bfloat16* xr = x + static_cast<size_t>(t) * kHidden;
+#pragma unroll
+  for (int b = 0; b < kHidden / 32; ++b) {
+    const int e = b * 32 + lane;
+    hr[e] = v[b];
+    xr[e] = __float2bfloat16_rn(v[b] * inv * __ldg(w + e));
+  }
+}
+
+// ---------------------------------------------------------------------------- post-norm
+// h <- (h + RMSNorm(y) * w_post) * layer_scalar            (norm.rs:65-94, layer.rs:20-50)
+// then the next pre-norm:  x = RMSNorm(h) * w_next
+//   FINAL = false: x is bf16 (the next GEMM's input)
+//   FINAL = true : the normalised row is written back over h in f32 (output_norm, model.rs:576)
+// One warp per row; lane owns elements [c*256 + lane*8, +8) for c = 0..2.
+template <bool FINAL>
+__global__ void post_norm_residual_kernel(const __nv_bfloat16* __restrict__ y, float* __restrict__ h,
+                                          const float* __restrict__ w_post, float layer_scalar,
+                                          const float* __restrict__ w_next, float eps, int n_tokens,
+                                          __nv_bfloat16* __restrict__ x) {
+  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (t >= n_tokens) return;
+  const __nv_bfloat16* yr = y + static_cast<size_t>(t) * kHidden;
+  float* hr = h + static_cast<size_t>(t) * kHidden;
+  float yv[kVecPerLane][8], hv[kVecPerLane][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < kVecPerLane; ++c) {
+    load_bf16x8(yr + c * 256 + lane * 8, yv[c]);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ss = fmaf(yv[c][j], yv[c][j], ss);
+  }
+  ss = warp_sum(ss);
+  const float inv_y = 1.0f / sqrtf(ss / static_cast<float>(kHidden) + eps);
+  float ss2 = 0.f;
+#pragma unroll
+  for (int c = 0; c < kVecPerLane; ++c) {
+    const int e0 = c * 256 + lane * 8;
+    float wv[8];
+    load_f32x8(hr + e0, hv[c]);
+    load_f32x8(w_post + e0, wv);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      hv[c][j] = (hv[c][j] + yv[c][j] * inv_y * wv[j]) * layer_scalar;
+      ss2 = fmaf(hv[c][j], hv[c][j], ss2);
+    }
+  }
+  ss2 = warp_sum(ss2);
+  const float inv_h = 1.0f / sqrtf(ss2 / static_cast<float>(kHidden) + eps);
+#pragma unroll
+  for (int c = 0; c < kVecPerLane; ++c) {
+    const int e0 = c * 256 + lane * 8;
+    float wv[8], o[8];
+    load_f32x8(w_next + e0, wv);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = hv[c][j] * inv_h * wv[j];
+    if constexpr (FINAL) {
+      store_f32x8(hr + e0, o);
+    } else {
+      store_f32x8(hr + e0, hv[c]);
+      store_bf16x8(x + static_cast<size_t>(t) * kHidden + e0, o);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------- positions
+// pos[t] = position of token t inside its sequence (RoPE positions restart at 0 for every
+// right-padded sequence, rope.rs:53-76).  Block per sequence.
+__global__ void positions_kernel(const int* __restrict__ cu_seqlens, int cu_base, int n_seq, int* __restrict__ pos) {
+  const int b = blockIdx.x;
+  if (b >= n_seq) return;
+  const int t0 = cu_seqlens[b] - cu_base, t1 = cu_seqlens[b + 1] - cu_base;
+  for (int t = t0 + threadIdx.x; t < t1; t += blockDim.x) pos[t] = t - t0;
+}
+
+// ---------------------------------------------------------------------------- pooling
+// pooled[b] = sum_{t in seq b} xf[t] / max(len_b, 1e-9)   (model.rs:671-680), f32, fixed
+// summation order (deterministic).  Block per sequence, 192 threads x 4 columns.
+__global__ void mean_pool_kernel(const float* __restrict__ xf, const int* __restrict__ cu_seqlens, int cu_base,
+                                 int n_seq, __nv_bfloat16* __restrict__ pooled_bf16,
+                                 float* __restrict__ pooled_f32) {
+  const int b = blockIdx.x;
+  if (b >= n_seq) return;
+  const int t0 = cu_seqlens[b] - cu_base, t1 = cu_seqlens[b + 1] - cu_base;
+  const int c = threadIdx.x * 4;
+  if (c >= kHidden) return;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int t = t0; t < t1; ++t) {
+    const float4 v = *reinterpret_cast<const float4*>(xf + static_cast<size_t>(t) * kHidden + c);
+    acc.x += v.x;
+    acc.y += v.y;
+    acc.z += v.z;
+    acc.w += v.w;
+  }
+  const float cnt = fmaxf(static_cast<float>(t1 - t0), 1e-9f);
+  acc.x /= cnt;
+  acc.y /= cnt;
+  acc.z /= cnt;
+  acc.w /= cnt;
+  if (pooled_f32) *reinterpret_cast<float4*>(pooled_f32 + static_cast<size_t>(b) * kHidden + c) = acc;
+  __nv_bfloat16* pb = pooled_bf16 + static_cast<size_t>(b) * kHidden + c;
+  pb[0] = __float2bfloat16_rn(acc.x);
+  pb[1] = __float2bfloat16_rn(acc.y);
+  pb[2] = __float2bfloat16_rn(acc.z);
+  pb[3] = __float2bfloat16_rn(acc.w);
+}
+
+// L2-normalise (clamp 1e-12) then MRL: the first out_dim values renormalised
+// (model.rs:682-698).  One warp per sequence; e is f32 [n_seq, dim].
+__global__ void l2_mrl_kernel(const float* __restrict__ e, int n_seq, int dim, int out_dim,
+                              float* __restrict__ out) {
+  const int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (b >= n_seq) return;
+  const float* r = e + static_cast<size_t>(b) * dim;
+  float ss = 0.f;
+  for (int j = lane; j < dim; j += 32) ss = fmaf(r[j], r[j], ss);
+  ss = warp_sum(ss);
+  const float inv = 1.0f / fmaxf(sqrtf(ss), 1e-12f);
+  float* o = out + static_cast<size_t>(b) * out_dim;
+  if (out_dim >= dim) {
+    for (int j = lane; j < dim; j += 32) o[j] = r[j] * inv;
+    return;
+  }
+  float s2 = 0.f;
+  for (int j = lane; j < out_dim; j += 32) {
+    const float v = r[j] * inv;
+    s2 = fmaf(v, v, s2);
+  }
+  s2 = warp_sum(s2);
+  const float inv2 = 1.0f / fmaxf(sqrtf(s2), 1e-12f);
+  for (int j = lane; j < out_dim; j += 32) o[j] = (r[j] * inv) * inv2;
+}
+
+}  // namespace glp

@@ -1,0 +1,151 @@
+/* glypr_cuda.h — C ABI of libglypr_cuda.so, the B200 (sm_100a) backend for glypr's
+ * EmbeddingGemma text path: token ids -> 24-layer encoder (Q8_0 or BF16 weights) -> masked
+ * mean-pool -> dense head -> L2 -> Matryoshka truncation.
+ *
+ * Conventions (mirroring glypr-core, crates/glypr-core/src):
+ *   - every function returns an int status, GLP_OK (0) on success; on failure no partial
+ *     output is written and glp_last_error() returns a message for the calling thread
+ *     (anyhow/candle errors in the reference, e.g. lib.rs:970-976, model.rs:500-506);
+ *   - the caller owns all buffers it passes; the context owns the weights (immutable after
+ *     glp_open, like EmbeddingGemma2Model in model.rs:14-26);
+ *   - one host thread at a time may call into a given context (the reference drives one
+ *     embedder from one worker thread, glypr-server/src/engine.rs:216-253); internally a
+ *     context runs one worker thread per device.
+ *   - pointers named d_* are device pointers on the context's device `dev_index`; functions
+ *     taking a `stream` (a cudaStream_t, NULL = legacy default stream) are stream-ordered
+ *     and return before the work completes.
+ */
+#ifndef GLYPR_CUDA_H_
+#define GLYPR_CUDA_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GLP_OK 0
+#define GLP_ERR_INVALID_ARG 1
+#define GLP_ERR_IO 2
+#define GLP_ERR_FORMAT 3
+#define GLP_ERR_UNSUPPORTED 4
+#define GLP_ERR_CUDA 5
+#define GLP_ERR_OOM 6
+#define GLP_ERR_DEVICE 7        /* a kernel's bounded wait expired (device status word) */
+#define GLP_ERR_CONTEXT_LIMIT 8 /* sequence longer than the model's context_length */
+
+#define GLP_MAX_DEVICES 16
+
+typedef struct glp_ctx glp_ctx;
+
+typedef struct glp_options {
+  int64_t max_batch_tokens; /* tokens per device launch chunk; 0 = 262144 */
+  int max_batch_seqs;       /* sequences per chunk; 0 = 4096 */
+  int reserved[6];
+} glp_options;
+
+typedef struct glp_model_info_t {
+  int n_layers, hidden, ffn, n_heads, n_kv_heads, head_dim, vocab;
+  int embedding_dim;  /* embedding_length_out */
+  int max_position;   /* context_length */
+  int sliding_window; /* 512, fixed as in config.rs:191 */
+  int weight_type;    /* ggml type id of the linears: 8 = Q8_0, 30 = BF16 */
+  int n_devices;
+} glp_model_info_t;
+
+typedef struct glp_timing {
+  int n_devices;
+  float device_ms[GLP_MAX_DEVICES]; /* per device: CUDA events from first H2D to last D2H */
+} glp_timing;
+
+/* Parse a GGUF file with glypr's key/tensor schema (config.rs:76-213, model.rs:244-488)
+ * and upload one weight replica to each listed device.  Replaces
+ * GlyprEmbedder::load_gguf / load_gguf_q8 (lib.rs:176-229). */
+int glp_open(const char* gguf_path, const int* device_ids, int n_devices, const glp_options* opt,
+             glp_ctx** out);
+
+/* Release every device allocation of the context.  NULL is a no-op. */
+void glp_close(glp_ctx* ctx);
+
+/* Thread-local message of the last failed call on this thread ("" if none). */
+const char* glp_last_error(void);
+
+/* Model hyperparameters as parsed from the GGUF (TextConfig, config.rs:8-60). */
+int glp_model_info(const glp_ctx* ctx, glp_model_info_t* info);
+
+/* Embed a right-padded batch of token ids: ids [n_seq * max_len] (pad id ignored),
+ * lengths [n_seq].  Writes out [n_seq * out_dim] f32, L2-normalised; out_dim < embedding_dim
+ * applies Matryoshka truncation + renormalisation.  Host buffers; sequences are sharded
+ * across the context's devices in contiguous ranges balanced by token count.
+ * Replaces EmbeddingGemma2Model::forward + pool_and_normalize (model.rs:498-510, 654-705)
+ * as driven by GlyprEmbedder::embed_batch / profile_encode_batch (lib.rs:731-952, 994-1068).
+ * Errors: lengths[i] > context_length -> GLP_ERR_CONTEXT_LIMIT ("exceeds model
+ * max_position_embeddings", model.rs:500-506); ids outside [0, vocab) -> GLP_ERR_INVALID_ARG. */
+int glp_embed_tokens(glp_ctx* ctx, const int32_t* ids, const int32_t* lengths, int n_seq, int max_len,
+                     int out_dim, float* out, glp_timing* timing);
+
+/* Device-resident variant on one device: d_ids = packed valid tokens of all sequences,
+ * d_cu_seqlens [n_seq + 1] device offsets into d_ids, h_cu_seqlens the same offsets on the
+ * host (used to cut launch chunks); d_out [n_seq * out_dim] f32.  Stream-ordered; the ids
+ * are not range-checked (the host variant checks them). */
+int glp_embed_packed_device(glp_ctx* ctx, int dev_index, const int32_t* d_ids, const int32_t* d_cu_seqlens,
+                            const int32_t* h_cu_seqlens, int n_seq, int out_dim, float* d_out, void* stream);
+
+/* Status word of the device kernels' bounded waits on device dev_index (0 = none); a
+ * non-zero value is also reported by the next glp_embed_* call as GLP_ERR_DEVICE. */
+int glp_device_status(glp_ctx* ctx, int dev_index, int* status);
+
+/* ---- per-kernel profiling (the reference's forward_profiled, profile.rs:55-430, done with
+ * CUDA events on the launching stream instead of wall clock + device sync) ---- */
+
+#define GLP_PROFILE_KINDS 12
+
+typedef struct glp_profile {
+  int n_kinds;
+  const char* names[GLP_PROFILE_KINDS]; /* static strings owned by the library */
+  int64_t launches[GLP_PROFILE_KINDS];  /* kernel launches per kind since the last read */
+  double total_ms[GLP_PROFILE_KINDS];   /* summed event time (0 unless timing is enabled) */
+  double flops[GLP_PROFILE_KINDS];      /* algorithmic FLOPs summed over the launches */
+  double bytes[GLP_PROFILE_KINDS];      /* algorithmic HBM bytes summed over the launches */
+  int64_t total_launches;
+} glp_profile;
+
+/* enable = 1: bracket every kernel launch on device dev_index with CUDA events; 0: only
+ * count launches.  Resets the counters either way. */
+int glp_profile_enable(glp_ctx* ctx, int dev_index, int enable);
+
+/* Synchronise the recorded events and return the per-kind totals since the last
+ * enable/read, then reset them. */
+int glp_profile_read(glp_ctx* ctx, int dev_index, glp_profile* out);
+
+/* ---- kernel-level entry points (microbenchmarks and tests; current device) ---- */
+
+/* Bit-exact Q8_0 dequantisation: out[32*b + j] = f32(d_b) * q_b[j] for n_blocks 34-byte
+ * blocks {fp16 d; int8 qs[32]} (ggml block_q8_0; metal_kernels/fused_ops.metal:568-581,
+ * candle QTensor::dequantize used at model.rs:35-36). */
+int glp_q8_0_dequant(const void* d_blocks, int64_t n_blocks, float* d_out, void* stream);
+
+/* y[M, N] = x[M, K] (bf16, row-major) * dequant(W[N, K])^T, W as raw Q8_0 rows of K/32
+ * blocks; y f32 (y_is_f32 = 1) or bf16.  K % 64 == 0, N % 128 == 0.  The Q8_0 matmul behind
+ * LinearOp::forward (linear.rs:150-172; Metal fused_metal_q8_0_matmul,
+ * metal_kernels/mod.rs:1271-1394).  Dequantises W into a context-free scratch buffer
+ * owned by the library (cached per device), then runs the tcgen05 GEMM. */
+int glp_q8_0_gemm(const void* d_q8_w, int N, int K, const void* d_x_bf16, int M, void* d_y, int y_is_f32,
+                  void* stream);
+
+/* Same GEMM on an already dequantised bf16 weight [N, K] (the model path's layout). */
+int glp_bf16_gemm(const void* d_w_bf16, int N, int K, const void* d_x_bf16, int M, void* d_y, int y_is_f32,
+                  void* stream);
+
+/* Flash attention over packed qkv (f16 [T, (Hq + 2 Hkv) * 256], per-head normed + RoPE'd)
+ * for n_seq sequences at d_cu_seqlens; window > 0 applies |i - j| <= window.  Writes
+ * d_out bf16 [T, Hq * 256].  The AttentionBackend::compute_attention seam
+ * (attention/traits.rs:37-46, AttentionMode::CudaFlash at attention/mod.rs:255-262). */
+int glp_flash_attention(const void* d_qkv, const int32_t* d_cu_seqlens, int n_seq, int max_len, int n_q_heads,
+                        int n_kv_heads, int head_dim, int window, void* d_out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GLYPR_CUDA_H_ */
