@@ -68,7 +68,7 @@ __device__ __forceinline__ void attn_load_tile(uint32_t sdst, const __half* qkv,
 __global__ void __launch_bounds__(kAttnThreads, 1)
     flash_attn_fwd_kernel(const __half* __restrict__ qkv, int ld_qkv, const int* __restrict__ cu_seqlens,
                           int cu_base, int n_q_heads, int n_kv_heads, int window,
-                          __nv_bfloat16* __restrict__ out, int ld_out) {
+                          __half* __restrict__ out, int ld_out) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
   const uint32_t sQ = smem_u32(smem);
@@ -220,7 +220,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     __syncthreads();  // this stage is overwritten by the load issued next iteration
   }
 
-  // ---- normalise and store (bf16, the O-projection input)
+  // ---- normalise and store (f16, the O-projection input)
   l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
   l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
   l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
@@ -229,16 +229,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const float r1 = l1 > 0.f ? 1.0f / l1 : 0.f;
   const int dcol = qcol + 2 * (lane & 3);
   if (i0 < len) {
-    __nv_bfloat16* dst = out + static_cast<size_t>(tok0 + i0) * ld_out + dcol;
+    __half* dst = out + static_cast<size_t>(tok0 + i0) * ld_out + dcol;
 #pragma unroll
     for (int n = 0; n < 32; ++n)
-      *reinterpret_cast<uint32_t*>(dst + n * 8) = pack_bf16(o[n][0] * r0, o[n][1] * r0);
+      *reinterpret_cast<uint32_t*>(dst + n * 8) = pack_f16(o[n][0] * r0, o[n][1] * r0);
   }
   if (i1 < len) {
-    __nv_bfloat16* dst = out + static_cast<size_t>(tok0 + i1) * ld_out + dcol;
+    __half* dst = out + static_cast<size_t>(tok0 + i1) * ld_out + dcol;
 #pragma unroll
     for (int n = 0; n < 32; ++n)
-      *reinterpret_cast<uint32_t*>(dst + n * 8) = pack_bf16(o[n][2] * r1, o[n][3] * r1);
+      *reinterpret_cast<uint32_t*>(dst + n * 8) = pack_f16(o[n][2] * r1, o[n][3] * r1);
   }
 }
 

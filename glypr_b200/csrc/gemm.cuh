@@ -1,7 +1,7 @@
 // Persistent tcgen05 GEMM for sm_100a:  C[M, N] = A[M, K] * B[N, K]^T
 //
-//   A  activations, bf16, row-major (K contiguous)        -> TMA, 128B swizzle
-//   B  weights (dequantised Q8_0 or bf16), row-major [N,K] -> TMA, 128B swizzle
+//   A  activations, 16-bit T (f16 or bf16), row-major (K contiguous) -> TMA, 128B swizzle
+//   B  weights (dequantised Q8_0 / converted BF16) as T, row-major [N,K] -> TMA, 128B swizzle
 //   accumulator f32 in tensor memory (TMEM), two buffers of BN columns
 //
 // Roles (192 threads): warp 0 = TMA producer, warp 1 = MMA issuer (+ TMEM owner),
@@ -11,18 +11,18 @@
 // once, then from L2) while the weights stay L2-resident.
 //
 // Epilogues (fused so the activations make one trip through HBM):
-//   kEpiBf16    store bf16
+//   kEpiStore16 store T
 //   kEpiF32     store f32
 //   kEpiQkv     per-head RMSNorm (q/k with gain, v without), NeoX RoPE on q/k, store f16.
 //               One 256-column tile == one head (attention/mod.rs:166-188, rope.rs:90-106).
-//   kEpiGeglu   B rows interleaved [gate 128 | up 128] per tile; out = gelu_tanh(g)*u, bf16
+//   kEpiGeglu   B rows interleaved [gate 128 | up 128] per tile; out = gelu_tanh(g)*u as T
 //               (cpu_simd/geglu.rs:6-18, with its +-10 clamp).
 #pragma once
 #include "common.cuh"
 
 namespace glp {
 
-enum EpiKind : int { kEpiBf16 = 0, kEpiF32 = 1, kEpiQkv = 2, kEpiGeglu = 3 };
+enum EpiKind : int { kEpiStore16 = 0, kEpiF32 = 1, kEpiQkv = 2, kEpiGeglu = 3 };
 
 struct GemmParams {
   int M, N, K;
@@ -32,9 +32,10 @@ struct GemmParams {
   // kEpiQkv
   const float* q_gain;    // [head_dim]
   const float* k_gain;    // [head_dim]
-  const float* rope_cos;  // [max_pos, head_dim/2] (cos of freqs; the table's halves are equal)
-  const float* rope_sin;  // [max_pos, head_dim/2]
+  const float* rope_cos;  // [head_dim/2, rope_stride] frequency-major (the table's halves are equal)
+  const float* rope_sin;  // [head_dim/2, rope_stride]
   const int* pos;         // [M] position of each row inside its sequence
+  int rope_stride;        // positions per frequency row (the model's context length)
   int n_q_heads, n_kv_heads;
   float eps;
   int* status;  // device status word (error codes above)
@@ -51,28 +52,16 @@ struct GemmCfg {
   static constexpr size_t SMEM = 1024 + STAGES * (A_BYTES + B_BYTES) + 256;
 };
 
-__device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float* v) {
+template <typename T>
+__device__ __forceinline__ void store16x32(T* dst, const float* v) {
   uint4* d = reinterpret_cast<uint4*>(dst);
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     uint4 u;
-    u.x = pack_bf16(v[8 * q + 0], v[8 * q + 1]);
-    u.y = pack_bf16(v[8 * q + 2], v[8 * q + 3]);
-    u.z = pack_bf16(v[8 * q + 4], v[8 * q + 5]);
-    u.w = pack_bf16(v[8 * q + 6], v[8 * q + 7]);
-    d[q] = u;
-  }
-}
-
-__device__ __forceinline__ void store_f16x32(__half* dst, const float* v) {
-  uint4* d = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    uint4 u;
-    u.x = pack_f16(v[8 * q + 0], v[8 * q + 1]);
-    u.y = pack_f16(v[8 * q + 2], v[8 * q + 3]);
-    u.z = pack_f16(v[8 * q + 4], v[8 * q + 5]);
-    u.w = pack_f16(v[8 * q + 6], v[8 * q + 7]);
+    u.x = Half16<T>::pack(v[8 * q + 0], v[8 * q + 1]);
+    u.y = Half16<T>::pack(v[8 * q + 2], v[8 * q + 3]);
+    u.z = Half16<T>::pack(v[8 * q + 4], v[8 * q + 5]);
+    u.w = Half16<T>::pack(v[8 * q + 6], v[8 * q + 7]);
     d[q] = u;
   }
 }
@@ -86,13 +75,13 @@ __device__ __forceinline__ float geglu_f(float g, float u) {
   return __fdividef(g, 1.0f + __expf(-2.0f * z)) * u;
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, typename T>
 __device__ __forceinline__ void gemm_epilogue_tile(const GemmParams& p, uint32_t tacc, int m_blk, int n_blk,
                                                    int row_in_tile) {
   const int row = m_blk * 128 + row_in_tile;
   const bool live = row < p.M;
   uint32_t r[32];
-  if constexpr (EPI == kEpiBf16 || EPI == kEpiF32) {
+  if constexpr (EPI == kEpiStore16 || EPI == kEpiF32) {
 #pragma unroll 1
     for (int c = 0; c < BN / 32; ++c) {
       tmem_ld32(tacc + c * 32, r);
@@ -102,8 +91,8 @@ __device__ __forceinline__ void gemm_epilogue_tile(const GemmParams& p, uint32_t
       for (int j = 0; j < 32; ++j) v[j] = u2f(r[j]);
       if (live) {
         const size_t off = static_cast<size_t>(row) * p.ldc + static_cast<size_t>(n_blk) * BN + c * 32;
-        if constexpr (EPI == kEpiBf16) {
-          store_bf16x32(reinterpret_cast<__nv_bfloat16*>(p.C) + off, v);
+        if constexpr (EPI == kEpiStore16) {
+          store16x32<T>(reinterpret_cast<T*>(p.C) + off, v);
         } else {
           float4* d = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.C) + off);
 #pragma unroll
@@ -124,7 +113,7 @@ __device__ __forceinline__ void gemm_epilogue_tile(const GemmParams& p, uint32_t
       for (int j = 0; j < 32; ++j) v[j] = geglu_f(u2f(r[j]), u2f(u[j]));
       if (live) {
         const size_t off = static_cast<size_t>(row) * p.ldc + static_cast<size_t>(n_blk) * 128 + c * 32;
-        store_bf16x32(reinterpret_cast<__nv_bfloat16*>(p.C) + off, v);
+        store16x32<T>(reinterpret_cast<T*>(p.C) + off, v);
       }
     }
   } else {  // kEpiQkv
@@ -144,12 +133,22 @@ __device__ __forceinline__ void gemm_epilogue_tile(const GemmParams& p, uint32_t
     const float* gain = is_q ? p.q_gain : (is_k ? p.k_gain : nullptr);
     const bool rope = is_q || is_k;
     const int pos = live ? p.pos[row] : 0;
-    const float* cs = p.rope_cos + static_cast<size_t>(pos) * 128;
-    const float* sn = p.rope_sin + static_cast<size_t>(pos) * 128;
+    // frequency-major tables: lanes (consecutive rows) read consecutive positions
+    const float* cs = p.rope_cos + pos;
+    const float* sn = p.rope_sin + pos;
+    const size_t fstride = static_cast<size_t>(p.rope_stride);
     __half* out = reinterpret_cast<__half*>(p.C) + static_cast<size_t>(row) * p.ldc + static_cast<size_t>(n_blk) * 256;
 #pragma unroll 1
     for (int c = 0; c < 4; ++c) {
       uint32_t h[32];
+      float cv[32], sv[32];
+      if (rope) {  // issue the table loads before waiting on tensor memory
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          cv[j] = __ldg(cs + static_cast<size_t>(c * 32 + j) * fstride);
+          sv[j] = __ldg(sn + static_cast<size_t>(c * 32 + j) * fstride);
+        }
+      }
       tmem_ld32(tacc + c * 32, r);        // x[i],       i = 32c + j
       tmem_ld32(tacc + 128 + c * 32, h);  // x[i + 128]
       tmem_ld_wait();
@@ -164,23 +163,22 @@ __device__ __forceinline__ void gemm_epilogue_tile(const GemmParams& p, uint32_t
           x2 *= __ldg(gain + i + 128);
         }
         if (rope) {
-          const float cv = __ldg(cs + i), sv = __ldg(sn + i);
-          lo[j] = x1 * cv + (-x2) * sv;  // x*cos + rotate_half(x)*sin, rotate_half = cat(-x2, x1)
-          hi[j] = x2 * cv + x1 * sv;
+          lo[j] = x1 * cv[j] + (-x2) * sv[j];  // x*cos + rotate_half(x)*sin, rotate_half = cat(-x2, x1)
+          hi[j] = x2 * cv[j] + x1 * sv[j];
         } else {
           lo[j] = x1;
           hi[j] = x2;
         }
       }
       if (live) {
-        store_f16x32(out + c * 32, lo);
-        store_f16x32(out + 128 + c * 32, hi);
+        store16x32<__half>(out + c * 32, lo);
+        store16x32<__half>(out + 128 + c * 32, hi);
       }
     }
   }
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, typename T>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const GemmParams p) {
@@ -252,7 +250,7 @@ __global__ void __launch_bounds__(192, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       // ------------------------------------------------------------ MMA issuer
-      constexpr uint32_t idesc = idesc_f16(128, BN, 1);
+      constexpr uint32_t idesc = idesc_f16(128, BN, Half16<T>::kIsBf16);
       int s = 0;
       uint32_t ph = 0;
       int ab = 0;
@@ -319,7 +317,7 @@ __global__ void __launch_bounds__(192, 1)
       }
       tc_fence_after();
       const uint32_t tacc = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(ab * BN);
-      gemm_epilogue_tile<BN, EPI>(p, tacc, m_blk, n_blk, row_in_tile);
+      gemm_epilogue_tile<BN, EPI, T>(p, tacc, m_blk, n_blk, row_in_tile);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[ab]);

@@ -24,6 +24,7 @@
 #include <vector>
 
 #include "attention.cuh"
+#include "attention_tc.cuh"
 #include "gemm.cuh"
 #include "gguf.h"
 #include "glypr_cuda.h"
@@ -72,9 +73,10 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// 2-D bf16 row-major [rows, cols] tensor, box = 64 columns (one 128-byte swizzle row) x
-// box_rows rows, 128B swizzle, out-of-bounds rows read as zero.
-int make_map_bf16(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int64_t ld_elems, int box_rows) {
+// 2-D 16-bit row-major [rows, cols] tensor, box = 64 columns (one 128-byte swizzle row) x
+// box_rows rows, 128B swizzle, out-of-bounds rows read as zero.  f16 = true for the model
+// path's operands, false for bf16.
+int make_map16(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int64_t ld_elems, int box_rows, bool f16) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return fail(GLP_ERR_CUDA, "cuTensorMapEncodeTiled unavailable (driver too old?)");
   if ((reinterpret_cast<uintptr_t>(base) & 15) || (ld_elems * 2) % 16 || cols % 64)
@@ -83,10 +85,50 @@ int make_map_bf16(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, 
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld_elems * 2)};
   const cuuint32_t box[2] = {64u, static_cast<cuuint32_t>(box_rows)};
   const cuuint32_t estr[2] = {1u, 1u};
-  const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  const CUresult r = fn(m, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                        const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(GLP_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string(r));
+  return GLP_OK;
+}
+
+// Attention engine: tcgen05 (default) or the warp-level mma.sync kernel (GLP_ATTENTION=mma).
+bool use_tc_attention() {
+  static const bool tc = [] {
+    const char* e = std::getenv("GLP_ATTENTION");
+    return !(e && std::string(e) == "mma");
+  }();
+  return tc;
+}
+
+// Launch attention over packed qkv rows [0, T) for n_seq sequences at cu (minus cu_base).
+int launch_attention(const __half* qkv, int64_t T, int qkv_width, const int* cu, int cu_base, int n_seq, int max_len,
+                     int n_q_heads, int n_kv_heads, int window, __half* out, int* status, cudaStream_t st) {
+  if (T <= 0 || n_seq <= 0 || max_len <= 0) return GLP_OK;
+  if (use_tc_attention()) {
+    CUtensorMap mq, mkv;
+    GLP_TRY(make_map16(&mq, qkv, T, qkv_width, qkv_width, glp::kFaBQ, true));
+    GLP_TRY(make_map16(&mkv, qkv, T, qkv_width, qkv_width, glp::kFaBKV, true));
+    glp::FaParams fp{};
+    fp.cu_seqlens = cu;
+    fp.cu_base = cu_base;
+    fp.n_q_heads = n_q_heads;
+    fp.n_kv_heads = n_kv_heads;
+    fp.window = window;
+    fp.out = out;
+    fp.ld_out = n_q_heads * glp::kFaD;
+    fp.status = status;
+    const dim3 grid(static_cast<unsigned>((max_len + glp::kFaBQ - 1) / glp::kFaBQ), static_cast<unsigned>(n_q_heads),
+                    static_cast<unsigned>(n_seq));
+    glp::flash_attn_tc_kernel<<<grid, 192, glp::kFaSmem, st>>>(mq, mkv, fp);
+  } else {
+    const dim3 grid(static_cast<unsigned>((max_len + glp::kAttnBQ - 1) / glp::kAttnBQ), static_cast<unsigned>(n_q_heads),
+                    static_cast<unsigned>(n_seq));
+    glp::flash_attn_fwd_kernel<<<grid, glp::kAttnThreads, glp::kAttnSmem, st>>>(
+        qkv, qkv_width, cu, cu_base, n_q_heads, n_kv_heads, window, out, n_q_heads * glp::kAttnD);
+  }
+  GLP_CUDA(cudaGetLastError());
   return GLP_OK;
 }
 
@@ -100,20 +142,22 @@ int ensure_kernel_attrs() {
   std::lock_guard<std::mutex> lk(g_attr_mu);
   if (dev < 0 || dev >= 64) return fail(GLP_ERR_INVALID_ARG, "device index out of range");
   if (g_attr_done[dev]) return GLP_OK;
-  GLP_CUDA(cudaFuncSetAttribute(glp::gemm_tc_kernel<256, glp::kEpiBf16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                static_cast<int>(glp::GemmCfg<256>::SMEM)));
-  GLP_CUDA(cudaFuncSetAttribute(glp::gemm_tc_kernel<256, glp::kEpiF32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                static_cast<int>(glp::GemmCfg<256>::SMEM)));
-  GLP_CUDA(cudaFuncSetAttribute(glp::gemm_tc_kernel<256, glp::kEpiQkv>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                static_cast<int>(glp::GemmCfg<256>::SMEM)));
-  GLP_CUDA(cudaFuncSetAttribute(glp::gemm_tc_kernel<256, glp::kEpiGeglu>,
-                                cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(glp::GemmCfg<256>::SMEM)));
-  GLP_CUDA(cudaFuncSetAttribute(glp::gemm_tc_kernel<128, glp::kEpiBf16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                static_cast<int>(glp::GemmCfg<128>::SMEM)));
-  GLP_CUDA(cudaFuncSetAttribute(glp::gemm_tc_kernel<128, glp::kEpiF32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                static_cast<int>(glp::GemmCfg<128>::SMEM)));
+  const int s256 = static_cast<int>(glp::GemmCfg<256>::SMEM), s128 = static_cast<int>(glp::GemmCfg<128>::SMEM);
+  const cudaFuncAttribute A = cudaFuncAttributeMaxDynamicSharedMemorySize;
+  GLP_CUDA(cudaFuncSetAttribute(glp::gemm_tc_kernel<256, glp::kEpiStore16, __half>, A, s256));
+  GLP_CUDA(cudaFuncSetAttribute(glp::gemm_tc_kernel<256, glp::kEpiF32, __half>, A, s256));
+  GLP_CUDA(cudaFuncSetAttribute(glp::gemm_tc_kernel<256, glp::kEpiQkv, __half>, A, s256));
+  GLP_CUDA(cudaFuncSetAttribute(glp::gemm_tc_kernel<256, glp::kEpiGeglu, __half>, A, s256));
+  GLP_CUDA(cudaFuncSetAttribute(glp::gemm_tc_kernel<128, glp::kEpiStore16, __half>, A, s128));
+  GLP_CUDA(cudaFuncSetAttribute(glp::gemm_tc_kernel<128, glp::kEpiF32, __half>, A, s128));
+  GLP_CUDA(cudaFuncSetAttribute(glp::gemm_tc_kernel<256, glp::kEpiStore16, __nv_bfloat16>, A, s256));
+  GLP_CUDA(cudaFuncSetAttribute(glp::gemm_tc_kernel<256, glp::kEpiF32, __nv_bfloat16>, A, s256));
+  GLP_CUDA(cudaFuncSetAttribute(glp::gemm_tc_kernel<128, glp::kEpiStore16, __nv_bfloat16>, A, s128));
+  GLP_CUDA(cudaFuncSetAttribute(glp::gemm_tc_kernel<128, glp::kEpiF32, __nv_bfloat16>, A, s128));
   GLP_CUDA(cudaFuncSetAttribute(glp::flash_attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 static_cast<int>(glp::kAttnSmem)));
+  GLP_CUDA(cudaFuncSetAttribute(glp::flash_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(glp::kFaSmem)));
   g_attr_done[dev] = true;
   return GLP_OK;
 }
@@ -127,8 +171,9 @@ int sm_count() {
 
 int bn_for(int n) { return n % 256 == 0 ? 256 : 128; }
 
-// Launch C = A * B^T with the given epilogue.  `ma` covers A [M, K] (box rows 128), `mb`
-// covers B [N, K] with box rows == bn.
+// Launch C = A * B^T with the given epilogue; T is the 16-bit operand type.  `ma` covers
+// A [M, K] (box rows 128), `mb` covers B [N, K] with box rows == bn.
+template <typename T>
 int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, int bn, int epi, GemmParams p, cudaStream_t st) {
   p.m_tiles = (p.M + 127) / 128;
   p.n_tiles = p.N / bn;
@@ -137,20 +182,27 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, int bn, int epi, G
   if (p.K % 64 || p.N % bn || p.K <= 0) return fail(GLP_ERR_INVALID_ARG, "GEMM needs K % 64 == 0 and N % tile == 0");
   const int tiles = p.m_tiles * p.n_tiles;
   const int grid = std::min(tiles, sm_count());
+  const bool f16 = std::is_same<T, __half>::value;
   if (bn == 256) {
     const size_t smem = glp::GemmCfg<256>::SMEM;
     switch (epi) {
-      case glp::kEpiBf16: glp::gemm_tc_kernel<256, glp::kEpiBf16><<<grid, 192, smem, st>>>(ma, mb, p); break;
-      case glp::kEpiF32: glp::gemm_tc_kernel<256, glp::kEpiF32><<<grid, 192, smem, st>>>(ma, mb, p); break;
-      case glp::kEpiQkv: glp::gemm_tc_kernel<256, glp::kEpiQkv><<<grid, 192, smem, st>>>(ma, mb, p); break;
-      case glp::kEpiGeglu: glp::gemm_tc_kernel<256, glp::kEpiGeglu><<<grid, 192, smem, st>>>(ma, mb, p); break;
+      case glp::kEpiStore16: glp::gemm_tc_kernel<256, glp::kEpiStore16, T><<<grid, 192, smem, st>>>(ma, mb, p); break;
+      case glp::kEpiF32: glp::gemm_tc_kernel<256, glp::kEpiF32, T><<<grid, 192, smem, st>>>(ma, mb, p); break;
+      case glp::kEpiQkv:
+        if (!f16) return fail(GLP_ERR_INVALID_ARG, "fused epilogues run on f16 operands");
+        glp::gemm_tc_kernel<256, glp::kEpiQkv, __half><<<grid, 192, smem, st>>>(ma, mb, p);
+        break;
+      case glp::kEpiGeglu:
+        if (!f16) return fail(GLP_ERR_INVALID_ARG, "fused epilogues run on f16 operands");
+        glp::gemm_tc_kernel<256, glp::kEpiGeglu, __half><<<grid, 192, smem, st>>>(ma, mb, p);
+        break;
       default: return fail(GLP_ERR_INVALID_ARG, "bad epilogue");
     }
   } else {
     const size_t smem = glp::GemmCfg<128>::SMEM;
     switch (epi) {
-      case glp::kEpiBf16: glp::gemm_tc_kernel<128, glp::kEpiBf16><<<grid, 192, smem, st>>>(ma, mb, p); break;
-      case glp::kEpiF32: glp::gemm_tc_kernel<128, glp::kEpiF32><<<grid, 192, smem, st>>>(ma, mb, p); break;
+      case glp::kEpiStore16: glp::gemm_tc_kernel<128, glp::kEpiStore16, T><<<grid, 192, smem, st>>>(ma, mb, p); break;
+      case glp::kEpiF32: glp::gemm_tc_kernel<128, glp::kEpiF32, T><<<grid, 192, smem, st>>>(ma, mb, p); break;
       default: return fail(GLP_ERR_INVALID_ARG, "fused epilogues need 256-wide tiles");
     }
   }
@@ -286,7 +338,7 @@ int validate_tensors(const glp::GgufFile& g, const Config& c) {
 
 // ------------------------------------------------------------------------------ device state
 struct LayerW {
-  __nv_bfloat16 *qkv = nullptr, *o = nullptr, *gu = nullptr, *down = nullptr;
+  __half *qkv = nullptr, *o = nullptr, *gu = nullptr, *down = nullptr;  // f16 weights
   float *attn_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr, *post_attn = nullptr, *ffn_norm = nullptr,
         *post_ffw = nullptr;
   float layer_scalar = 1.0f;
@@ -295,7 +347,7 @@ struct LayerW {
 };
 
 struct HeadW {
-  __nv_bfloat16* w = nullptr;
+  __half* w = nullptr;
   int n = 0, k = 0, bn = 256;
   CUtensorMap map;
 };
@@ -314,14 +366,14 @@ struct Device {
   int64_t cap_tokens = 0;
   int cap_seqs = 0;
   float* h = nullptr;
-  __nv_bfloat16* x = nullptr;
+  __half* x = nullptr;
   __half* qkv = nullptr;
-  __nv_bfloat16* attn = nullptr;
-  __nv_bfloat16* y = nullptr;
-  __nv_bfloat16* a = nullptr;
+  __half* attn = nullptr;
+  __half* y = nullptr;
+  __half* a = nullptr;
   int* pos = nullptr;
-  __nv_bfloat16* pooled = nullptr;
-  __nv_bfloat16* mid = nullptr;
+  __half* pooled = nullptr;
+  __half* mid = nullptr;
   float* emb = nullptr;
   int* status = nullptr;
   // host-API staging (device + pinned host), grown on demand
@@ -470,7 +522,7 @@ int upload_gain(Device& d, const glp::GgufFile& g, const std::string& name, int 
 
 // Upload linear `name` [n, k] into rows of dst (bf16 [*, k]) with the row mapping of
 // q8_0_dequant_bf16_rows_kernel.  Uses a device staging buffer for the raw bytes.
-int upload_linear(Device& d, const glp::GgufFile& g, const std::string& name, int n, int k, __nv_bfloat16* dst,
+int upload_linear(Device& d, const glp::GgufFile& g, const std::string& name, int n, int k, __half* dst,
                   int row_base, int group, int group_stride, void* staging, size_t staging_bytes) {
   const glp::GgufTensor* t = g.tensor(name);
   if (!t) return fail(GLP_ERR_FORMAT, "missing tensor " + name);
@@ -479,11 +531,11 @@ int upload_linear(Device& d, const glp::GgufFile& g, const std::string& name, in
   GLP_CUDA(cudaMemcpy(staging, t->data, t->nbytes, cudaMemcpyHostToDevice));
   if (t->type == glp::kGgmlQ8_0) {
     const int64_t nb = static_cast<int64_t>(n) * (k / 32);
-    glp::q8_0_dequant_bf16_rows_kernel<<<static_cast<unsigned>((nb + 255) / 256), 256>>>(
+    glp::q8_0_dequant_rows_kernel<__half><<<static_cast<unsigned>((nb + 255) / 256), 256>>>(
         static_cast<const uint8_t*>(staging), n, k, dst, row_base, group, group_stride);
   } else if (t->type == glp::kGgmlBF16) {
-    const int64_t nc = static_cast<int64_t>(n) * (k / 8);
-    glp::bf16_rows_copy_kernel<<<static_cast<unsigned>((nc + 255) / 256), 256>>>(
+    const int64_t nc = static_cast<int64_t>(n) * (k / 2);
+    glp::bf16_rows_convert_kernel<__half><<<static_cast<unsigned>((nc + 255) / 256), 256>>>(
         static_cast<const __nv_bfloat16*>(staging), n, k, dst, row_base, group, group_stride);
   } else {
     return fail(GLP_ERR_UNSUPPORTED, "linear " + name + " must be Q8_0 or BF16");
@@ -495,16 +547,17 @@ int upload_linear(Device& d, const glp::GgufFile& g, const std::string& name, in
 
 // RoPE tables exactly as rope.rs:14-87: inv_freq_i = f32(1 / theta^(2i/d)) in f64, then
 // freqs = f32(pos) * inv_freq (f32), cos/sin in f32.  Only the first half is stored (the
-// reference table is cat(freqs, freqs)).
+// reference table is cat(freqs, freqs)), frequency-major [half][max_pos] so that the GEMM
+// epilogue's 32 lanes (consecutive rows = consecutive positions) read one coalesced line.
 int upload_rope(Device& d, double theta, int d_head, int max_pos, float** cs, float** sn) {
   const int half = d_head / 2;
   std::vector<float> inv(half), c(static_cast<size_t>(max_pos) * half), s(static_cast<size_t>(max_pos) * half);
   for (int i = 0; i < half; ++i) inv[i] = static_cast<float>(1.0 / std::pow(theta, (2.0 * i) / d_head));
-  for (int p = 0; p < max_pos; ++p)
-    for (int i = 0; i < half; ++i) {
+  for (int i = 0; i < half; ++i)
+    for (int p = 0; p < max_pos; ++p) {
       const float f = static_cast<float>(p) * inv[i];
-      c[static_cast<size_t>(p) * half + i] = std::cos(f);
-      s[static_cast<size_t>(p) * half + i] = std::sin(f);
+      c[static_cast<size_t>(i) * max_pos + p] = std::cos(f);
+      s[static_cast<size_t>(i) * max_pos + p] = std::sin(f);
     }
   GLP_TRY(d.alloc(cs, c.size()));
   GLP_TRY(d.alloc(sn, s.size()));
@@ -584,10 +637,10 @@ int setup_device(Device& d, const Config& c, const glp::GgufFile& g, int64_t cap
     GLP_TRY(upload_linear(d, g, p + "ffn_gate.weight", F, H, L.gu, 0, 128, 256, staging, staging_bytes));
     GLP_TRY(upload_linear(d, g, p + "ffn_up.weight", F, H, L.gu, 128, 128, 256, staging, staging_bytes));
     GLP_TRY(upload_linear(d, g, p + "ffn_down.weight", H, F, L.down, 0, 0, 0, staging, staging_bytes));
-    GLP_TRY(make_map_bf16(&L.m_qkv, L.qkv, QKV, H, H, 256));
-    GLP_TRY(make_map_bf16(&L.m_o, L.o, H, AW, AW, bn_for(H)));
-    GLP_TRY(make_map_bf16(&L.m_gu, L.gu, 2 * F, H, H, 256));
-    GLP_TRY(make_map_bf16(&L.m_down, L.down, H, F, F, bn_for(H)));
+    GLP_TRY(make_map16(&L.m_qkv, L.qkv, QKV, H, H, 256, true));
+    GLP_TRY(make_map16(&L.m_o, L.o, H, AW, AW, bn_for(H), true));
+    GLP_TRY(make_map16(&L.m_gu, L.gu, 2 * F, H, H, 256, true));
+    GLP_TRY(make_map16(&L.m_down, L.down, H, F, F, bn_for(H), true));
   }
   GLP_TRY(upload_gain(d, g, "output_norm.weight", H, &d.out_norm));
   // dense head: dense.0 .. dense.N (BASELINE two-stage 768->3072->768), else output.weight
@@ -603,7 +656,7 @@ int setup_device(Device& d, const Config& c, const glp::GgufFile& g, int64_t cap
     hw.bn = bn_for(hw.n);
     GLP_TRY(d.alloc(&hw.w, static_cast<size_t>(hw.n) * hw.k));
     GLP_TRY(upload_linear(d, g, nm, hw.n, hw.k, hw.w, 0, 0, 0, staging, staging_bytes));
-    GLP_TRY(make_map_bf16(&hw.map, hw.w, hw.n, hw.k, hw.k, hw.bn));
+    GLP_TRY(make_map16(&hw.map, hw.w, hw.n, hw.k, hw.k, hw.bn, true));
     d.head.push_back(hw);
     prev = hw.n;
   }
@@ -617,7 +670,7 @@ int setup_device(Device& d, const Config& c, const glp::GgufFile& g, int64_t cap
     hw.bn = bn_for(hw.n);
     GLP_TRY(d.alloc(&hw.w, static_cast<size_t>(hw.n) * hw.k));
     GLP_TRY(upload_linear(d, g, "output.weight", hw.n, hw.k, hw.w, 0, 0, 0, staging, staging_bytes));
-    GLP_TRY(make_map_bf16(&hw.map, hw.w, hw.n, hw.k, hw.k, hw.bn));
+    GLP_TRY(make_map16(&hw.map, hw.w, hw.n, hw.k, hw.k, hw.bn, true));
     d.head.push_back(hw);
   }
   if (d.head.back().n != c.emb_out) return fail(GLP_ERR_FORMAT, "head output dim != embedding_length_out");
@@ -679,11 +732,9 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
     }));
 
     CUtensorMap m_x, m_attn, m_a;
-    GLP_TRY(make_map_bf16(&m_x, d.x, T, H, H, 128));
-    GLP_TRY(make_map_bf16(&m_attn, d.attn, T, AW, AW, 128));
-    GLP_TRY(make_map_bf16(&m_a, d.a, T, F, F, 128));
-    const dim3 attn_grid(static_cast<unsigned>((max_len + glp::kAttnBQ - 1) / glp::kAttnBQ),
-                         static_cast<unsigned>(c.n_heads), static_cast<unsigned>(n_seq));
+    GLP_TRY(make_map16(&m_x, d.x, T, H, H, 128, true));
+    GLP_TRY(make_map16(&m_attn, d.attn, T, AW, AW, 128, true));
+    GLP_TRY(make_map16(&m_a, d.a, T, F, F, 128, true));
     double pairs_local = 0, pairs_global = 0;
     for (int b = 0; b < n_seq; ++b) {
       const int64_t len = h_cu_chunk[b + 1] - h_cu_chunk[b];
@@ -707,18 +758,17 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
       p.rope_cos = L.sliding ? d.cos_swa : d.cos_full;
       p.rope_sin = L.sliding ? d.sin_swa : d.sin_full;
       p.pos = d.pos;
+      p.rope_stride = c.max_pos;
       p.n_q_heads = c.n_heads;
       p.n_kv_heads = c.n_kv;
       p.eps = eps;
       GLP_TRY(prof_launch(d, st, kProfGemmQkv, gemm_flops(Td, QKV, H), gemm_bytes(Td, QKV, H, 2.0),
-                          [&] { return launch_gemm(m_x, L.m_qkv, 256, glp::kEpiQkv, p, st); }));
+                          [&] { return launch_gemm<__half>(m_x, L.m_qkv, 256, glp::kEpiQkv, p, st); }));
       // attention
       const double pairs = L.sliding ? pairs_local : pairs_global;
       GLP_TRY(prof_launch(d, st, kProfAttention, 4.0 * D * c.n_heads * pairs, attn_bytes, [&] {
-        glp::flash_attn_fwd_kernel<<<attn_grid, glp::kAttnThreads, glp::kAttnSmem, st>>>(
-            d.qkv, QKV, d_cu_chunk, base, c.n_heads, c.n_kv, L.sliding ? c.window : 0, d.attn, AW);
-        GLP_CUDA(cudaGetLastError());
-        return GLP_OK;
+        return launch_attention(d.qkv, T, QKV, d_cu_chunk, base, n_seq, max_len, c.n_heads, c.n_kv,
+                                L.sliding ? c.window : 0, d.attn, d.status, st);
       }));
       // O projection
       GemmParams po{};
@@ -729,7 +779,7 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
       po.ldc = H;
       po.status = d.status;
       GLP_TRY(prof_launch(d, st, kProfGemmO, gemm_flops(Td, H, AW), gemm_bytes(Td, H, AW, 2.0),
-                          [&] { return launch_gemm(m_attn, L.m_o, bn_for(H), glp::kEpiBf16, po, st); }));
+                          [&] { return launch_gemm<__half>(m_attn, L.m_o, bn_for(H), glp::kEpiStore16, po, st); }));
       GLP_TRY(prof_launch(d, st, kProfPostNorm, 0.0, post_bytes, [&] {
         glp::post_norm_residual_kernel<false><<<rows_grid, 256, 0, st>>>(d.y, d.h, L.post_attn, 1.0f, L.ffn_norm,
                                                                          eps, T, d.x);
@@ -746,7 +796,7 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
       pg.status = d.status;
       GLP_TRY(prof_launch(d, st, kProfGemmGateUp, gemm_flops(Td, 2.0 * F, H),
                           2.0 * Td * H + 2.0 * 2.0 * F * H + 2.0 * Td * F,
-                          [&] { return launch_gemm(m_x, L.m_gu, 256, glp::kEpiGeglu, pg, st); }));
+                          [&] { return launch_gemm<__half>(m_x, L.m_gu, 256, glp::kEpiGeglu, pg, st); }));
       // down projection
       GemmParams pd{};
       pd.M = T;
@@ -756,7 +806,7 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
       pd.ldc = H;
       pd.status = d.status;
       GLP_TRY(prof_launch(d, st, kProfGemmDown, gemm_flops(Td, H, F), gemm_bytes(Td, H, F, 2.0),
-                          [&] { return launch_gemm(m_a, L.m_down, bn_for(H), glp::kEpiBf16, pd, st); }));
+                          [&] { return launch_gemm<__half>(m_a, L.m_down, bn_for(H), glp::kEpiStore16, pd, st); }));
       const bool last = l + 1 == c.n_layers;
       GLP_TRY(prof_launch(d, st, kProfPostNorm, 0.0, last ? Td * 10.0 * H : post_bytes, [&] {
         if (!last)
@@ -776,13 +826,13 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
     GLP_CUDA(cudaGetLastError());
     return GLP_OK;
   }));
-  const __nv_bfloat16* cur = d.pooled;
+  const __half* cur = d.pooled;
   int cur_k = H;
   for (size_t j = 0; j < d.head.size(); ++j) {
     HeadW& hw = d.head[j];
     const bool last = j + 1 == d.head.size();
     CUtensorMap m_in;
-    GLP_TRY(make_map_bf16(&m_in, cur, n_seq, cur_k, cur_k, 128));
+    GLP_TRY(make_map16(&m_in, cur, n_seq, cur_k, cur_k, 128, true));
     GemmParams ph{};
     ph.M = n_seq;
     ph.N = hw.n;
@@ -792,8 +842,8 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
     ph.status = d.status;
     GLP_TRY(prof_launch(d, st, kProfHeadGemm, gemm_flops(n_seq, hw.n, hw.k),
                         gemm_bytes(n_seq, hw.n, hw.k, last ? 4.0 : 2.0),
-                        [&] { return launch_gemm(m_in, hw.map, hw.bn, last ? glp::kEpiF32 : glp::kEpiBf16, ph, st); }));
-    cur = static_cast<const __nv_bfloat16*>(ph.C);
+                        [&] { return launch_gemm<__half>(m_in, hw.map, hw.bn, last ? glp::kEpiF32 : glp::kEpiStore16, ph, st); }));
+    cur = static_cast<const __half*>(ph.C);
     cur_k = hw.n;
   }
   GLP_TRY(prof_launch(d, st, kProfL2, 0.0, 4.0 * n_seq * (c.emb_out + out_dim), [&] {
@@ -930,8 +980,8 @@ int run_bf16_gemm(const __nv_bfloat16* w, int N, int K, const void* x, int M, vo
   if (M == 0) return GLP_OK;
   const int bn = bn_for(N);
   CUtensorMap ma, mb;
-  GLP_TRY(make_map_bf16(&ma, x, M, K, K, 128));
-  GLP_TRY(make_map_bf16(&mb, w, N, K, K, bn));
+  GLP_TRY(make_map16(&ma, x, M, K, K, 128, false));
+  GLP_TRY(make_map16(&mb, w, N, K, K, bn, false));
   GemmParams p{};
   p.M = M;
   p.N = N;
@@ -939,7 +989,7 @@ int run_bf16_gemm(const __nv_bfloat16* w, int N, int K, const void* x, int M, vo
   p.C = y;
   p.ldc = N;
   p.status = status;
-  return launch_gemm(ma, mb, bn, y_is_f32 ? glp::kEpiF32 : glp::kEpiBf16, p, st);
+  return launch_gemm<__nv_bfloat16>(ma, mb, bn, y_is_f32 ? glp::kEpiF32 : glp::kEpiStore16, p, st);
 }
 
 }  // namespace
@@ -1203,7 +1253,7 @@ int glp_q8_0_gemm(const void* d_q8_w, int N, int K, const void* d_x_bf16, int M,
     w = g_scratch.w[dev];
   }
   const int64_t nb = static_cast<int64_t>(N) * (K / 32);
-  glp::q8_0_dequant_bf16_rows_kernel<<<static_cast<unsigned>((nb + 255) / 256), 256, 0, st>>>(
+  glp::q8_0_dequant_rows_kernel<__nv_bfloat16><<<static_cast<unsigned>((nb + 255) / 256), 256, 0, st>>>(
       static_cast<const uint8_t*>(d_q8_w), N, K, w, 0, 0, 0);
   GLP_CUDA(cudaGetLastError());
   return run_bf16_gemm(w, N, K, d_x_bf16, M, d_y, y_is_f32, st);
@@ -1223,14 +1273,16 @@ int glp_flash_attention(const void* d_qkv, const int32_t* d_cu_seqlens, int n_se
   if (n_seq == 0 || max_len == 0) return GLP_OK;
   if (!d_qkv || !d_cu_seqlens || !d_out) return fail(GLP_ERR_INVALID_ARG, "null pointer");
   GLP_TRY(ensure_kernel_attrs());
-  const dim3 grid(static_cast<unsigned>((max_len + glp::kAttnBQ - 1) / glp::kAttnBQ), static_cast<unsigned>(n_q_heads),
-                  static_cast<unsigned>(n_seq));
+  int dev = 0;
+  GLP_CUDA(cudaGetDevice(&dev));
+  int* status = nullptr;
+  GLP_TRY(device_status_word(dev, &status));
   const int ld = (n_q_heads + 2 * n_kv_heads) * head_dim;
-  glp::flash_attn_fwd_kernel<<<grid, glp::kAttnThreads, glp::kAttnSmem, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __half*>(d_qkv), ld, d_cu_seqlens, 0, n_q_heads, n_kv_heads, window,
-      static_cast<__nv_bfloat16*>(d_out), n_q_heads * head_dim);
-  GLP_CUDA(cudaGetLastError());
-  return GLP_OK;
+  int total = 0;
+  GLP_CUDA(cudaMemcpy(&total, d_cu_seqlens + n_seq, sizeof(int), cudaMemcpyDeviceToHost));
+  return launch_attention(static_cast<const __half*>(d_qkv), total, ld, d_cu_seqlens, 0, n_seq, max_len, n_q_heads,
+                          n_kv_heads, window, static_cast<__half*>(d_out), status,
+                          static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

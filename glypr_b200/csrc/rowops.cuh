@@ -1,7 +1,9 @@
 // Memory-bound row kernels (one warp per token row, 128-bit vector accesses, warp-shuffle
 // reductions) and the Q8_0 dequantisation kernels.
 //
-// Residual stream h is f32 [T, H]; the GEMM inputs x are bf16 [T, H].
+// Residual stream h is f32 [T, H]; the GEMM inputs x are f16 [T, H] (every GEMM input is a
+// normalised row or a convex combination of normalised rows, so f16's range suffices and its
+// 11-bit mantissa keeps the dequantised weights and activations close to exact).
 #pragma once
 #include "common.cuh"
 
@@ -27,13 +29,13 @@ __global__ void q8_0_dequant_f32_kernel(const uint8_t* __restrict__ blocks, int6
   }
 }
 
-// Dequantise a Q8_0 matrix [N, K] into bf16 rows of a destination matrix.  Row n goes to
+// Dequantise a Q8_0 matrix [N, K] into 16-bit rows of a destination matrix.  Row n goes to
 //   dst_row = group ? (n / group) * group_stride + row_base + n % group : row_base + n
 // which builds the fused QKV weight (row_base offsets) and the gate/up interleave
 // (group = 128, group_stride = 256, row_base = 0 for gate and 128 for up).
-__global__ void q8_0_dequant_bf16_rows_kernel(const uint8_t* __restrict__ blocks, int n, int k,
-                                              __nv_bfloat16* __restrict__ dst, int row_base, int group,
-                                              int group_stride) {
+template <typename T>
+__global__ void q8_0_dequant_rows_kernel(const uint8_t* __restrict__ blocks, int n, int k, T* __restrict__ dst,
+                                         int row_base, int group, int group_stride) {
   const int nb = k / 32;
   const int64_t b = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (b >= static_cast<int64_t>(n) * nb) return;
@@ -46,25 +48,26 @@ __global__ void q8_0_dequant_bf16_rows_kernel(const uint8_t* __restrict__ blocks
   for (int q = 0; q < 4; ++q) {
     const int8_t* s = reinterpret_cast<const int8_t*>(src + 2 + 8 * q);
     uint4 u;
-    u.x = pack_bf16(s[0] * d, s[1] * d);
-    u.y = pack_bf16(s[2] * d, s[3] * d);
-    u.z = pack_bf16(s[4] * d, s[5] * d);
-    u.w = pack_bf16(s[6] * d, s[7] * d);
+    u.x = Half16<T>::pack(s[0] * d, s[1] * d);
+    u.y = Half16<T>::pack(s[2] * d, s[3] * d);
+    u.z = Half16<T>::pack(s[4] * d, s[5] * d);
+    u.w = Half16<T>::pack(s[6] * d, s[7] * d);
     out[q] = u;
   }
 }
 
-// bf16 [N, K] source (BF16 GGUF weights) copied into the same fused/interleaved layout.
-__global__ void bf16_rows_copy_kernel(const __nv_bfloat16* __restrict__ src, int n, int k,
-                                      __nv_bfloat16* __restrict__ dst, int row_base, int group,
-                                      int group_stride) {
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;  // 8-element chunks
-  const int per_row = k / 8;
+// bf16 [N, K] source (BF16 GGUF weights) converted into the same fused/interleaved layout.
+template <typename T>
+__global__ void bf16_rows_convert_kernel(const __nv_bfloat16* __restrict__ src, int n, int k, T* __restrict__ dst,
+                                         int row_base, int group, int group_stride) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;  // 2-element pairs
+  const int per_row = k / 2;
   if (i >= static_cast<int64_t>(n) * per_row) return;
   const int row = static_cast<int>(i / per_row), c = static_cast<int>(i % per_row);
   const int drow = group ? (row / group) * group_stride + row_base + row % group : row_base + row;
-  reinterpret_cast<uint4*>(dst + static_cast<size_t>(drow) * k)[c] =
-      reinterpret_cast<const uint4*>(src + static_cast<size_t>(row) * k)[c];
+  const __nv_bfloat162 v = reinterpret_cast<const __nv_bfloat162*>(src + static_cast<size_t>(row) * k)[c];
+  const float2 f = __bfloat1622float2(v);
+  reinterpret_cast<uint32_t*>(dst + static_cast<size_t>(drow) * k)[c] = Half16<T>::pack(f.x, f.y);
 }
 
 // ---------------------------------------------------------------------------- helpers
@@ -78,34 +81,34 @@ __device__ __forceinline__ void store_f32x8(float* p, const float* v) {
   reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
   reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
 }
-__device__ __forceinline__ void load_bf16x8(const __nv_bfloat16* p, float* v) {
+__device__ __forceinline__ void load_f16x8(const __half* p, float* v) {
   const uint4 u = *reinterpret_cast<const uint4*>(p);
   const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&w[i]);
-    const float2 f = __bfloat1622float2(h);
+    const __half2 h = *reinterpret_cast<const __half2*>(&w[i]);
+    const float2 f = __half22float2(h);
     v[2 * i] = f.x;
     v[2 * i + 1] = f.y;
   }
 }
-__device__ __forceinline__ void store_bf16x8(__nv_bfloat16* p, const float* v) {
+__device__ __forceinline__ void store_f16x8(__half* p, const float* v) {
   uint4 u;
-  u.x = pack_bf16(v[0], v[1]);
-  u.y = pack_bf16(v[2], v[3]);
-  u.z = pack_bf16(v[4], v[5]);
-  u.w = pack_bf16(v[6], v[7]);
+  u.x = pack_f16(v[0], v[1]);
+  u.y = pack_f16(v[2], v[3]);
+  u.z = pack_f16(v[4], v[5]);
+  u.w = pack_f16(v[6], v[7]);
   *reinterpret_cast<uint4*>(p) = u;
 }
 
 // ---------------------------------------------------------------------------- embedding
 // h[t] = dequant(E[id_t]) * f32(sqrt(H))   (model.rs:252-255, 507-508)
-// x[t] = bf16(RMSNorm(h[t]) * w)            (first layer's attn_norm, norm.rs:22-63)
+// x[t] = f16(RMSNorm(h[t]) * w)             (first layer's attn_norm, norm.rs:22-63)
 // One warp per token; lane l covers elements l, l+32, ... (coalesced byte reads of the
 // 34-byte blocks).
 __global__ void embed_gather_norm_kernel(const uint8_t* __restrict__ table, const int* __restrict__ ids,
                                          int n_tokens, float scale, const float* __restrict__ w, float eps,
-                                         float* __restrict__ h, __nv_bfloat16* __restrict__ x) {
+                                         float* __restrict__ h, __half* __restrict__ x) {
   const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (t >= n_tokens) return;
@@ -123,19 +126,19 @@ __global__ void embed_gather_norm_kernel(const uint8_t* __restrict__ table, cons
   ss = warp_sum(ss);
   const float inv = 1.0f / sqrtf(ss / static_cast<float>(kHidden) + eps);
   float* hr = h + static_cast<size_t>(t) * kHidden;
-  __nv_bfloat16* xr = x + static_cast<size_t>(t) * kHidden;
+  __half* xr = x + static_cast<size_t>(t) * kHidden;
 #pragma unroll
   for (int b = 0; b < kHidden / 32; ++b) {
     const int e = b * 32 + lane;
     hr[e] = v[b];
-    xr[e] = __float2bfloat16_rn(v[b] * inv * __ldg(w + e));
+    xr[e] = __float2half_rn(v[b] * inv * __ldg(w + e));
   }
 }
 
 // Same gather for a bf16 token table (BF16 GGUF).
 __global__ void embed_gather_norm_bf16_kernel(const __nv_bfloat16* __restrict__ table, const int* __restrict__ ids,
                                               int n_tokens, float scale, const float* __restrict__ w, float eps,
-                                              float* __restrict__ h, __nv_bfloat16* __restrict__ x) {
+                                              float* __restrict__ h, __half* __restrict__ x) {
   const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (t >= n_tokens) return;
@@ -150,36 +153,36 @@ __global__ void embed_gather_norm_bf16_kernel(const __nv_bfloat16* __restrict__ 
   ss = warp_sum(ss);
   const float inv = 1.0f / sqrtf(ss / static_cast<float>(kHidden) + eps);
   float* hr = h + static_cast<size_t>(t) * kHidden;
-  __nv_bfloat16* xr = x + static_cast<size_t>(t) * kHidden;
+  __half* xr = x + static_cast<size_t>(t) * kHidden;
 #pragma unroll
   for (int b = 0; b < kHidden / 32; ++b) {
     const int e = b * 32 + lane;
     hr[e] = v[b];
-    xr[e] = __float2bfloat16_rn(v[b] * inv * __ldg(w + e));
+    xr[e] = __float2half_rn(v[b] * inv * __ldg(w + e));
   }
 }
 
 // ---------------------------------------------------------------------------- post-norm
 // h <- (h + RMSNorm(y) * w_post) * layer_scalar            (norm.rs:65-94, layer.rs:20-50)
 // then the next pre-norm:  x = RMSNorm(h) * w_next
-//   FINAL = false: x is bf16 (the next GEMM's input)
+//   FINAL = false: x is f16 (the next GEMM's input)
 //   FINAL = true : the normalised row is written back over h in f32 (output_norm, model.rs:576)
 // One warp per row; lane owns elements [c*256 + lane*8, +8) for c = 0..2.
 template <bool FINAL>
-__global__ void post_norm_residual_kernel(const __nv_bfloat16* __restrict__ y, float* __restrict__ h,
+__global__ void post_norm_residual_kernel(const __half* __restrict__ y, float* __restrict__ h,
                                           const float* __restrict__ w_post, float layer_scalar,
                                           const float* __restrict__ w_next, float eps, int n_tokens,
-                                          __nv_bfloat16* __restrict__ x) {
+                                          __half* __restrict__ x) {
   const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (t >= n_tokens) return;
-  const __nv_bfloat16* yr = y + static_cast<size_t>(t) * kHidden;
+  const __half* yr = y + static_cast<size_t>(t) * kHidden;
   float* hr = h + static_cast<size_t>(t) * kHidden;
   float yv[kVecPerLane][8], hv[kVecPerLane][8];
   float ss = 0.f;
 #pragma unroll
   for (int c = 0; c < kVecPerLane; ++c) {
-    load_bf16x8(yr + c * 256 + lane * 8, yv[c]);
+    load_f16x8(yr + c * 256 + lane * 8, yv[c]);
 #pragma unroll
     for (int j = 0; j < 8; ++j) ss = fmaf(yv[c][j], yv[c][j], ss);
   }
@@ -211,7 +214,7 @@ __global__ void post_norm_residual_kernel(const __nv_bfloat16* __restrict__ y, f
       store_f32x8(hr + e0, o);
     } else {
       store_f32x8(hr + e0, hv[c]);
-      store_bf16x8(x + static_cast<size_t>(t) * kHidden + e0, o);
+      store_f16x8(x + static_cast<size_t>(t) * kHidden + e0, o);
     }
   }
 }
@@ -230,7 +233,7 @@ __global__ void positions_kernel(const int* __restrict__ cu_seqlens, int cu_base
 // pooled[b] = sum_{t in seq b} xf[t] / max(len_b, 1e-9)   (model.rs:671-680), f32, fixed
 // summation order (deterministic).  Block per sequence, 192 threads x 4 columns.
 __global__ void mean_pool_kernel(const float* __restrict__ xf, const int* __restrict__ cu_seqlens, int cu_base,
-                                 int n_seq, __nv_bfloat16* __restrict__ pooled_bf16,
+                                 int n_seq, __half* __restrict__ pooled16,
                                  float* __restrict__ pooled_f32) {
   const int b = blockIdx.x;
   if (b >= n_seq) return;
@@ -251,11 +254,10 @@ __global__ void mean_pool_kernel(const float* __restrict__ xf, const int* __rest
   acc.z /= cnt;
   acc.w /= cnt;
   if (pooled_f32) *reinterpret_cast<float4*>(pooled_f32 + static_cast<size_t>(b) * kHidden + c) = acc;
-  __nv_bfloat16* pb = pooled_bf16 + static_cast<size_t>(b) * kHidden + c;
-  pb[0] = __float2bfloat16_rn(acc.x);
-  pb[1] = __float2bfloat16_rn(acc.y);
-  pb[2] = __float2bfloat16_rn(acc.z);
-  pb[3] = __float2bfloat16_rn(acc.w);
+  uint2 pk;
+  pk.x = pack_f16(acc.x, acc.y);
+  pk.y = pack_f16(acc.z, acc.w);
+  *reinterpret_cast<uint2*>(pooled16 + static_cast<size_t>(b) * kHidden + c) = pk;
 }
 
 // L2-normalise (clamp 1e-12) then MRL: the first out_dim values renormalised

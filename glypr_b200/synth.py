@@ -184,6 +184,11 @@ def _kv(key: str, vtype: int, value) -> bytes:
     return out
 
 
+def _kv_key(kv: bytes) -> str:
+    (n,) = struct.unpack_from("<Q", kv, 0)
+    return kv[8:8 + n].decode()
+
+
 def _tensor_order(cfg: EncoderConfig) -> List[Tuple[str, Tuple[int, ...], str]]:
     """(name, shape [rows, cols] or [n], kind) in the fixed sub-stream order."""
     h, f, d = cfg.hidden, cfg.ffn, cfg.head_dim
@@ -278,18 +283,32 @@ def _nbytes(shape, ggml_type) -> int:
     raise ValueError(ggml_type)
 
 
-def write_gguf(path: str, cfg: EncoderConfig = BASELINE, seed: int = MASTER_SEED) -> str:
-    """Write the synthetic encoder to ``path`` (returns ``path``)."""
-    order = _tensor_order(cfg)
+def write_gguf(path: str, cfg: EncoderConfig = BASELINE, seed: int = MASTER_SEED,
+               drop: Iterable[str] = (), extra_f32: Sequence[Tuple[str, Tuple[int, ...]]] = (),
+               f32_mats: Iterable[str] = ()) -> str:
+    """Write the synthetic encoder to ``path`` (returns ``path``).
+
+    ``drop`` omits metadata keys or tensors by name, ``extra_f32`` appends zero F32 tensors
+    and ``f32_mats`` stores the named matrices as F32 instead of Q8_0/BF16 -- used by the
+    host-side fault-injection tests to build malformed files."""
+    drop = set(drop)
+    f32_mats = set(f32_mats)
+    order = [o for o in _tensor_order(cfg) if o[0] not in drop]
+    order_idx = {n: i for i, (n, _, _) in enumerate(_tensor_order(cfg))}
     mat_type = GGML_Q8_0 if cfg.weight_type == "q8_0" else GGML_BF16
     infos = []
     offset = 0
     for name, shape, kind in order:
-        t = GGML_F32 if kind in ("gain", "qkgain") else mat_type
+        t = GGML_F32 if kind in ("gain", "qkgain") or name in f32_mats else mat_type
         infos.append((name, shape, t, offset))
         offset += _nbytes(shape, t)
         offset = (offset + ALIGNMENT - 1) // ALIGNMENT * ALIGNMENT
-    kvs = metadata(cfg)
+    for name, shape in extra_f32:
+        infos.append((name, shape, GGML_F32, offset))
+        order.append((name, shape, "zero"))
+        offset += _nbytes(shape, GGML_F32)
+        offset = (offset + ALIGNMENT - 1) // ALIGNMENT * ALIGNMENT
+    kvs = [kv for kv in metadata(cfg) if _kv_key(kv) not in drop]
     header = struct.pack("<IIQQ", GGUF_MAGIC, GGUF_VERSION, len(infos), len(kvs)) + b"".join(kvs)
     tinfo = b""
     for name, shape, t, off in infos:
@@ -302,12 +321,19 @@ def write_gguf(path: str, cfg: EncoderConfig = BASELINE, seed: int = MASTER_SEED
     with open(tmp, "wb") as fh:
         fh.write(head + b"\0" * pad)
         pos = 0
-        for idx, ((name, shape, kind), (_, _, t, off)) in enumerate(zip(order, infos)):
+        for (name, shape, kind), (_, _, t, off) in zip(order, infos):
             if pos < off:
                 fh.write(b"\0" * (off - pos))
                 pos = off
-            gt, raw, _ = generate_tensor(cfg, seed, idx, shape, kind)
-            assert gt == t and len(raw) == _nbytes(shape, t), name
+            if kind == "zero":
+                raw = np.zeros(shape, dtype=np.float32).tobytes()
+            elif name in f32_mats:
+                rng = _rng(seed, order_idx[name])
+                raw = (rng.standard_normal(shape, dtype=np.float32) * np.float32(cfg.weight_std)).tobytes()
+            else:
+                gt, raw, _ = generate_tensor(cfg, seed, order_idx[name], shape, kind)
+                assert gt == t, name
+            assert len(raw) == _nbytes(shape, t), name
             fh.write(raw)
             pos += len(raw)
     os.replace(tmp, path)

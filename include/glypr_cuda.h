@@ -139,7 +139,7 @@ int glp_bf16_gemm(const void* d_w_bf16, int N, int K, const void* d_x_bf16, int 
 
 /* Flash attention over packed qkv (f16 [T, (Hq + 2 Hkv) * 256], per-head normed + RoPE'd)
  * for n_seq sequences at d_cu_seqlens; window > 0 applies |i - j| <= window.  Writes
- * d_out bf16 [T, Hq * 256].  The AttentionBackend::compute_attention seam
+ * d_out f16 [T, Hq * 256].  The AttentionBackend::compute_attention seam
  * (attention/traits.rs:37-46, AttentionMode::CudaFlash at attention/mod.rs:255-262). */
 int glp_flash_attention(const void* d_qkv, const int32_t* d_cu_seqlens, int n_seq, int max_len, int n_q_heads,
                         int n_kv_heads, int head_dim, int window, void* d_out, void* stream);

@@ -132,7 +132,7 @@ def _attn_case(lengths, n_heads, n_kv, window, seed, logit_scale=1.0):
     cu = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int32)
     d_qkv = _dev(qkv16)
     d_cu = _dev(cu)
-    out = torch.zeros((max(t, 1), n_heads * d), dtype=torch.bfloat16, device="cuda")
+    out = torch.zeros((max(t, 1), n_heads * d), dtype=torch.float16, device="cuda")
     api.flash_attention(d_qkv.data_ptr(), d_cu.data_ptr(), len(lengths), int(max(lengths)), n_heads, n_kv, d,
                         window, out.data_ptr())
     torch.cuda.synchronize()

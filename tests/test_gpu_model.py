@@ -47,13 +47,31 @@ def _check(got, want, cos_gate=COS_GATE, abs_gate=ABS_GATE):
     return cos, err
 
 
+def _check_both(got, orc, ids, lens, out_dim=None):
+    """Gate against the exact-dequant oracle (M2) for every sequence, and against the
+    candle-faithful reference path (M1) for sequences of >= 16 tokens.  M1 quantises every
+    activation row to int8 blocks; for a very short sequence that noise is not averaged by
+    the mean-pool and M1 itself sits ~1.6e-4 (cosine) from the exact result (single-token
+    golden case), so there the M1 check allows the M1-vs-exact gap."""
+    m1 = orc.embed(ids, lens, oracle.M1_CANDLE, out_dim=out_dim)
+    m2 = orc.embed(ids, lens, oracle.M2_EXACT, out_dim=out_dim)
+    # MRL renormalises the first out_dim values: element magnitudes (and absolute errors)
+    # grow by ~sqrt(E / out_dim), so the 768-d absolute gate scales with it
+    abs_gate = ABS_GATE * np.sqrt(got.shape[1] and 768.0 / got.shape[1])
+    _check(got, m2, abs_gate=abs_gate)
+    long_ = np.asarray(lens) >= 16
+    if long_.any():
+        _check(got[long_], m1[long_], abs_gate=abs_gate)
+    gap = 1.0 - cosine_rows(m1, m2)
+    cos1 = cosine_rows(got, m1)
+    assert (cos1 >= np.minimum(COS_GATE, 1.0 - 2.0 * gap - 2e-5)).all(), (cos1, gap)
+    return m1, m2
+
+
 def test_small_parity_ragged(small_emb, small_oracle):
     ids, lens = synth.make_batch(6, 700, small_oracle.vocab, lengths=[700, 513, 512, 64, 1, 300])
     got = small_emb.embed_tokens(ids, lens)
-    want = small_oracle.embed(ids, lens, oracle.M1_CANDLE)
-    _check(got, want)
-    exact = small_oracle.embed(ids, lens, oracle.M2_EXACT)
-    _check(got, exact)
+    _check_both(got, small_oracle, ids, lens)
     np.testing.assert_allclose(np.linalg.norm(got, axis=1), 1.0, atol=1e-5)
 
 
@@ -63,8 +81,7 @@ def test_small_parity_mrl(small_emb, small_oracle):
     full = small_emb.embed_tokens(ids, lens)
     # MRL on the device == truncate + renormalise of the 768-d output (model.rs:691-698)
     np.testing.assert_allclose(got256, np.stack([api.truncate_mrl(f, 256) for f in full]), atol=2e-6)
-    want = small_oracle.embed(ids, lens, oracle.M1_CANDLE, out_dim=256)
-    _check(got256, want)
+    _check_both(got256, small_oracle, ids, lens, out_dim=256)
 
 
 def test_deterministic_and_batch_invariant(small_emb, small_oracle):
@@ -122,13 +139,12 @@ def test_deep_parity(deep_cond_gguf):
     with GlyprEmbedder.load_gguf(deep_cond_gguf, [0]) as emb:
         ids, lens = synth.make_batch(4, 1024, orc.vocab, lengths=[512, 1024, 77, 300])
         got = emb.embed_tokens(ids, lens)
-    want = orc.embed(ids, lens, oracle.M1_CANDLE)
-    _check(got, want)
+    _check_both(got, orc, ids, lens)
 
 
 def test_chaotic_baseline_init_properties(deep_gguf):
-    """BASELINE init: outputs are unit vectors, deterministic, batch-invariant, and the
-    first layer tracks the oracle closely (the divergence is the model's, not the path's)."""
+    """BASELINE init, 24 layers: outputs are finite unit vectors, deterministic and
+    batch-invariant (the end-to-end value is chaotic in any rounding, see module doc)."""
     orc = oracle.OracleModel(deep_gguf)
     with GlyprEmbedder.load_gguf(deep_gguf, [0]) as emb:
         ids, lens = synth.make_batch(3, 512, orc.vocab, lengths=[512, 200, 31])
@@ -137,3 +153,20 @@ def test_chaotic_baseline_init_properties(deep_gguf):
     np.testing.assert_allclose(np.linalg.norm(a, axis=1), 1.0, atol=1e-5)
     np.testing.assert_array_equal(a[1], b[0])
     assert np.isfinite(a).all()
+
+
+def test_baseline_init_one_layer(gguf_dir):
+    """BASELINE init, one layer: the GPU path stays as close to the exact result as the
+    reference's own candle-faithful path does (the amplification starts in layer 1)."""
+    import os
+    path = synth.ensure_gguf(os.path.join(str(gguf_dir), "one_layer.gguf"), synth.EncoderConfig(n_layers=1, vocab=4096))
+    orc = oracle.OracleModel(path)
+    ids, lens = synth.make_batch(4, 512, orc.vocab, lengths=[512, 300, 100, 40])
+    with GlyprEmbedder.load_gguf(path, [0]) as emb:
+        got = emb.embed_tokens(ids, lens)
+    m1 = orc.embed(ids, lens, oracle.M1_CANDLE)
+    m2 = orc.embed(ids, lens, oracle.M2_EXACT)
+    gpu_gap = 1.0 - cosine_rows(got, m2)
+    ref_gap = 1.0 - cosine_rows(m1, m2)
+    print("1-layer BASELINE init: 1-cos(gpu, exact) =", gpu_gap, " 1-cos(M1, exact) =", ref_gap)
+    assert (gpu_gap <= np.maximum(2.0 * ref_gap, 1e-4)).all()

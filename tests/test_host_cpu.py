@@ -1,0 +1,124 @@
+"""Host-side checks of libglypr_cuda.so that need no GPU: the library loads, exports every
+function include/glypr_cuda.h declares, and rejects malformed GGUF files (host-side fault
+injection: corrupt, truncated, missing keys/tensors, unsupported layouts) before it touches a
+device -- the reference's anyhow errors from config.rs:79-95 / model.rs:251-473."""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+from glypr_b200 import api, synth
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "glypr_cuda.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(glp_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = api.load_library()
+    names = declared_functions()
+    assert len(names) >= 13
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, missing
+    assert set(names) == set(api.EXPORTED_SYMBOLS)
+    assert lib.glp_last_error() is not None
+
+
+def _open(path):
+    L = api.load_library()
+    out = ctypes.c_void_p()
+    rc = L.glp_open(path.encode(), None, 0, None, ctypes.byref(out))
+    msg = L.glp_last_error().decode()
+    if rc == api.GLP_OK:
+        L.glp_close(out)
+    return rc, msg
+
+
+@pytest.fixture(scope="module")
+def tiny_cfg():
+    return synth.small_config(n_layers=1, vocab=256)
+
+
+def test_open_missing_file(tmp_path):
+    rc, msg = _open(str(tmp_path / "nope.gguf"))
+    assert rc == api.GLP_ERR_IO and "cannot open" in msg
+
+
+def test_open_not_gguf(tmp_path):
+    p = tmp_path / "junk.gguf"
+    p.write_bytes(os.urandom(4096))
+    rc, msg = _open(str(p))
+    assert rc == api.GLP_ERR_FORMAT and "magic" in msg
+
+
+@pytest.mark.parametrize("keep", [40, 300, 0.5])
+def test_open_truncated(tmp_path, tiny_cfg, keep):
+    full = synth.write_gguf(str(tmp_path / "full.gguf"), tiny_cfg)
+    data = open(full, "rb").read()
+    n = int(len(data) * keep) if isinstance(keep, float) else keep
+    p = tmp_path / "cut.gguf"
+    p.write_bytes(data[:n])
+    rc, msg = _open(str(p))
+    assert rc == api.GLP_ERR_FORMAT, msg
+    assert "truncated" in msg or "out of file bounds" in msg or "too small" in msg
+
+
+def test_open_missing_metadata(tmp_path, tiny_cfg):
+    p = synth.write_gguf(str(tmp_path / "m.gguf"), tiny_cfg, drop={"gemma-embedding2.block_count"})
+    rc, msg = _open(p)
+    assert rc == api.GLP_ERR_FORMAT and msg == "Missing gemma-embedding2.block_count"
+
+
+def test_open_missing_tensor(tmp_path, tiny_cfg):
+    p = synth.write_gguf(str(tmp_path / "t.gguf"), tiny_cfg, drop={"blk.0.ffn_up.weight"})
+    rc, msg = _open(p)
+    assert rc == api.GLP_ERR_FORMAT and "blk.0.ffn_up.weight" in msg
+
+
+def test_open_rejects_ple(tmp_path, tiny_cfg):
+    p = synth.write_gguf(str(tmp_path / "ple.gguf"), tiny_cfg, extra_f32=[("blk.0.proj.weight", (768, 256))])
+    rc, msg = _open(p)
+    assert rc == api.GLP_ERR_UNSUPPORTED and "PLE" in msg
+
+
+def test_open_rejects_f32_linear(tmp_path, tiny_cfg):
+    p = synth.write_gguf(str(tmp_path / "f32.gguf"), tiny_cfg, f32_mats={"blk.0.attn_k.weight"})
+    rc, msg = _open(p)
+    assert rc == api.GLP_ERR_UNSUPPORTED and "attn_k" in msg
+
+
+def test_open_rejects_other_hidden(tmp_path):
+    cfg = synth.small_config(n_layers=1, vocab=256, hidden=512, head_dims=(512,))
+    p = synth.write_gguf(str(tmp_path / "h512.gguf"), cfg)
+    rc, msg = _open(p)
+    assert rc == api.GLP_ERR_UNSUPPORTED and "768" in msg
+
+
+def test_open_rejects_head_dim_override(tmp_path):
+    cfg = synth.small_config(n_layers=6, vocab=256)
+    p = synth.write_gguf(str(tmp_path / "hd.gguf"), cfg, drop={"gemma-embedding2.attention.key_length"})
+    # key_length defaults to 512 for the global layer (config.rs:143-144): not supported here
+    rc, msg = _open(p)
+    assert rc == api.GLP_ERR_UNSUPPORTED and "head_dim" in msg
+
+
+def test_util_mirrors():
+    v = api.l2_normalize(np.zeros(4, np.float32))
+    np.testing.assert_array_equal(v, 0)  # util.rs:24-25 returns the zero vector unchanged
+    assert api.cosine_similarity(np.zeros(3), np.ones(3)) == 0.0
+    assert abs(api.cosine_similarity([1, 0], [0, 1])) < 1e-7
+
+
+def test_make_batch_padding():
+    ids, lens = synth.make_batch(5, 40, 1000, len_range=(3, 40))
+    assert ids.shape == (5, 40) and lens.min() >= 3 and lens.max() <= 40
+    for i, L in enumerate(lens):
+        assert (ids[i, L:] == 0).all() and (ids[i, :L] >= 2).all() and (ids[i, :L] < 1000).all()
