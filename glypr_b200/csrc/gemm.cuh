@@ -4,8 +4,10 @@
 //   B  weights (dequantised Q8_0 / converted BF16) as T, row-major [N,K] -> TMA, 128B swizzle
 //   accumulator f32 in tensor memory (TMEM), two buffers of BN columns
 //
-// Roles (192 threads): warp 0 = TMA producer, warp 1 = MMA issuer (+ TMEM owner),
-// warps 2..5 = epilogue (warp w reads TMEM lanes 32*(w%4)..+31, one output row per thread).
+// Roles (320 threads): warp 0 = TMA producer, warp 1 = MMA issuer (+ TMEM owner),
+// warps 2..9 = epilogue: warp w reads TMEM lanes 32*(w%4)..+31 (one output row per thread)
+// and converts half of the tile's columns ((w-2)/4 selects the half), so every lane
+// quadrant has two warps converting while the next tile accumulates.
 // Tiles are 128 x BN, K is consumed 64 elements (one 128-byte swizzle row) per stage.
 // Tile order is M-major over N so consecutive CTAs share the same A rows (read from HBM
 // once, then from L2) while the weights stay L2-resident.
@@ -49,7 +51,9 @@ struct GemmCfg {
   static constexpr uint32_t A_BYTES = BM * BK * 2;
   static constexpr uint32_t B_BYTES = BN * BK * 2;
   static constexpr uint32_t TMEM_COLS = 2 * BN;  // double-buffered accumulator
-  static constexpr size_t SMEM = 1024 + STAGES * (A_BYTES + B_BYTES) + 256;
+  // after the stages: 512 B of barriers/flags, then the epilogue pairs' row-sum exchange
+  static constexpr uint32_t RED_OFFSET = 512;
+  static constexpr size_t SMEM = 1024 + STAGES * (A_BYTES + B_BYTES) + RED_OFFSET + 2 * 2 * 128 * 4;
 };
 
 template <typename T>
@@ -66,68 +70,129 @@ __device__ __forceinline__ void store16x32(T* dst, const float* v) {
   }
 }
 
-// gelu_tanh(g) * u with the reference's clamp (cpu_simd/geglu.rs:6-18).  Uses the identity
-// 0.5 * (1 + tanh(z)) = 1 / (1 + exp(-2 z)).
+// gelu_tanh(g) * u with the reference's clamp (cpu_simd/geglu.rs:6-18), branch-free so the
+// 32 elements of a chunk interleave.  Uses the identity 0.5 * (1 + tanh(z)) = 1 / (1 + e^-2z);
+// for g <= -10 the exponential may overflow to inf, giving -0 before the clamp selects 0.
 __device__ __forceinline__ float geglu_f(float g, float u) {
-  if (g <= -10.0f) return 0.0f;
-  if (g >= 10.0f) return g * u;
-  const float z = 0.7978846f * (g + 0.044715f * g * g * g);
-  return __fdividef(g, 1.0f + __expf(-2.0f * z)) * u;
+  const float z = 0.7978846f * fmaf(0.044715f * g, g * g, g);
+  float a = __fdividef(g, 1.0f + __expf(-2.0f * z)) * u;
+  a = g >= 10.0f ? g * u : a;
+  return g <= -10.0f ? 0.0f : a;
 }
 
+template <int EPI, typename T>
+__device__ __forceinline__ void epi_store_chunk(const GemmParams& p, int row, int col, const uint32_t (&r)[32]) {
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = u2f(r[j]);
+  const size_t off = static_cast<size_t>(row) * p.ldc + col;
+  if constexpr (EPI == kEpiStore16) {
+    store16x32<T>(reinterpret_cast<T*>(p.C) + off, v);
+  } else {
+    float4* d = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.C) + off);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) d[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void epi_geglu_chunk(const GemmParams& p, int row, int col, const uint32_t (&g)[16],
+                                                const uint32_t (&u)[16]) {
+  float v[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) v[j] = geglu_f(u2f(g[j]), u2f(u[j]));
+  uint4* d = reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.C) + static_cast<size_t>(row) * p.ldc + col);
+  d[0] = make_uint4(Half16<T>::pack(v[0], v[1]), Half16<T>::pack(v[2], v[3]), Half16<T>::pack(v[4], v[5]),
+                    Half16<T>::pack(v[6], v[7]));
+  d[1] = make_uint4(Half16<T>::pack(v[8], v[9]), Half16<T>::pack(v[10], v[11]), Half16<T>::pack(v[12], v[13]),
+                    Half16<T>::pack(v[14], v[15]));
+}
+
+// 16 frequency pairs (i, i + 128) of one head row: RMS scale, gain, NeoX RoPE, f16 store.
+__device__ __forceinline__ void epi_qkv_chunk(__half* out, int c, float inv, const float* gain, bool rope,
+                                              const uint32_t (&lo)[16], const uint32_t (&hi)[16],
+                                              const float (&cv)[16], const float (&sv)[16]) {
+  uint32_t plo[8], phi[8];
+#pragma unroll
+  for (int j = 0; j < 16; j += 2) {
+    float a[2], b[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int i = c * 16 + j + e;
+      float x1 = u2f(lo[j + e]) * inv;
+      float x2 = u2f(hi[j + e]) * inv;
+      if (gain) {
+        x1 *= __ldg(gain + i);
+        x2 *= __ldg(gain + i + 128);
+      }
+      if (rope) {  // x*cos + rotate_half(x)*sin, rotate_half = cat(-x2, x1)
+        a[e] = x1 * cv[j + e] + (-x2) * sv[j + e];
+        b[e] = x2 * cv[j + e] + x1 * sv[j + e];
+      } else {
+        a[e] = x1;
+        b[e] = x2;
+      }
+    }
+    plo[j / 2] = pack_f16(a[0], a[1]);
+    phi[j / 2] = pack_f16(b[0], b[1]);
+  }
+  uint4* dlo = reinterpret_cast<uint4*>(out + c * 16);
+  uint4* dhi = reinterpret_cast<uint4*>(out + 128 + c * 16);
+  dlo[0] = make_uint4(plo[0], plo[1], plo[2], plo[3]);
+  dlo[1] = make_uint4(plo[4], plo[5], plo[6], plo[7]);
+  dhi[0] = make_uint4(phi[0], phi[1], phi[2], phi[3]);
+  dhi[1] = make_uint4(phi[4], phi[5], phi[6], phi[7]);
+}
+
+// One accumulator tile -> global, by the two epilogue warps of one TMEM lane quadrant: `half`
+// selects which half of the tile's columns this warp converts.  Tensor-memory reads are
+// software-pipelined (the next chunk's tcgen05.ld is in flight while the current chunk is
+// converted and stored).  `red` is the pair's shared-memory exchange for the QKV row sums,
+// synchronised through the pair's rendezvous barrier `xbar` (phase bit `xph`).  Returns false
+// if that rendezvous timed out.
 template <int BN, int EPI, typename T>
-__device__ __forceinline__ void gemm_epilogue_tile(const GemmParams& p, uint32_t tacc, int m_blk, int n_blk,
-                                                   int row_in_tile) {
+__device__ __forceinline__ bool gemm_epilogue_tile(const GemmParams& p, uint32_t tacc, int m_blk, int n_blk,
+                                                   int row_in_tile, int half, float* red, uint64_t* xbar,
+                                                   uint32_t& xph, volatile int* abort_flag) {
   const int row = m_blk * 128 + row_in_tile;
   const bool live = row < p.M;
-  uint32_t r[32];
   if constexpr (EPI == kEpiStore16 || EPI == kEpiF32) {
+    constexpr int NCH = BN / 64;  // 32-column chunks per half (4 or 2)
+    const int c0 = half * NCH;
+    uint32_t ra[32], rb[32];
+    tmem_ld32(tacc + c0 * 32, ra);
+    tmem_ld_wait_tied(ra);
 #pragma unroll 1
-    for (int c = 0; c < BN / 32; ++c) {
-      tmem_ld32(tacc + c * 32, r);
-      tmem_ld_wait();
-      float v[32];
-#pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = u2f(r[j]);
-      if (live) {
-        const size_t off = static_cast<size_t>(row) * p.ldc + static_cast<size_t>(n_blk) * BN + c * 32;
-        if constexpr (EPI == kEpiStore16) {
-          store16x32<T>(reinterpret_cast<T*>(p.C) + off, v);
-        } else {
-          float4* d = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.C) + off);
-#pragma unroll
-          for (int q = 0; q < 8; ++q) d[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-        }
-      }
+    for (int c = c0; c < c0 + NCH; c += 2) {
+      tmem_ld32(tacc + (c + 1) * 32, rb);
+      if (live) epi_store_chunk<EPI, T>(p, row, n_blk * BN + c * 32, ra);
+      tmem_ld_wait_tied(rb);
+      if (c + 2 < c0 + NCH) tmem_ld32(tacc + (c + 2) * 32, ra);
+      if (live) epi_store_chunk<EPI, T>(p, row, n_blk * BN + (c + 1) * 32, rb);
+      if (c + 2 < c0 + NCH) tmem_ld_wait_tied(ra);
     }
   } else if constexpr (EPI == kEpiGeglu) {
     static_assert(BN == 256, "GeGLU tiles pair 128 gate with 128 up columns");
+    const int c0 = half * 4;  // 16-column output chunks [c0, c0 + 4)
+    uint32_t ga[16], ua[16], gb[16], ub[16];
+    tmem_ld16(tacc + c0 * 16, ga);
+    tmem_ld16(tacc + 128 + c0 * 16, ua);
+    tmem_ld_wait_tied16(ga, ua);
 #pragma unroll 1
-    for (int c = 0; c < 4; ++c) {
-      uint32_t u[32];
-      tmem_ld32(tacc + c * 32, r);
-      tmem_ld32(tacc + 128 + c * 32, u);
-      tmem_ld_wait();
-      float v[32];
-#pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = geglu_f(u2f(r[j]), u2f(u[j]));
-      if (live) {
-        const size_t off = static_cast<size_t>(row) * p.ldc + static_cast<size_t>(n_blk) * 128 + c * 32;
-        store16x32<T>(reinterpret_cast<T*>(p.C) + off, v);
+    for (int c = c0; c < c0 + 4; c += 2) {
+      tmem_ld16(tacc + (c + 1) * 16, gb);
+      tmem_ld16(tacc + 128 + (c + 1) * 16, ub);
+      if (live) epi_geglu_chunk<T>(p, row, n_blk * 128 + c * 16, ga, ua);
+      tmem_ld_wait_tied16(gb, ub);
+      if (c + 2 < c0 + 4) {
+        tmem_ld16(tacc + (c + 2) * 16, ga);
+        tmem_ld16(tacc + 128 + (c + 2) * 16, ua);
       }
+      if (live) epi_geglu_chunk<T>(p, row, n_blk * 128 + (c + 1) * 16, gb, ub);
+      if (c + 2 < c0 + 4) tmem_ld_wait_tied16(ga, ua);
     }
-  } else {  // kEpiQkv
+  } else {  // kEpiQkv: this warp owns frequency pairs (i, i + 128), i in [64 half, 64 half + 64)
     static_assert(BN == 256, "QKV tiles are one 256-wide head");
-    // pass 1: sum of squares over the head (cpu_simd/rmsnorm.rs:13-21)
-    float ss = 0.f;
-#pragma unroll 1
-    for (int c = 0; c < 8; ++c) {
-      tmem_ld32(tacc + c * 32, r);
-      tmem_ld_wait();
-#pragma unroll
-      for (int j = 0; j < 32; ++j) ss = fmaf(u2f(r[j]), u2f(r[j]), ss);
-    }
-    const float inv = 1.0f / sqrtf(ss / 256.0f + p.eps);
     const bool is_q = n_blk < p.n_q_heads;
     const bool is_k = !is_q && n_blk < p.n_q_heads + p.n_kv_heads;
     const float* gain = is_q ? p.q_gain : (is_k ? p.k_gain : nullptr);
@@ -137,49 +202,65 @@ __device__ __forceinline__ void gemm_epilogue_tile(const GemmParams& p, uint32_t
     const float* cs = p.rope_cos + pos;
     const float* sn = p.rope_sin + pos;
     const size_t fstride = static_cast<size_t>(p.rope_stride);
+    const int c0 = half * 4;  // 16-frequency chunks [c0, c0 + 4)
+    float cva[16], sva[16], cvb[16], svb[16];
+    auto load_tab = [&](int c, float (&cv)[16], float (&sv)[16]) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        cv[j] = __ldg(cs + static_cast<size_t>(c * 16 + j) * fstride);
+        sv[j] = __ldg(sn + static_cast<size_t>(c * 16 + j) * fstride);
+      }
+    };
+    if (rope) load_tab(c0, cva, sva);  // in flight during pass 1
+    // pass 1: this warp's half of the head's sum of squares (cpu_simd/rmsnorm.rs:13-21)
+    float ss = 0.f;
+    {
+      uint32_t ra[32], rb[32];
+      tmem_ld32(tacc + half * 64, ra);
+      tmem_ld32(tacc + half * 64 + 32, rb);
+      tmem_ld_wait_tied(ra);
+      tmem_ld_wait_tied(rb);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) ss = fmaf(u2f(ra[j]), u2f(ra[j]), ss);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) ss = fmaf(u2f(rb[j]), u2f(rb[j]), ss);
+      tmem_ld32(tacc + 128 + half * 64, ra);
+      tmem_ld32(tacc + 128 + half * 64 + 32, rb);
+      tmem_ld_wait_tied(ra);
+      tmem_ld_wait_tied(rb);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) ss = fmaf(u2f(ra[j]), u2f(ra[j]), ss);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) ss = fmaf(u2f(rb[j]), u2f(rb[j]), ss);
+    }
+    red[half * 128 + row_in_tile] = ss;
+    if (!pair_rendezvous(xbar, xph, abort_flag)) return false;
+    ss += red[(half ^ 1) * 128 + row_in_tile];
+    const float inv = 1.0f / sqrtf(ss / 256.0f + p.eps);
     __half* out = reinterpret_cast<__half*>(p.C) + static_cast<size_t>(row) * p.ldc + static_cast<size_t>(n_blk) * 256;
+    // pass 2: 4 chunks of 16 frequency pairs; the next chunk's table values are in flight
 #pragma unroll 1
-    for (int c = 0; c < 4; ++c) {
-      uint32_t h[32];
-      float cv[32], sv[32];
-      if (rope) {  // issue the table loads before waiting on tensor memory
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          cv[j] = __ldg(cs + static_cast<size_t>(c * 32 + j) * fstride);
-          sv[j] = __ldg(sn + static_cast<size_t>(c * 32 + j) * fstride);
-        }
-      }
-      tmem_ld32(tacc + c * 32, r);        // x[i],       i = 32c + j
-      tmem_ld32(tacc + 128 + c * 32, h);  // x[i + 128]
-      tmem_ld_wait();
-      float lo[32], hi[32];
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const int i = c * 32 + j;
-        float x1 = u2f(r[j]) * inv;
-        float x2 = u2f(h[j]) * inv;
-        if (gain) {
-          x1 *= __ldg(gain + i);
-          x2 *= __ldg(gain + i + 128);
-        }
-        if (rope) {
-          lo[j] = x1 * cv[j] + (-x2) * sv[j];  // x*cos + rotate_half(x)*sin, rotate_half = cat(-x2, x1)
-          hi[j] = x2 * cv[j] + x1 * sv[j];
-        } else {
-          lo[j] = x1;
-          hi[j] = x2;
-        }
-      }
-      if (live) {
-        store16x32<__half>(out + c * 32, lo);
-        store16x32<__half>(out + 128 + c * 32, hi);
-      }
+    for (int c = c0; c < c0 + 4; c += 2) {
+      uint32_t lo[16], hi[16];
+      if (rope) load_tab(c + 1, cvb, svb);
+      tmem_ld16(tacc + c * 16, lo);
+      tmem_ld16(tacc + 128 + c * 16, hi);
+      tmem_ld_wait_tied16(lo, hi);
+      if (live) epi_qkv_chunk(out, c, inv, gain, rope, lo, hi, cva, sva);
+      if (rope && c + 2 < c0 + 4) load_tab(c + 2, cva, sva);
+      tmem_ld16(tacc + (c + 1) * 16, lo);
+      tmem_ld16(tacc + 128 + (c + 1) * 16, hi);
+      tmem_ld_wait_tied16(lo, hi);
+      if (live) epi_qkv_chunk(out, c + 1, inv, gain, rope, lo, hi, cvb, svb);
     }
   }
+  return true;
 }
 
+constexpr int kGemmThreads = 320;
+
 template <int BN, int EPI, typename T>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const GemmParams p) {
   using Cfg = GemmCfg<BN>;
@@ -193,8 +274,11 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* xbar = drain + 1;  // [4] per-quadrant rendezvous of the two epilogue warps
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xbar + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  // [2 accumulator buffers][2 halves][128 rows]
+  float* red = reinterpret_cast<float*>(sB + STAGES * Cfg::B_BYTES + Cfg::RED_OFFSET);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -207,9 +291,10 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 4);
+      mbar_init(&tempty[b], 8);
     }
     mbar_init(drain, 1);
+    for (int q = 0; q < 4; ++q) mbar_init(&xbar[q], 2);
     *abort_flag = 0;
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
@@ -301,7 +386,9 @@ __global__ void __launch_bounds__(192, 1)
   } else {
     // -------------------------------------------------------------- epilogue warps
     const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int row_in_tile = quad * 32 + lane;
+    uint32_t xph = 0;
     int ab = 0;
     uint32_t aph = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -317,7 +404,14 @@ __global__ void __launch_bounds__(192, 1)
       }
       tc_fence_after();
       const uint32_t tacc = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(ab * BN);
-      gemm_epilogue_tile<BN, EPI, T>(p, tacc, m_blk, n_blk, row_in_tile);
+      if (!gemm_epilogue_tile<BN, EPI, T>(p, tacc, m_blk, n_blk, row_in_tile, half, red + ab * 256, &xbar[quad],
+                                           xph, abort_flag)) {
+        if (lane == 0) {
+          record_error(p.status, kErrTimeoutEpilogue);
+          *abort_flag = 1;
+        }
+        break;
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[ab]);

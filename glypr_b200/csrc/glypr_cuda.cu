@@ -93,6 +93,8 @@ int make_map16(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int
   return GLP_OK;
 }
 
+int sm_count();
+
 // Attention engine: tcgen05 (default) or the warp-level mma.sync kernel (GLP_ATTENTION=mma).
 bool use_tc_attention() {
   static const bool tc = [] {
@@ -113,15 +115,17 @@ int launch_attention(const __half* qkv, int64_t T, int qkv_width, const int* cu,
     glp::FaParams fp{};
     fp.cu_seqlens = cu;
     fp.cu_base = cu_base;
+    fp.n_seq = n_seq;
+    fp.q_blocks = (max_len + glp::kFaBQ - 1) / glp::kFaBQ;
     fp.n_q_heads = n_q_heads;
     fp.n_kv_heads = n_kv_heads;
     fp.window = window;
     fp.out = out;
     fp.ld_out = n_q_heads * glp::kFaD;
     fp.status = status;
-    const dim3 grid(static_cast<unsigned>((max_len + glp::kFaBQ - 1) / glp::kFaBQ), static_cast<unsigned>(n_q_heads),
-                    static_cast<unsigned>(n_seq));
-    glp::flash_attn_tc_kernel<<<grid, 192, glp::kFaSmem, st>>>(mq, mkv, fp);
+    const int64_t items = static_cast<int64_t>(n_seq) * fp.q_blocks * n_q_heads;
+    const int grid = static_cast<int>(std::min<int64_t>(items, sm_count()));  // persistent CTAs
+    glp::flash_attn_tc_kernel<<<grid, glp::kFaThreads, glp::kFaSmem, st>>>(mq, mkv, fp);
   } else {
     const dim3 grid(static_cast<unsigned>((max_len + glp::kAttnBQ - 1) / glp::kAttnBQ), static_cast<unsigned>(n_q_heads),
                     static_cast<unsigned>(n_seq));
@@ -186,23 +190,23 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, int bn, int epi, G
   if (bn == 256) {
     const size_t smem = glp::GemmCfg<256>::SMEM;
     switch (epi) {
-      case glp::kEpiStore16: glp::gemm_tc_kernel<256, glp::kEpiStore16, T><<<grid, 192, smem, st>>>(ma, mb, p); break;
-      case glp::kEpiF32: glp::gemm_tc_kernel<256, glp::kEpiF32, T><<<grid, 192, smem, st>>>(ma, mb, p); break;
+      case glp::kEpiStore16: glp::gemm_tc_kernel<256, glp::kEpiStore16, T><<<grid, glp::kGemmThreads, smem, st>>>(ma, mb, p); break;
+      case glp::kEpiF32: glp::gemm_tc_kernel<256, glp::kEpiF32, T><<<grid, glp::kGemmThreads, smem, st>>>(ma, mb, p); break;
       case glp::kEpiQkv:
         if (!f16) return fail(GLP_ERR_INVALID_ARG, "fused epilogues run on f16 operands");
-        glp::gemm_tc_kernel<256, glp::kEpiQkv, __half><<<grid, 192, smem, st>>>(ma, mb, p);
+        glp::gemm_tc_kernel<256, glp::kEpiQkv, __half><<<grid, glp::kGemmThreads, smem, st>>>(ma, mb, p);
         break;
       case glp::kEpiGeglu:
         if (!f16) return fail(GLP_ERR_INVALID_ARG, "fused epilogues run on f16 operands");
-        glp::gemm_tc_kernel<256, glp::kEpiGeglu, __half><<<grid, 192, smem, st>>>(ma, mb, p);
+        glp::gemm_tc_kernel<256, glp::kEpiGeglu, __half><<<grid, glp::kGemmThreads, smem, st>>>(ma, mb, p);
         break;
       default: return fail(GLP_ERR_INVALID_ARG, "bad epilogue");
     }
   } else {
     const size_t smem = glp::GemmCfg<128>::SMEM;
     switch (epi) {
-      case glp::kEpiStore16: glp::gemm_tc_kernel<128, glp::kEpiStore16, T><<<grid, 192, smem, st>>>(ma, mb, p); break;
-      case glp::kEpiF32: glp::gemm_tc_kernel<128, glp::kEpiF32, T><<<grid, 192, smem, st>>>(ma, mb, p); break;
+      case glp::kEpiStore16: glp::gemm_tc_kernel<128, glp::kEpiStore16, T><<<grid, glp::kGemmThreads, smem, st>>>(ma, mb, p); break;
+      case glp::kEpiF32: glp::gemm_tc_kernel<128, glp::kEpiF32, T><<<grid, glp::kGemmThreads, smem, st>>>(ma, mb, p); break;
       default: return fail(GLP_ERR_INVALID_ARG, "fused epilogues need 256-wide tiles");
     }
   }
@@ -365,7 +369,8 @@ struct Device {
   float *cos_swa = nullptr, *sin_swa = nullptr, *cos_full = nullptr, *sin_full = nullptr;
   int64_t cap_tokens = 0;
   int cap_seqs = 0;
-  float* h = nullptr;
+  __nv_bfloat16* h = nullptr;  // residual stream
+  float* xf = nullptr;          // final normalised rows (pooling input)
   __half* x = nullptr;
   __half* qkv = nullptr;
   __half* attn = nullptr;
@@ -683,6 +688,7 @@ int setup_device(Device& d, const Config& c, const glp::GgufFile& g, int64_t cap
   int max_head = H;
   for (auto& hw : d.head) max_head = std::max(max_head, hw.n);
   GLP_TRY(d.alloc(&d.h, static_cast<size_t>(cap_tokens) * H));
+  GLP_TRY(d.alloc(&d.xf, static_cast<size_t>(cap_tokens) * H));
   GLP_TRY(d.alloc(&d.x, static_cast<size_t>(cap_tokens) * H));
   GLP_TRY(d.alloc(&d.qkv, static_cast<size_t>(cap_tokens) * QKV));
   GLP_TRY(d.alloc(&d.attn, static_cast<size_t>(cap_tokens) * AW));
@@ -719,7 +725,7 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
     const unsigned rows_grid = static_cast<unsigned>((T + 7) / 8);
     const float scale = static_cast<float>(std::sqrt(static_cast<double>(H)));
     const double row_in = d.table_type == glp::kGgmlQ8_0 ? H / 32 * 34.0 : 2.0 * H;
-    GLP_TRY(prof_launch(d, st, kProfEmbed, 0.0, Td * (4.0 + row_in + 6.0 * H), [&] {
+    GLP_TRY(prof_launch(d, st, kProfEmbed, 0.0, Td * (4.0 + row_in + 4.0 * H), [&] {
       if (d.table_type == glp::kGgmlQ8_0)
         glp::embed_gather_norm_kernel<<<rows_grid, 256, 0, st>>>(static_cast<const uint8_t*>(d.table), d_ids_chunk,
                                                                  T, scale, d.layers[0].attn_norm, eps, d.h, d.x);
@@ -742,7 +748,7 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
       pairs_global += visible_pairs(len, 0);
     }
     const double attn_bytes = 2.0 * Td * QKV + 2.0 * Td * AW;
-    const double post_bytes = Td * (2.0 * H + 8.0 * H + 2.0 * H);
+    const double post_bytes = Td * (2.0 * H + 4.0 * H + 2.0 * H);  // y + h in/out + x (16-bit)
     for (int l = 0; l < c.n_layers; ++l) {
       LayerW& L = d.layers[l];
       GemmParams p{};
@@ -782,7 +788,7 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
                           [&] { return launch_gemm<__half>(m_attn, L.m_o, bn_for(H), glp::kEpiStore16, po, st); }));
       GLP_TRY(prof_launch(d, st, kProfPostNorm, 0.0, post_bytes, [&] {
         glp::post_norm_residual_kernel<false><<<rows_grid, 256, 0, st>>>(d.y, d.h, L.post_attn, 1.0f, L.ffn_norm,
-                                                                         eps, T, d.x);
+                                                                         eps, T, d.x, nullptr);
         GLP_CUDA(cudaGetLastError());
         return GLP_OK;
       }));
@@ -808,13 +814,13 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
       GLP_TRY(prof_launch(d, st, kProfGemmDown, gemm_flops(Td, H, F), gemm_bytes(Td, H, F, 2.0),
                           [&] { return launch_gemm<__half>(m_a, L.m_down, bn_for(H), glp::kEpiStore16, pd, st); }));
       const bool last = l + 1 == c.n_layers;
-      GLP_TRY(prof_launch(d, st, kProfPostNorm, 0.0, last ? Td * 10.0 * H : post_bytes, [&] {
+      GLP_TRY(prof_launch(d, st, kProfPostNorm, 0.0, last ? Td * 8.0 * H : post_bytes, [&] {
         if (!last)
           glp::post_norm_residual_kernel<false><<<rows_grid, 256, 0, st>>>(
-              d.y, d.h, L.post_ffw, L.layer_scalar, d.layers[l + 1].attn_norm, eps, T, d.x);
+              d.y, d.h, L.post_ffw, L.layer_scalar, d.layers[l + 1].attn_norm, eps, T, d.x, nullptr);
         else
           glp::post_norm_residual_kernel<true><<<rows_grid, 256, 0, st>>>(d.y, d.h, L.post_ffw, L.layer_scalar,
-                                                                          d.out_norm, eps, T, d.x);
+                                                                          d.out_norm, eps, T, nullptr, d.xf);
         GLP_CUDA(cudaGetLastError());
         return GLP_OK;
       }));
@@ -822,7 +828,7 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
   }
   // masked mean of the final-normed rows, then the dense head on the pooled vectors
   GLP_TRY(prof_launch(d, st, kProfPool, 0.0, 4.0 * Td * H + 2.0 * n_seq * H, [&] {
-    glp::mean_pool_kernel<<<n_seq, 192, 0, st>>>(d.h, d_cu_chunk, base, n_seq, d.pooled, nullptr);
+    glp::mean_pool_kernel<<<n_seq, 192, 0, st>>>(d.xf, d_cu_chunk, base, n_seq, d.pooled, nullptr);
     GLP_CUDA(cudaGetLastError());
     return GLP_OK;
   }));

@@ -1,7 +1,8 @@
 // Memory-bound row kernels (one warp per token row, 128-bit vector accesses, warp-shuffle
 // reductions) and the Q8_0 dequantisation kernels.
 //
-// Residual stream h is f32 [T, H]; the GEMM inputs x are f16 [T, H] (every GEMM input is a
+// Residual stream h is bf16 [T, H] (the hidden-state type of the reference's Metal path; f32
+// arithmetic on every update); the GEMM inputs x are f16 [T, H] (every GEMM input is a
 // normalised row or a convex combination of normalised rows, so f16's range suffices and its
 // 11-bit mantissa keeps the dequantised weights and activations close to exact).
 #pragma once
@@ -92,6 +93,22 @@ __device__ __forceinline__ void load_f16x8(const __half* p, float* v) {
     v[2 * i + 1] = f.y;
   }
 }
+template <typename T>
+__device__ __forceinline__ void load16x8(const T* p, float* v) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = Half16<T>::to_f32(e[i]);
+}
+template <typename T>
+__device__ __forceinline__ void store16x8(T* p, const float* v) {
+  uint4 u;
+  u.x = Half16<T>::pack(v[0], v[1]);
+  u.y = Half16<T>::pack(v[2], v[3]);
+  u.z = Half16<T>::pack(v[4], v[5]);
+  u.w = Half16<T>::pack(v[6], v[7]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
 __device__ __forceinline__ void store_f16x8(__half* p, const float* v) {
   uint4 u;
   u.x = pack_f16(v[0], v[1]);
@@ -108,7 +125,7 @@ __device__ __forceinline__ void store_f16x8(__half* p, const float* v) {
 // 34-byte blocks).
 __global__ void embed_gather_norm_kernel(const uint8_t* __restrict__ table, const int* __restrict__ ids,
                                          int n_tokens, float scale, const float* __restrict__ w, float eps,
-                                         float* __restrict__ h, __half* __restrict__ x) {
+                                         __nv_bfloat16* __restrict__ h, __half* __restrict__ x) {
   const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (t >= n_tokens) return;
@@ -125,12 +142,12 @@ __global__ void embed_gather_norm_kernel(const uint8_t* __restrict__ table, cons
   }
   ss = warp_sum(ss);
   const float inv = 1.0f / sqrtf(ss / static_cast<float>(kHidden) + eps);
-  float* hr = h + static_cast<size_t>(t) * kHidden;
+  __nv_bfloat16* hr = h + static_cast<size_t>(t) * kHidden;
   __half* xr = x + static_cast<size_t>(t) * kHidden;
 #pragma unroll
   for (int b = 0; b < kHidden / 32; ++b) {
     const int e = b * 32 + lane;
-    hr[e] = v[b];
+    hr[e] = __float2bfloat16_rn(v[b]);
     xr[e] = __float2half_rn(v[b] * inv * __ldg(w + e));
   }
 }
@@ -138,7 +155,7 @@ __global__ void embed_gather_norm_kernel(const uint8_t* __restrict__ table, cons
 // Same gather for a bf16 token table (BF16 GGUF).
 __global__ void embed_gather_norm_bf16_kernel(const __nv_bfloat16* __restrict__ table, const int* __restrict__ ids,
                                               int n_tokens, float scale, const float* __restrict__ w, float eps,
-                                              float* __restrict__ h, __half* __restrict__ x) {
+                                              __nv_bfloat16* __restrict__ h, __half* __restrict__ x) {
   const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (t >= n_tokens) return;
@@ -152,12 +169,12 @@ __global__ void embed_gather_norm_bf16_kernel(const __nv_bfloat16* __restrict__ 
   }
   ss = warp_sum(ss);
   const float inv = 1.0f / sqrtf(ss / static_cast<float>(kHidden) + eps);
-  float* hr = h + static_cast<size_t>(t) * kHidden;
+  __nv_bfloat16* hr = h + static_cast<size_t>(t) * kHidden;
   __half* xr = x + static_cast<size_t>(t) * kHidden;
 #pragma unroll
   for (int b = 0; b < kHidden / 32; ++b) {
     const int e = b * 32 + lane;
-    hr[e] = v[b];
+    hr[e] = __float2bfloat16_rn(v[b]);
     xr[e] = __float2half_rn(v[b] * inv * __ldg(w + e));
   }
 }
@@ -165,24 +182,25 @@ __global__ void embed_gather_norm_bf16_kernel(const __nv_bfloat16* __restrict__ 
 // ---------------------------------------------------------------------------- post-norm
 // h <- (h + RMSNorm(y) * w_post) * layer_scalar            (norm.rs:65-94, layer.rs:20-50)
 // then the next pre-norm:  x = RMSNorm(h) * w_next
-//   FINAL = false: x is f16 (the next GEMM's input)
-//   FINAL = true : the normalised row is written back over h in f32 (output_norm, model.rs:576)
-// One warp per row; lane owns elements [c*256 + lane*8, +8) for c = 0..2.
+//   FINAL = false: h is updated (bf16) and x is f16 (the next GEMM's input)
+//   FINAL = true : the normalised row is written to xf in f32 (output_norm, model.rs:576)
+// All arithmetic in f32.  One warp per row; lane owns elements [c*256 + lane*8, +8).
 template <bool FINAL>
-__global__ void post_norm_residual_kernel(const __half* __restrict__ y, float* __restrict__ h,
+__global__ void post_norm_residual_kernel(const __half* __restrict__ y, __nv_bfloat16* __restrict__ h,
                                           const float* __restrict__ w_post, float layer_scalar,
                                           const float* __restrict__ w_next, float eps, int n_tokens,
-                                          __half* __restrict__ x) {
+                                          __half* __restrict__ x, float* __restrict__ xf) {
   const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (t >= n_tokens) return;
   const __half* yr = y + static_cast<size_t>(t) * kHidden;
-  float* hr = h + static_cast<size_t>(t) * kHidden;
+  __nv_bfloat16* hr = h + static_cast<size_t>(t) * kHidden;
   float yv[kVecPerLane][8], hv[kVecPerLane][8];
   float ss = 0.f;
 #pragma unroll
   for (int c = 0; c < kVecPerLane; ++c) {
-    load_f16x8(yr + c * 256 + lane * 8, yv[c]);
+    load16x8<__half>(yr + c * 256 + lane * 8, yv[c]);
+    load16x8<__nv_bfloat16>(hr + c * 256 + lane * 8, hv[c]);
 #pragma unroll
     for (int j = 0; j < 8; ++j) ss = fmaf(yv[c][j], yv[c][j], ss);
   }
@@ -193,7 +211,6 @@ __global__ void post_norm_residual_kernel(const __half* __restrict__ y, float* _
   for (int c = 0; c < kVecPerLane; ++c) {
     const int e0 = c * 256 + lane * 8;
     float wv[8];
-    load_f32x8(hr + e0, hv[c]);
     load_f32x8(w_post + e0, wv);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
@@ -211,10 +228,10 @@ __global__ void post_norm_residual_kernel(const __half* __restrict__ y, float* _
 #pragma unroll
     for (int j = 0; j < 8; ++j) o[j] = hv[c][j] * inv_h * wv[j];
     if constexpr (FINAL) {
-      store_f32x8(hr + e0, o);
+      store_f32x8(xf + static_cast<size_t>(t) * kHidden + e0, o);
     } else {
-      store_f32x8(hr + e0, hv[c]);
-      store_f16x8(x + static_cast<size_t>(t) * kHidden + e0, o);
+      store16x8<__nv_bfloat16>(hr + e0, hv[c]);
+      store16x8<__half>(x + static_cast<size_t>(t) * kHidden + e0, o);
     }
   }
 }
