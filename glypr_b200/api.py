@@ -39,7 +39,7 @@ GLP_PROFILE_KINDS = 12
 EXPORTED_SYMBOLS = (
     "glp_open", "glp_close", "glp_last_error", "glp_model_info", "glp_embed_tokens",
     "glp_embed_packed_device", "glp_device_status", "glp_profile_enable", "glp_profile_read",
-    "glp_q8_0_dequant", "glp_q8_0_gemm", "glp_bf16_gemm", "glp_flash_attention",
+    "glp_q8_0_dequant", "glp_q8_0_gemm", "glp_q8_0_gemm_noalloc", "glp_bf16_gemm", "glp_flash_attention",
 )
 
 
@@ -110,6 +110,7 @@ def load_library(path: Optional[str] = None) -> ctypes.CDLL:
         L.glp_profile_read.argtypes = [P, I, P]
         L.glp_q8_0_dequant.argtypes = [P, I64, P, P]
         L.glp_q8_0_gemm.argtypes = [P, I, I, P, I, P, I, P]
+        L.glp_q8_0_gemm_noalloc.argtypes = [P, I, I, P, I, P, I, P]
         L.glp_bf16_gemm.argtypes = [P, I, I, P, I, P, I, P]
         L.glp_flash_attention.argtypes = [P, P, I, I, I, I, I, I, P, P]
         _lib = L
@@ -278,6 +279,12 @@ def q8_0_dequant(d_blocks: int, n_blocks: int, d_out: int, stream: int = 0) -> N
 def q8_0_gemm(d_w: int, n: int, k: int, d_x: int, m: int, d_y: int, y_is_f32: bool, stream: int = 0) -> None:
     check(load_library().glp_q8_0_gemm(ctypes.c_void_p(d_w), n, k, ctypes.c_void_p(d_x), m, ctypes.c_void_p(d_y),
                                        int(y_is_f32), ctypes.c_void_p(stream)))
+
+
+def q8_0_gemm_noalloc(d_w: int, n: int, k: int, d_x: int, m: int, d_y: int, y_is_f32: bool, stream: int = 0) -> None:
+    """glp_q8_0_gemm_noalloc: the same GEMM with its scratch in the library's fixed array."""
+    check(load_library().glp_q8_0_gemm_noalloc(ctypes.c_void_p(d_w), n, k, ctypes.c_void_p(d_x), m,
+                                               ctypes.c_void_p(d_y), int(y_is_f32), ctypes.c_void_p(stream)))
 
 
 def bf16_gemm(d_w: int, n: int, k: int, d_x: int, m: int, d_y: int, y_is_f32: bool, stream: int = 0) -> None:

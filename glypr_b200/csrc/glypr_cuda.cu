@@ -1000,6 +1000,42 @@ int run_bf16_gemm(const __nv_bfloat16* w, int N, int K, const void* x, int M, vo
 
 }  // namespace
 
+// ------------------------------------------------------------------------------ no-allocation GEMM
+// glp_q8_0_gemm_noalloc keeps its dequantised weight in this file-scope device array instead
+// of memory the library allocates: every GPU that loads the library holds the array (6 MiB
+// of bf16) until the process exits, and every call on a device shares it.
+constexpr int64_t kNoAllocMaxWeightElems = 3 * 1024 * 1024;  // N * K limit of the entry point
+static __device__ __align__(256) __nv_bfloat16 g_noalloc_weight[kNoAllocMaxWeightElems];
+static __device__ int g_noalloc_status;
+
+namespace {
+
+struct NoAllocDevicePtrs {
+  std::mutex mu;
+  std::array<__nv_bfloat16*, 64> weight{};
+  std::array<int*, 64> status{};
+};
+NoAllocDevicePtrs g_noalloc_ptrs;
+
+// Device addresses of the file-scope scratch on the current device, looked up once per device
+// with that device current (the host-side names are only stand-ins for them).
+int noalloc_pointers(int dev, __nv_bfloat16** weight, int** status) {
+  std::lock_guard<std::mutex> lk(g_noalloc_ptrs.mu);
+  if (!g_noalloc_ptrs.weight[dev]) {
+    void* w = nullptr;
+    void* s = nullptr;
+    GLP_CUDA(cudaGetSymbolAddress(&w, g_noalloc_weight));
+    GLP_CUDA(cudaGetSymbolAddress(&s, g_noalloc_status));
+    g_noalloc_ptrs.weight[dev] = static_cast<__nv_bfloat16*>(w);
+    g_noalloc_ptrs.status[dev] = static_cast<int*>(s);
+  }
+  *weight = g_noalloc_ptrs.weight[dev];
+  *status = g_noalloc_ptrs.status[dev];
+  return GLP_OK;
+}
+
+}  // namespace
+
 // ================================================================================= C ABI
 extern "C" {
 
@@ -1289,6 +1325,45 @@ int glp_flash_attention(const void* d_qkv, const int32_t* d_cu_seqlens, int n_se
   return launch_attention(static_cast<const __half*>(d_qkv), total, ld, d_cu_seqlens, 0, n_seq, max_len, n_q_heads,
                           n_kv_heads, window, static_cast<__half*>(d_out), status,
                           static_cast<cudaStream_t>(stream));
+}
+
+// Variant of glp_q8_0_gemm for callers that cannot allocate device memory: the dequantised
+// weight goes into the library's file-scope scratch array instead of a cudaMalloc'd buffer,
+// and the call itself allocates nothing.  N * K must not exceed kNoAllocMaxWeightElems.
+int glp_q8_0_gemm_noalloc(const void* d_q8_w, int N, int K, const void* d_x_bf16, int M, void* d_y, int y_is_f32,
+                          void* stream) {
+  if (N <= 0 || K <= 0 || N % 128 || K % 64 || M < 0)
+    return fail(GLP_ERR_INVALID_ARG, "Q8_0 GEMM needs N % 128 == 0, K % 64 == 0, M >= 0");
+  if (static_cast<int64_t>(N) * K > kNoAllocMaxWeightElems)
+    return fail(GLP_ERR_INVALID_ARG, "glp_q8_0_gemm_noalloc: weight of " + std::to_string(static_cast<int64_t>(N) * K) +
+                                         " elements exceeds the no-allocation scratch limit of " +
+                                         std::to_string(kNoAllocMaxWeightElems) + " (N * K)");
+  if (!d_q8_w || !d_x_bf16 || !d_y) return fail(GLP_ERR_INVALID_ARG, "null pointer");
+  int dev = 0;
+  GLP_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(GLP_ERR_INVALID_ARG, "device index out of range");
+  __nv_bfloat16* w = nullptr;
+  int* status = nullptr;
+  GLP_TRY(noalloc_pointers(dev, &w, &status));
+  GLP_TRY(ensure_kernel_attrs());
+  if (M == 0) return GLP_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t nb = static_cast<int64_t>(N) * (K / 32);
+  glp::q8_0_dequant_rows_kernel<__nv_bfloat16><<<static_cast<unsigned>((nb + 255) / 256), 256, 0, st>>>(
+      static_cast<const uint8_t*>(d_q8_w), N, K, w, 0, 0, 0);
+  GLP_CUDA(cudaGetLastError());
+  const int bn = bn_for(N);
+  CUtensorMap ma, mb;
+  GLP_TRY(make_map16(&ma, d_x_bf16, M, K, K, 128, false));
+  GLP_TRY(make_map16(&mb, w, N, K, K, bn, false));
+  GemmParams p{};
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.C = d_y;
+  p.ldc = N;
+  p.status = status;
+  return launch_gemm<__nv_bfloat16>(ma, mb, bn, y_is_f32 ? glp::kEpiF32 : glp::kEpiStore16, p, st);
 }
 
 }  // extern "C"

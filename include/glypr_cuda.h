@@ -133,6 +133,20 @@ int glp_q8_0_dequant(const void* d_blocks, int64_t n_blocks, float* d_out, void*
 int glp_q8_0_gemm(const void* d_q8_w, int N, int K, const void* d_x_bf16, int M, void* d_y, int y_is_f32,
                   void* stream);
 
+/* The Q8_0 GEMM above for callers that cannot allocate device memory (no counterpart in the
+ * reference): code running where cudaMalloc is unavailable or must not be called, such as
+ * inside a host callback, under a caller-owned memory pool or fixed memory budget, or from a
+ * framework that forbids allocations after start-up.  The dequantised weight goes into a
+ * fixed scratch array inside the library (6 MiB per GPU that loads the library, held until
+ * the process exits), so N * K must be at most 3,145,728; larger weights are rejected with
+ * GLP_ERR_INVALID_ARG.  The call allocates nothing and frees nothing.  The first call on a
+ * device looks up the array's device address; make that first call before any stream
+ * capture.  All calls on a device share the array: calls that overlap on the GPU (other
+ * streams, other host threads) race on it.  Each call overwrites every scratch element it
+ * reads, so nothing needs to be cleared between calls. */
+int glp_q8_0_gemm_noalloc(const void* d_q8_w, int N, int K, const void* d_x_bf16, int M, void* d_y, int y_is_f32,
+                          void* stream);
+
 /* Same GEMM on an already dequantised bf16 weight [N, K] (the model path's layout). */
 int glp_bf16_gemm(const void* d_w_bf16, int N, int K, const void* d_x_bf16, int M, void* d_y, int y_is_f32,
                   void* stream);
