@@ -11,7 +11,7 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libglypr_cuda.so")
 SOURCES = ["glypr_cuda.cu", "gguf.cpp"]
-HEADERS = ["common.cuh", "gemm.cuh", "attention.cuh", "rowops.cuh", "gguf.h"]
+HEADERS = ["common.cuh", "gemm.cuh", "attention.cuh", "attention_tc.cuh", "rowops.cuh", "gguf.h"]
 
 
 def nvcc() -> str:

@@ -109,9 +109,12 @@ int launch_attention(const __half* qkv, int64_t T, int qkv_width, const int* cu,
                      int n_q_heads, int n_kv_heads, int window, __half* out, int* status, cudaStream_t st) {
   if (T <= 0 || n_seq <= 0 || max_len <= 0) return GLP_OK;
   if (use_tc_attention()) {
-    CUtensorMap mq, mkv;
+    CUtensorMap mq, mkv, mo;
     GLP_TRY(make_map16(&mq, qkv, T, qkv_width, qkv_width, glp::kFaBQ, true));
     GLP_TRY(make_map16(&mkv, qkv, T, qkv_width, qkv_width, glp::kFaBKV, true));
+    // output rows [T, Hq * 256]: bulk stores of 64 columns x 32 rows
+    GLP_TRY(make_map16(&mo, out, T, static_cast<int64_t>(n_q_heads) * glp::kFaD,
+                       static_cast<int64_t>(n_q_heads) * glp::kFaD, glp::kFaOutBoxRows, true));
     glp::FaParams fp{};
     fp.cu_seqlens = cu;
     fp.cu_base = cu_base;
@@ -125,7 +128,7 @@ int launch_attention(const __half* qkv, int64_t T, int qkv_width, const int* cu,
     fp.status = status;
     const int64_t items = static_cast<int64_t>(n_seq) * fp.q_blocks * n_q_heads;
     const int grid = static_cast<int>(std::min<int64_t>(items, sm_count()));  // persistent CTAs
-    glp::flash_attn_tc_kernel<<<grid, glp::kFaThreads, glp::kFaSmem, st>>>(mq, mkv, fp);
+    glp::flash_attn_tc_kernel<<<grid, glp::kFaThreads, glp::kFaSmem, st>>>(mq, mkv, mo, fp);
   } else {
     const dim3 grid(static_cast<unsigned>((max_len + glp::kAttnBQ - 1) / glp::kAttnBQ), static_cast<unsigned>(n_q_heads),
                     static_cast<unsigned>(n_seq));
