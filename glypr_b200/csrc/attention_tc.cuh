@@ -10,11 +10,14 @@
 // Persistent kernel: one CTA per SM loops over work items (sequence, 128-row query block,
 // head), ordered so that the CTAs running at the same time share sequences (K/V stay in L2).
 // Tensor memory and the mbarriers are set up once; every ring below is indexed by a running
-// KV-tile counter g that continues across items.  320 threads:
-//   warp 0      TMA producer: Q of the item (4 boxes of 64 dims x 128 rows) once the
-//               previous item's Q has been copied out of the buffer, then K and V tiles of 64
-//               keys into two separate 2-stage rings (a K stage frees as soon as S_j is
-//               computed)
+// KV-tile counter g that continues across items.  352 threads:
+//   warp 0      TMA producer of Q and K: Q of the item (4 boxes of 64 dims x 128 rows) once
+//               the previous item's Q has been copied out of the buffer, then the K tiles of
+//               64 keys into a 2-stage ring (a stage frees as soon as S_j is computed)
+//   warp 10     TMA producer of the V tiles (2-stage ring, a stage frees once P_j V_j is
+//               computed).  K and V have separate producers so that a K load never queues
+//               behind a wait for a V stage: S_{j+2} needs K_{j+2} about one softmax tile
+//               after S_j frees its stage, which is little more than an L2 round trip.
 //   warp 1      TMEM owner + single-thread MMA issuer.  Both MMAs read their A operand from
 //               tensor memory, so shared-memory bandwidth goes to K and V only:
 //                 Q  -> TMEM      (16 tcgen05.cp of 128 rows x 16 dims, once per item)
@@ -39,8 +42,8 @@
 //   * 2^x: MUFU.EX2 for most pairs, a degree-4 polynomial on the FMA pipe for the pairs in
 //     kFaPolyPairs (the special-function unit is the bottleneck otherwise);
 //   * P (f16 pairs) into tensor memory over the first 32 columns of its own S slot (both
-//     halves have read S_j before either writes P_j: the write follows the exchange); the
-//     next tile's scores are read from TMEM before the P store so their latency overlaps it.
+//     halves have read S_j before either writes P_j: the write follows the exchange); only
+//     then is the next tile's S waited for and read.
 // At the item's end O / l is converted to f16 and staged through shared memory (4 KB per
 // warp): bulk tensor stores for 32-row slices inside the sequence, coalesced stores row by
 // row for the slice that crosses its end.
@@ -62,7 +65,7 @@ constexpr uint32_t kFaBarBytes = 256;
 constexpr uint32_t kFaXchBytes = 2 * 2 * 128 * 4;        // [2 slots][2 halves][128 rows] f32
 // the dynamic shared-memory base is declared 1024-aligned (checked at run time)
 constexpr size_t kFaSmem = kFaQBytes + 4 * kFaKVBytes + kFaStageBytes + kFaBarBytes + kFaXchBytes;
-constexpr int kFaThreads = 320;
+constexpr int kFaThreads = 352;
 constexpr int kFaOutBoxRows = 32;                        // rows of one output bulk store
 constexpr uint32_t kFaTmemQ = 128;                       // TMEM column of Q (128 columns)
 constexpr uint32_t kFaTmemO = 256;                       // TMEM column of O (256 columns)
@@ -222,7 +225,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      // ------------------------------------------------------------------ producer
+      // ------------------------------------------------------------------ Q / K producer
       int it = 0;
       uint32_t g = 0;
       bool ok = true;
@@ -247,7 +250,26 @@ __global__ void __launch_bounds__(kFaThreads, 1)
           mbar_arrive_expect_tx(&k_full[st], kFaKVBytes);
           for (int c = 0; c < 4; ++c)
             tma_load_2d(sK + st * kFaKVBytes + c * kFaKVChunk, &tmKV, &k_full[st], w.kcol + 64 * c, row);
-          if (!mbar_wait(&v_empty[st], ph, abort_flag)) {
+        }
+        ++it;
+      }
+      if (!ok) {
+        if (!*abort_flag) record_error(p.status, kErrTimeoutProducer);
+        *abort_flag = 1;
+      }
+    }
+  } else if (warp == 10) {
+    if (lane == 0) {
+      // ------------------------------------------------------------------ V producer
+      uint32_t g = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x) {
+        const FaItem w = fa_item(p, item);
+        if (!w.valid) continue;
+        for (int j = 0; j < w.n_tiles; ++j, ++g) {
+          const int st = g & 1;
+          const int row = w.tok0 + (w.t_lo + j) * kFaBKV;
+          if (!mbar_wait(&v_empty[st], ((g >> 1) & 1) ^ 1, abort_flag)) {
             ok = false;
             break;
           }
@@ -255,7 +277,6 @@ __global__ void __launch_bounds__(kFaThreads, 1)
           for (int c = 0; c < 4; ++c)
             tma_load_2d(sV + st * kFaKVBytes + c * kFaKVChunk, &tmKV, &v_full[st], w.vcol + 64 * c, row);
         }
-        ++it;
       }
       if (!ok) {
         if (!*abort_flag) record_error(p.status, kErrTimeoutProducer);
@@ -354,6 +375,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     }
   } else {
     // -------------------------------------------------------------------- softmax + epilogue
+    // (warps 2..9)
     const int quad = warp & 3;
     const int half = (warp - 2) >> 2;  // which 32 key columns of S / 128 columns of O
     const int r = quad * 32 + lane;    // query row inside the tile == TMEM lane
@@ -494,9 +516,15 @@ __global__ void __launch_bounds__(kFaThreads, 1)
           }
           tmem_st_wait();
         }
-        // read the next tile's scores now: the TMEM load latency overlaps the P store
-        const bool more = j + 1 < w.n_tiles;
-        if (more) {
+        // P row r, this half's 32 keys: 16 columns of f16 pairs over the S slot
+        tmem_st16(lane_base + st * kFaBKV + half * 16, pk);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[st]);
+        // then the next tile's scores (S_{j+1} is queued behind P_{j-1} V_{j-1}: waiting for it
+        // before publishing P_j would chain the tensor core and the softmax)
+        if (j + 1 < w.n_tiles) {
           const uint32_t gn = gj + 1;
           const bool wt = mbar_wait(&s_full[gn & 1], (gn >> 1) & 1, abort_flag);
           if (!__all_sync(0xffffffffu, wt)) {
@@ -505,14 +533,8 @@ __global__ void __launch_bounds__(kFaThreads, 1)
           }
           tc_fence_after();
           tmem_ld32(lane_base + (gn & 1) * kFaBKV + half * 32, sr);
+          tmem_ld_wait_tied(sr);
         }
-        // P row r, this half's 32 keys: 16 columns of f16 pairs over the S slot
-        tmem_st16(lane_base + st * kFaBKV + half * 16, pk);
-        tmem_st_wait();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&p_full[st]);
-        if (more) tmem_ld_wait_tied(sr);
       }
       if (!ok) break;
       // ---- drain O of this item (the next item's Q load and S_0 are already in flight)

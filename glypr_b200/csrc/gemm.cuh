@@ -51,24 +51,15 @@ struct GemmCfg {
   static constexpr uint32_t A_BYTES = BM * BK * 2;
   static constexpr uint32_t B_BYTES = BN * BK * 2;
   static constexpr uint32_t TMEM_COLS = 2 * BN;  // double-buffered accumulator
-  // after the stages: 512 B of barriers/flags, then the epilogue pairs' row-sum exchange
+  // after the stages: 512 B of barriers/flags, the epilogue pairs' row-sum exchange, then one
+  // 32-row x 128-byte output staging tile per epilogue warp
   static constexpr uint32_t RED_OFFSET = 512;
-  static constexpr size_t SMEM = 1024 + STAGES * (A_BYTES + B_BYTES) + RED_OFFSET + 2 * 2 * 128 * 4;
+  static constexpr uint32_t RED_BYTES = 2 * 2 * 128 * 4;
+  static constexpr uint32_t STAGE_OFFSET = STAGES * (A_BYTES + B_BYTES) + RED_OFFSET + RED_BYTES;
+  static constexpr uint32_t STAGE_BYTES = 8 * 32 * 128;
+  // the dynamic shared-memory base is declared 1024-aligned (checked at run time)
+  static constexpr size_t SMEM = STAGE_OFFSET + STAGE_BYTES;
 };
-
-template <typename T>
-__device__ __forceinline__ void store16x32(T* dst, const float* v) {
-  uint4* d = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    uint4 u;
-    u.x = Half16<T>::pack(v[8 * q + 0], v[8 * q + 1]);
-    u.y = Half16<T>::pack(v[8 * q + 2], v[8 * q + 3]);
-    u.z = Half16<T>::pack(v[8 * q + 4], v[8 * q + 5]);
-    u.w = Half16<T>::pack(v[8 * q + 6], v[8 * q + 7]);
-    d[q] = u;
-  }
-}
 
 // gelu_tanh(g) * u with the reference's clamp (cpu_simd/geglu.rs:6-18), branch-free so the
 // 32 elements of a chunk interleave.  Uses the identity 0.5 * (1 + tanh(z)) = 1 / (1 + e^-2z);
@@ -80,50 +71,59 @@ __device__ __forceinline__ float geglu_f(float g, float u) {
   return g <= -10.0f ? 0.0f : a;
 }
 
-template <int EPI, typename T>
-__device__ __forceinline__ void epi_store_chunk(const GemmParams& p, int row, int col, const uint32_t (&r)[32]) {
-  float v[32];
+// The epilogue warps write their rows through a per-warp staging tile: thread `lane` puts its
+// row's 128 bytes into row `lane` (16-byte chunks swizzled by the row, conflict-free), then
+// the warp writes the 32 rows out 4 at a time, 128 contiguous bytes each (a store instruction
+// covers 4 full lines instead of 32 partial ones).
+__device__ __forceinline__ void stage_chunk(uint8_t* stage, int c, uint4 v) {
+  const int lane = threadIdx.x & 31;
+  *reinterpret_cast<uint4*>(stage + lane * 128 + ((c ^ (lane & 7)) << 4)) = v;
+}
+// rows [0, rows_valid) of the staging tile -> dst0 + row * ld_bytes
+__device__ __forceinline__ void flush_rows128(const uint8_t* stage, uint8_t* dst0, size_t ld_bytes, int rows_valid) {
+  const int lane = threadIdx.x & 31;
+  __syncwarp();
 #pragma unroll
-  for (int j = 0; j < 32; ++j) v[j] = u2f(r[j]);
-  const size_t off = static_cast<size_t>(row) * p.ldc + col;
-  if constexpr (EPI == kEpiStore16) {
-    store16x32<T>(reinterpret_cast<T*>(p.C) + off, v);
-  } else {
-    float4* d = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.C) + off);
-#pragma unroll
-    for (int q = 0; q < 8; ++q) d[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+  for (int it = 0; it < 8; ++it) {
+    const int row = it * 4 + (lane >> 3), c = lane & 7;
+    const uint4 v = *reinterpret_cast<const uint4*>(stage + row * 128 + ((c ^ (row & 7)) << 4));
+    if (row < rows_valid) *reinterpret_cast<uint4*>(dst0 + row * ld_bytes + c * 16) = v;
   }
+  __syncwarp();
+}
+// 32 consecutive 32-bit words (e.g. 64 packed 16-bit outputs) as one staged row
+__device__ __forceinline__ void stage_words32(uint8_t* stage, const uint32_t (&w)[32]) {
+#pragma unroll
+  for (int c = 0; c < 8; ++c) stage_chunk(stage, c, make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]));
 }
 
-template <typename T>
-__device__ __forceinline__ void epi_geglu_chunk(const GemmParams& p, int row, int col, const uint32_t (&g)[16],
-                                                const uint32_t (&u)[16]) {
-  float v[16];
+// 8 frequency pairs (i, i + 128), i = f0 .. f0 + 7, of one head row: RMS scale, gain, NeoX
+// RoPE; f16 pairs of the lower (x1) and upper (x2) halves into plo / phi.
+__device__ __forceinline__ void epi_qkv_chunk8(int f0, float inv, const float* gain, bool rope,
+                                               const uint32_t (&lo)[8], const uint32_t (&hi)[8],
+                                               const float (&cv)[8], const float (&sv)[8], uint32_t (&plo)[4],
+                                               uint32_t (&phi)[4]) {
+  float g1[8], g2[8];
+  if (gain) {
+    const float4* ga = reinterpret_cast<const float4*>(gain + f0);
+    const float4* gb = reinterpret_cast<const float4*>(gain + 128 + f0);
 #pragma unroll
-  for (int j = 0; j < 16; ++j) v[j] = geglu_f(u2f(g[j]), u2f(u[j]));
-  uint4* d = reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.C) + static_cast<size_t>(row) * p.ldc + col);
-  d[0] = make_uint4(Half16<T>::pack(v[0], v[1]), Half16<T>::pack(v[2], v[3]), Half16<T>::pack(v[4], v[5]),
-                    Half16<T>::pack(v[6], v[7]));
-  d[1] = make_uint4(Half16<T>::pack(v[8], v[9]), Half16<T>::pack(v[10], v[11]), Half16<T>::pack(v[12], v[13]),
-                    Half16<T>::pack(v[14], v[15]));
-}
-
-// 16 frequency pairs (i, i + 128) of one head row: RMS scale, gain, NeoX RoPE, f16 store.
-__device__ __forceinline__ void epi_qkv_chunk(__half* out, int c, float inv, const float* gain, bool rope,
-                                              const uint32_t (&lo)[16], const uint32_t (&hi)[16],
-                                              const float (&cv)[16], const float (&sv)[16]) {
-  uint32_t plo[8], phi[8];
+    for (int q = 0; q < 2; ++q) {
+      const float4 a = __ldg(ga + q), b = __ldg(gb + q);
+      g1[4 * q] = a.x, g1[4 * q + 1] = a.y, g1[4 * q + 2] = a.z, g1[4 * q + 3] = a.w;
+      g2[4 * q] = b.x, g2[4 * q + 1] = b.y, g2[4 * q + 2] = b.z, g2[4 * q + 3] = b.w;
+    }
+  }
 #pragma unroll
-  for (int j = 0; j < 16; j += 2) {
+  for (int j = 0; j < 8; j += 2) {
     float a[2], b[2];
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
-      const int i = c * 16 + j + e;
       float x1 = u2f(lo[j + e]) * inv;
       float x2 = u2f(hi[j + e]) * inv;
       if (gain) {
-        x1 *= __ldg(gain + i);
-        x2 *= __ldg(gain + i + 128);
+        x1 *= g1[j + e];
+        x2 *= g2[j + e];
       }
       if (rope) {  // x*cos + rotate_half(x)*sin, rotate_half = cat(-x2, x1)
         a[e] = x1 * cv[j + e] + (-x2) * sv[j + e];
@@ -136,63 +136,84 @@ __device__ __forceinline__ void epi_qkv_chunk(__half* out, int c, float inv, con
     plo[j / 2] = pack_f16(a[0], a[1]);
     phi[j / 2] = pack_f16(b[0], b[1]);
   }
-  uint4* dlo = reinterpret_cast<uint4*>(out + c * 16);
-  uint4* dhi = reinterpret_cast<uint4*>(out + 128 + c * 16);
-  dlo[0] = make_uint4(plo[0], plo[1], plo[2], plo[3]);
-  dlo[1] = make_uint4(plo[4], plo[5], plo[6], plo[7]);
-  dhi[0] = make_uint4(phi[0], phi[1], phi[2], phi[3]);
-  dhi[1] = make_uint4(phi[4], phi[5], phi[6], phi[7]);
 }
 
 // One accumulator tile -> global, by the two epilogue warps of one TMEM lane quadrant: `half`
-// selects which half of the tile's columns this warp converts.  Tensor-memory reads are
-// software-pipelined (the next chunk's tcgen05.ld is in flight while the current chunk is
-// converted and stored).  `red` is the pair's shared-memory exchange for the QKV row sums,
-// synchronised through the pair's rendezvous barrier `xbar` (phase bit `xph`).  Returns false
-// if that rendezvous timed out.
+// selects which half of the tile's columns this warp converts; `stage` is the warp's
+// 32 x 128 B staging tile and `row0` the tile row of its lane 0.  `red` is the pair's
+// shared-memory exchange for the QKV row sums, synchronised through the pair's rendezvous
+// barrier `xbar` (phase bit `xph`).  Returns false if that rendezvous timed out.
 template <int BN, int EPI, typename T>
 __device__ __forceinline__ bool gemm_epilogue_tile(const GemmParams& p, uint32_t tacc, int m_blk, int n_blk,
                                                    int row_in_tile, int half, float* red, uint64_t* xbar,
-                                                   uint32_t& xph, volatile int* abort_flag) {
+                                                   uint32_t& xph, volatile int* abort_flag, uint8_t* stage) {
   const int row = m_blk * 128 + row_in_tile;
-  const bool live = row < p.M;
+  const int wrow0 = row - (threadIdx.x & 31);  // first row of this warp's 32
+  const int rows_valid = min(32, p.M - wrow0);
   if constexpr (EPI == kEpiStore16 || EPI == kEpiF32) {
-    constexpr int NCH = BN / 64;  // 32-column chunks per half (4 or 2)
-    const int c0 = half * NCH;
-    uint32_t ra[32], rb[32];
-    tmem_ld32(tacc + c0 * 32, ra);
-    tmem_ld_wait_tied(ra);
+    // this warp's BN/2 columns in slices of 128 bytes per row: 64 16-bit or 32 f32 columns
+    constexpr int ELT = EPI == kEpiF32 ? 4 : 2;
+    constexpr int SLICE = 128 / ELT;
+    constexpr int NSL = BN / 2 / SLICE;
+    const int col0 = n_blk * BN + half * (BN / 2);
+    const size_t ld_bytes = static_cast<size_t>(p.ldc) * ELT;
+    uint8_t* dst0 = reinterpret_cast<uint8_t*>(p.C) + (static_cast<size_t>(wrow0) * p.ldc + col0) * ELT;
+    const uint32_t tbase = tacc + half * (BN / 2);
 #pragma unroll 1
-    for (int c = c0; c < c0 + NCH; c += 2) {
-      tmem_ld32(tacc + (c + 1) * 32, rb);
-      if (live) epi_store_chunk<EPI, T>(p, row, n_blk * BN + c * 32, ra);
-      tmem_ld_wait_tied(rb);
-      if (c + 2 < c0 + NCH) tmem_ld32(tacc + (c + 2) * 32, ra);
-      if (live) epi_store_chunk<EPI, T>(p, row, n_blk * BN + (c + 1) * 32, rb);
-      if (c + 2 < c0 + NCH) tmem_ld_wait_tied(ra);
+    for (int sl = 0; sl < NSL; ++sl) {
+      uint32_t w[32];
+      if constexpr (EPI == kEpiF32) {
+        tmem_ld32(tbase + sl * 32, w);
+        tmem_ld_wait_tied(w);
+      } else {
+        uint32_t ra[32], rb[32];
+        tmem_ld32(tbase + sl * 64, ra);
+        tmem_ld32(tbase + sl * 64 + 32, rb);
+        tmem_ld_wait_tied(ra);
+        tmem_ld_wait_tied(rb);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          w[j] = Half16<T>::pack(u2f(ra[2 * j]), u2f(ra[2 * j + 1]));
+          w[16 + j] = Half16<T>::pack(u2f(rb[2 * j]), u2f(rb[2 * j + 1]));
+        }
+      }
+      stage_words32(stage, w);
+      flush_rows128(stage, dst0 + sl * 128, ld_bytes, rows_valid);
     }
   } else if constexpr (EPI == kEpiGeglu) {
     static_assert(BN == 256, "GeGLU tiles pair 128 gate with 128 up columns");
     const int c0 = half * 4;  // 16-column output chunks [c0, c0 + 4)
     uint32_t ga[16], ua[16], gb[16], ub[16];
+    uint32_t w[32];
+    auto chunk = [&](int c, const uint32_t(&g)[16], const uint32_t(&u)[16]) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        w[(c - c0) * 8 + j] = Half16<T>::pack(geglu_f(u2f(g[2 * j]), u2f(u[2 * j])),
+                                              geglu_f(u2f(g[2 * j + 1]), u2f(u[2 * j + 1])));
+    };
     tmem_ld16(tacc + c0 * 16, ga);
     tmem_ld16(tacc + 128 + c0 * 16, ua);
     tmem_ld_wait_tied16(ga, ua);
-#pragma unroll 1
+#pragma unroll
     for (int c = c0; c < c0 + 4; c += 2) {
       tmem_ld16(tacc + (c + 1) * 16, gb);
       tmem_ld16(tacc + 128 + (c + 1) * 16, ub);
-      if (live) epi_geglu_chunk<T>(p, row, n_blk * 128 + c * 16, ga, ua);
+      chunk(c, ga, ua);
       tmem_ld_wait_tied16(gb, ub);
       if (c + 2 < c0 + 4) {
         tmem_ld16(tacc + (c + 2) * 16, ga);
         tmem_ld16(tacc + 128 + (c + 2) * 16, ua);
       }
-      if (live) epi_geglu_chunk<T>(p, row, n_blk * 128 + (c + 1) * 16, gb, ub);
+      chunk(c + 1, gb, ub);
       if (c + 2 < c0 + 4) tmem_ld_wait_tied16(ga, ua);
     }
+    stage_words32(stage, w);
+    uint8_t* dst0 = reinterpret_cast<uint8_t*>(p.C) +
+                    (static_cast<size_t>(wrow0) * p.ldc + n_blk * 128 + c0 * 16) * sizeof(T);
+    flush_rows128(stage, dst0, static_cast<size_t>(p.ldc) * sizeof(T), rows_valid);
   } else {  // kEpiQkv: this warp owns frequency pairs (i, i + 128), i in [64 half, 64 half + 64)
     static_assert(BN == 256, "QKV tiles are one 256-wide head");
+    const bool live = row < p.M;
     const bool is_q = n_blk < p.n_q_heads;
     const bool is_k = !is_q && n_blk < p.n_q_heads + p.n_kv_heads;
     const float* gain = is_q ? p.q_gain : (is_k ? p.k_gain : nullptr);
@@ -202,30 +223,30 @@ __device__ __forceinline__ bool gemm_epilogue_tile(const GemmParams& p, uint32_t
     const float* cs = p.rope_cos + pos;
     const float* sn = p.rope_sin + pos;
     const size_t fstride = static_cast<size_t>(p.rope_stride);
-    const int c0 = half * 4;  // 16-frequency chunks [c0, c0 + 4)
-    float cva[16], sva[16], cvb[16], svb[16];
-    auto load_tab = [&](int c, float (&cv)[16], float (&sv)[16]) {
+    const int f0 = half * 64;  // this warp's frequencies [f0, f0 + 64), 8 chunks of 8
+    float cva[8], sva[8], cvb[8], svb[8];
+    auto load_tab = [&](int k, float (&cv)[8], float (&sv)[8]) {
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        cv[j] = __ldg(cs + static_cast<size_t>(c * 16 + j) * fstride);
-        sv[j] = __ldg(sn + static_cast<size_t>(c * 16 + j) * fstride);
+      for (int j = 0; j < 8; ++j) {
+        cv[j] = __ldg(cs + static_cast<size_t>(f0 + 8 * k + j) * fstride);
+        sv[j] = __ldg(sn + static_cast<size_t>(f0 + 8 * k + j) * fstride);
       }
     };
-    if (rope) load_tab(c0, cva, sva);  // in flight during pass 1
+    if (rope) load_tab(0, cva, sva);  // in flight during pass 1
     // pass 1: this warp's half of the head's sum of squares (cpu_simd/rmsnorm.rs:13-21)
     float ss = 0.f;
     {
       uint32_t ra[32], rb[32];
-      tmem_ld32(tacc + half * 64, ra);
-      tmem_ld32(tacc + half * 64 + 32, rb);
+      tmem_ld32(tacc + f0, ra);
+      tmem_ld32(tacc + f0 + 32, rb);
       tmem_ld_wait_tied(ra);
       tmem_ld_wait_tied(rb);
 #pragma unroll
       for (int j = 0; j < 32; ++j) ss = fmaf(u2f(ra[j]), u2f(ra[j]), ss);
 #pragma unroll
       for (int j = 0; j < 32; ++j) ss = fmaf(u2f(rb[j]), u2f(rb[j]), ss);
-      tmem_ld32(tacc + 128 + half * 64, ra);
-      tmem_ld32(tacc + 128 + half * 64 + 32, rb);
+      tmem_ld32(tacc + 128 + f0, ra);
+      tmem_ld32(tacc + 128 + f0 + 32, rb);
       tmem_ld_wait_tied(ra);
       tmem_ld_wait_tied(rb);
 #pragma unroll
@@ -237,22 +258,37 @@ __device__ __forceinline__ bool gemm_epilogue_tile(const GemmParams& p, uint32_t
     if (!pair_rendezvous(xbar, xph, abort_flag)) return false;
     ss += red[(half ^ 1) * 128 + row_in_tile];
     const float inv = 1.0f / sqrtf(ss / 256.0f + p.eps);
-    __half* out = reinterpret_cast<__half*>(p.C) + static_cast<size_t>(row) * p.ldc + static_cast<size_t>(n_blk) * 256;
-    // pass 2: 4 chunks of 16 frequency pairs; the next chunk's table values are in flight
-#pragma unroll 1
-    for (int c = c0; c < c0 + 4; c += 2) {
-      uint32_t lo[16], hi[16];
-      if (rope) load_tab(c + 1, cvb, svb);
-      tmem_ld16(tacc + c * 16, lo);
-      tmem_ld16(tacc + 128 + c * 16, hi);
-      tmem_ld_wait_tied16(lo, hi);
-      if (live) epi_qkv_chunk(out, c, inv, gain, rope, lo, hi, cva, sva);
-      if (rope && c + 2 < c0 + 4) load_tab(c + 2, cva, sva);
-      tmem_ld16(tacc + (c + 1) * 16, lo);
-      tmem_ld16(tacc + 128 + (c + 1) * 16, hi);
-      tmem_ld_wait_tied16(lo, hi);
-      if (live) epi_qkv_chunk(out, c + 1, inv, gain, rope, lo, hi, cvb, svb);
+    // pass 2: 8 chunks of 8 frequency pairs; the next chunk's table values are in flight.
+    // The lower halves go straight into the staging tile; the upper halves are parked in
+    // accumulator columns this warp has already consumed (chunk k's 4 words at columns
+    // f0 + 4k, which chunks <= k have read) and staged after the lower slice is out.
+    const uint32_t park = tacc + f0;
+    auto chunk = [&](int k, const float (&cv)[8], const float (&sv)[8]) {
+      uint32_t lo[8], hi[8], plo[4], phi[4];
+      tmem_ld8(tacc + f0 + 8 * k, lo);
+      tmem_ld8(tacc + 128 + f0 + 8 * k, hi);
+      tmem_ld_wait_tied8(lo, hi);
+      epi_qkv_chunk8(f0 + 8 * k, inv, gain, rope, lo, hi, cv, sv, plo, phi);
+      stage_chunk(stage, k, make_uint4(plo[0], plo[1], plo[2], plo[3]));
+      tmem_st4(park + 4 * k, phi);
+    };
+#pragma unroll
+    for (int k = 0; k < 8; k += 2) {
+      if (rope) load_tab(k + 1, cvb, svb);
+      chunk(k, cva, sva);
+      if (rope && k + 2 < 8) load_tab(k + 2, cva, sva);
+      chunk(k + 1, cvb, svb);
     }
+    const size_t ld_bytes = static_cast<size_t>(p.ldc) * 2;
+    uint8_t* dst0 = reinterpret_cast<uint8_t*>(p.C) +
+                    (static_cast<size_t>(wrow0) * p.ldc + static_cast<size_t>(n_blk) * 256 + f0) * 2;
+    flush_rows128(stage, dst0, ld_bytes, rows_valid);
+    uint32_t w[32];
+    tmem_st_wait();
+    tmem_ld32(park, w);
+    tmem_ld_wait_tied(w);
+    stage_words32(stage, w);
+    flush_rows128(stage, dst0 + 256, ld_bytes, rows_valid);
   }
   return true;
 }
@@ -265,8 +301,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                    const GemmParams p) {
   using Cfg = GemmCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  if (smem_u32(smem_raw) & 1023) {  // the swizzled operand tiles need a 1024-byte aligned base
+    if (threadIdx.x == 0) record_error(p.status, kErrBadArgs);
+    return;
+  }
+  uint8_t* smem = smem_raw;
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * Cfg::A_BYTES;
   uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * Cfg::B_BYTES);
@@ -388,6 +428,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int quad = warp & 3;
     const int half = (warp - 2) >> 2;
     const int row_in_tile = quad * 32 + lane;
+    uint8_t* stage = smem + Cfg::STAGE_OFFSET + (warp - 2) * (32 * 128);
     uint32_t xph = 0;
     int ab = 0;
     uint32_t aph = 0;
@@ -405,7 +446,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_after();
       const uint32_t tacc = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(ab * BN);
       if (!gemm_epilogue_tile<BN, EPI, T>(p, tacc, m_blk, n_blk, row_in_tile, half, red + ab * 256, &xbar[quad],
-                                           xph, abort_flag)) {
+                                           xph, abort_flag, stage)) {
         if (lane == 0) {
           record_error(p.status, kErrTimeoutEpilogue);
           *abort_flag = 1;
