@@ -358,6 +358,33 @@ struct Half16<__nv_bfloat16> {
   static __device__ __forceinline__ __nv_bfloat16 from_f32(float v) { return __float2bfloat16_rn(v); }
 };
 
+// ------------------------------------------------------------------------- coalesced row stores
+// Row-per-thread output through a per-warp staging tile: thread `lane` puts its
+// row's 128 bytes into row `lane` (16-byte chunks swizzled by the row, conflict-free), then
+// the warp writes the 32 rows out 4 at a time, 128 contiguous bytes each (a store instruction
+// covers 4 full lines instead of 32 partial ones).
+__device__ __forceinline__ void stage_chunk(uint8_t* stage, int c, uint4 v) {
+  const int lane = threadIdx.x & 31;
+  *reinterpret_cast<uint4*>(stage + lane * 128 + ((c ^ (lane & 7)) << 4)) = v;
+}
+// rows [0, rows_valid) of the staging tile -> dst0 + row * ld_bytes
+__device__ __forceinline__ void flush_rows128(const uint8_t* stage, uint8_t* dst0, size_t ld_bytes, int rows_valid) {
+  const int lane = threadIdx.x & 31;
+  __syncwarp();
+#pragma unroll
+  for (int it = 0; it < 8; ++it) {
+    const int row = it * 4 + (lane >> 3), c = lane & 7;
+    const uint4 v = *reinterpret_cast<const uint4*>(stage + row * 128 + ((c ^ (row & 7)) << 4));
+    if (row < rows_valid) *reinterpret_cast<uint4*>(dst0 + row * ld_bytes + c * 16) = v;
+  }
+  __syncwarp();
+}
+// 32 consecutive 32-bit words (e.g. 64 packed 16-bit outputs) as one staged row
+__device__ __forceinline__ void stage_words32(uint8_t* stage, const uint32_t (&w)[32]) {
+#pragma unroll
+  for (int c = 0; c < 8; ++c) stage_chunk(stage, c, make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]));
+}
+
 // ------------------------------------------------------------------------- packed f32x2 (sm_100)
 // Two f32 lanes in one 64-bit register pair: one instruction for two FMAs / adds / products.
 __device__ __forceinline__ uint64_t f2(float lo, float hi) {

@@ -71,32 +71,6 @@ __device__ __forceinline__ float geglu_f(float g, float u) {
   return g <= -10.0f ? 0.0f : a;
 }
 
-// The epilogue warps write their rows through a per-warp staging tile: thread `lane` puts its
-// row's 128 bytes into row `lane` (16-byte chunks swizzled by the row, conflict-free), then
-// the warp writes the 32 rows out 4 at a time, 128 contiguous bytes each (a store instruction
-// covers 4 full lines instead of 32 partial ones).
-__device__ __forceinline__ void stage_chunk(uint8_t* stage, int c, uint4 v) {
-  const int lane = threadIdx.x & 31;
-  *reinterpret_cast<uint4*>(stage + lane * 128 + ((c ^ (lane & 7)) << 4)) = v;
-}
-// rows [0, rows_valid) of the staging tile -> dst0 + row * ld_bytes
-__device__ __forceinline__ void flush_rows128(const uint8_t* stage, uint8_t* dst0, size_t ld_bytes, int rows_valid) {
-  const int lane = threadIdx.x & 31;
-  __syncwarp();
-#pragma unroll
-  for (int it = 0; it < 8; ++it) {
-    const int row = it * 4 + (lane >> 3), c = lane & 7;
-    const uint4 v = *reinterpret_cast<const uint4*>(stage + row * 128 + ((c ^ (row & 7)) << 4));
-    if (row < rows_valid) *reinterpret_cast<uint4*>(dst0 + row * ld_bytes + c * 16) = v;
-  }
-  __syncwarp();
-}
-// 32 consecutive 32-bit words (e.g. 64 packed 16-bit outputs) as one staged row
-__device__ __forceinline__ void stage_words32(uint8_t* stage, const uint32_t (&w)[32]) {
-#pragma unroll
-  for (int c = 0; c < 8; ++c) stage_chunk(stage, c, make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]));
-}
-
 // 8 frequency pairs (i, i + 128), i = f0 .. f0 + 7, of one head row: RMS scale, gain, NeoX
 // RoPE; f16 pairs of the lower (x1) and upper (x2) halves into plo / phi.
 __device__ __forceinline__ void epi_qkv_chunk8(int f0, float inv, const float* gain, bool rope,
