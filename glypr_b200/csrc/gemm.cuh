@@ -443,4 +443,215 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------- CTA-pair GEMM
+// The same GEMM on pairs of SMs (cluster of 2, tcgen05.mma.cta_group::2): a pair computes a
+// 256 x 256 tile, each CTA loading its 128 rows of A and 128 of the 256 B rows per K step and
+// holding its 128 accumulator rows.  Per SM and K step that is 32 KB instead of the 48 KB of a
+// 128 x 256 tile of its own, so the same 192 KB of stages cover 6 K steps of load latency
+// instead of 4.  Roles per CTA as above; the MMA warp of the leader (rank 0) issues for both,
+// signals both CTAs' empty / tfull barriers (one commit per CTA, no multicast), and owns the
+// tempty barriers that the epilogue warps of both CTAs release.  The loads of both CTAs
+// complete on the leader's full barriers (its producer expects the bytes of both).
+struct GemmPairCfg {
+  static constexpr int BM = 128;  // rows per CTA (256 per pair)
+  static constexpr int BN = 256;  // columns per pair tile; each CTA loads 128 rows of B
+  static constexpr int BK = 64;
+  static constexpr int STAGES = 6;
+  static constexpr uint32_t A_BYTES = 128 * BK * 2;
+  static constexpr uint32_t B_BYTES = 128 * BK * 2;
+  static constexpr uint32_t TMEM_COLS = 2 * BN;
+  static constexpr uint32_t RED_OFFSET = 512;
+  static constexpr uint32_t RED_BYTES = 2 * 2 * 128 * 4;
+  static constexpr uint32_t STAGE_OFFSET = STAGES * (A_BYTES + B_BYTES) + RED_OFFSET + RED_BYTES;
+  static constexpr uint32_t STAGE_BYTES = 8 * 32 * 128;
+  static constexpr size_t SMEM = STAGE_OFFSET + STAGE_BYTES;
+};
+
+// p.m_tiles counts 256-row pair tiles here.
+template <int EPI, typename T>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const GemmParams p) {
+  using Cfg = GemmPairCfg;
+  constexpr int STAGES = Cfg::STAGES;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // (the same for both CTAs of the pair, so both leave before any cluster-wide step)
+  if (smem_u32(smem_raw) & 1023) {
+    if (threadIdx.x == 0) record_error(p.status, kErrBadArgs);
+    return;
+  }
+  uint8_t* smem = smem_raw;
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * Cfg::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * Cfg::B_BYTES);  // used in the leader
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;  // used in the leader: 8 local + 8 peer epilogue warps
+  uint64_t* drain = tempty + 2;
+  uint64_t* xbar = drain + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xbar + 4);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* red = reinterpret_cast<float*>(sB + STAGES * Cfg::B_BYTES + Cfg::RED_OFFSET);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = static_cast<int>(cluster_id_x());
+  const int n_pairs = static_cast<int>(n_clusters_x());
+  const int num_tiles = p.m_tiles * p.n_tiles;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 16);
+    }
+    mbar_init(drain, 1);
+    for (int q = 0; q < 4; ++q) mbar_init(&xbar[q], 2);
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {  // the same warp in both CTAs allocates the pair's tensor memory
+    tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  // barriers of both CTAs initialised and tensor memory allocated before anyone uses them
+  tc_fence_before();
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ TMA producer (both CTAs)
+      int s = 0;
+      uint32_t ph = 0;
+      for (int tile = pair; tile < num_tiles && !*abort_flag; tile += n_pairs) {
+        const int m_blk = tile / p.n_tiles, n_blk = tile % p.n_tiles;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) {
+            record_error(p.status, kErrTimeoutProducer);
+            *abort_flag = 1;
+            break;
+          }
+          if (leader) mbar_arrive_expect_tx(&full[s], 2 * (Cfg::A_BYTES + Cfg::B_BYTES));
+          const uint32_t fbar = mapa_shared(smem_u32(&full[s]), 0);
+          tma_load_2d_pair(sA + s * Cfg::A_BYTES, &tmA, fbar, kb * Cfg::BK, m_blk * 256 + static_cast<int>(rank) * 128);
+          tma_load_2d_pair(sB + s * Cfg::B_BYTES, &tmB, fbar, kb * Cfg::BK, n_blk * 256 + static_cast<int>(rank) * 128);
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ------------------------------------------------------------ MMA issuer (leader only)
+      constexpr uint32_t idesc = idesc_f16(256, Cfg::BN, Half16<T>::kIsBf16);
+      int s = 0;
+      uint32_t ph = 0;
+      int ab = 0;
+      uint32_t aph = 0;
+      bool issued = false;
+      for (int tile = pair; tile < num_tiles && !*abort_flag; tile += n_pairs) {
+        if (!mbar_wait(&tempty[ab], aph ^ 1, abort_flag)) {
+          record_error(p.status, kErrTimeoutMma);
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(ab * Cfg::BN);
+        bool ok = true;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&full[s], ph, abort_flag)) {
+            record_error(p.status, kErrTimeoutMma);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t adesc = desc_kmajor_sw128(smem_u32(sA + s * Cfg::A_BYTES));
+          const uint64_t bdesc = desc_kmajor_sw128(smem_u32(sB + s * Cfg::B_BYTES));
+#pragma unroll
+          for (int k = 0; k < Cfg::BK / 16; ++k)
+            umma_f16_pair(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
+          issued = true;
+          umma_commit_pair(smem_u32(&empty[s]));                  // this CTA's stage
+          umma_commit_pair(mapa_shared(smem_u32(&empty[s]), 1));  // the peer's stage
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(smem_u32(&tfull[ab]));
+        umma_commit_pair(mapa_shared(smem_u32(&tfull[ab]), 1));
+        ab ^= 1;
+        if (ab == 0) aph ^= 1;
+      }
+      if (issued) {
+        // every MMA (which writes both CTAs' tensor memory) retires before the pair leaves
+        umma_commit_pair(smem_u32(drain));
+        if (!mbar_wait(drain, 0, abort_flag) && !*abort_flag) record_error(p.status, kErrTimeoutDrain);
+      }
+    }
+  } else {
+    // -------------------------------------------------------------- epilogue warps (both CTAs)
+    const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int row_in_tile = quad * 32 + lane;
+    uint8_t* stage = smem + Cfg::STAGE_OFFSET + (warp - 2) * (32 * 128);
+    const uint32_t tempty_leader0 = mapa_shared(smem_u32(&tempty[0]), 0);
+    uint32_t xph = 0;
+    int ab = 0;
+    uint32_t aph = 0;
+    for (int tile = pair; tile < num_tiles; tile += n_pairs) {
+      const int m_blk = tile / p.n_tiles, n_blk = tile % p.n_tiles;
+      bool ok = mbar_wait(&tfull[ab], aph, abort_flag);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) {
+        if (lane == 0) {
+          record_error(p.status, kErrTimeoutEpilogue);
+          *abort_flag = 1;
+        }
+        break;
+      }
+      tc_fence_after();
+      const uint32_t tacc =
+          tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(ab * Cfg::BN);
+      // this CTA's 128 rows are 128-row block 2 m_blk + rank
+      if (!gemm_epilogue_tile<256, EPI, T>(p, tacc, 2 * m_blk + static_cast<int>(rank), n_blk, row_in_tile, half,
+                                           red + ab * 256, &xbar[quad], xph, abort_flag, stage)) {
+        if (lane == 0) {
+          record_error(p.status, kErrTimeoutEpilogue);
+          *abort_flag = 1;
+        }
+        break;
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty_leader0 + static_cast<uint32_t>(ab * sizeof(uint64_t)));
+      ab ^= 1;
+      if (ab == 0) aph ^= 1;
+    }
+  }
+
+  // neither CTA leaves (or frees tensor memory) while the other may still touch its shared
+  // memory, barriers or tensor memory
+  tc_fence_before();
+  cluster_sync_all();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
 }  // namespace glp

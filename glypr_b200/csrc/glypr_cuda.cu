@@ -161,6 +161,13 @@ int ensure_kernel_attrs() {
   GLP_CUDA(cudaFuncSetAttribute(glp::gemm_tc_kernel<256, glp::kEpiF32, __nv_bfloat16>, A, s256));
   GLP_CUDA(cudaFuncSetAttribute(glp::gemm_tc_kernel<128, glp::kEpiStore16, __nv_bfloat16>, A, s128));
   GLP_CUDA(cudaFuncSetAttribute(glp::gemm_tc_kernel<128, glp::kEpiF32, __nv_bfloat16>, A, s128));
+  const int sp = static_cast<int>(glp::GemmPairCfg::SMEM);
+  GLP_CUDA(cudaFuncSetAttribute(glp::gemm_pair_kernel<glp::kEpiStore16, __half>, A, sp));
+  GLP_CUDA(cudaFuncSetAttribute(glp::gemm_pair_kernel<glp::kEpiF32, __half>, A, sp));
+  GLP_CUDA(cudaFuncSetAttribute(glp::gemm_pair_kernel<glp::kEpiQkv, __half>, A, sp));
+  GLP_CUDA(cudaFuncSetAttribute(glp::gemm_pair_kernel<glp::kEpiGeglu, __half>, A, sp));
+  GLP_CUDA(cudaFuncSetAttribute(glp::gemm_pair_kernel<glp::kEpiStore16, __nv_bfloat16>, A, sp));
+  GLP_CUDA(cudaFuncSetAttribute(glp::gemm_pair_kernel<glp::kEpiF32, __nv_bfloat16>, A, sp));
   GLP_CUDA(cudaFuncSetAttribute(glp::flash_attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 static_cast<int>(glp::kAttnSmem)));
   GLP_CUDA(cudaFuncSetAttribute(glp::flash_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -178,18 +185,54 @@ int sm_count() {
 
 int bn_for(int n) { return n % 256 == 0 ? 256 : 128; }
 
+// GEMM engine for 256-wide tiles.  Default: CTA pairs for the plain-store epilogues (O, down,
+// head, the kernel-level entry points), whose MMA waits on its loads; one CTA per tile for the
+// fused QKV and GeGLU epilogues, which are bound by their epilogue work and lose when a pair
+// waits for the slower of its two epilogues (measured: O 0.312 -> 0.271 ms, down 0.414 ->
+// 0.371 ms, QKV 0.585 -> 0.624 ms, gate/up 0.906 -> 0.914 ms per 262,144-token launch).
+// GLP_GEMM=pair / single forces one engine for every epilogue.
+bool use_pair_gemm(int epi) {
+  static const int mode = [] {
+    const char* e = std::getenv("GLP_GEMM");
+    if (e && std::string(e) == "single") return 0;
+    if (e && std::string(e) == "pair") return 2;
+    return 1;
+  }();
+  if (mode != 1) return mode == 2;
+  return epi == glp::kEpiStore16 || epi == glp::kEpiF32;
+}
+
 // Launch C = A * B^T with the given epilogue; T is the 16-bit operand type.  `ma` covers
-// A [M, K] (box rows 128), `mb` covers B [N, K] with box rows == bn.
+// A [M, K] (box rows 128), `mb` covers B [N, K] with box rows == bn; `mb_pair` (optional,
+// box rows 128) lets 256-wide tiles run on CTA pairs.
 template <typename T>
-int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, int bn, int epi, GemmParams p, cudaStream_t st) {
+int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, int bn, int epi, GemmParams p, cudaStream_t st,
+                const CUtensorMap* mb_pair = nullptr) {
   p.m_tiles = (p.M + 127) / 128;
   p.n_tiles = p.N / bn;
   p.k_blocks = p.K / 64;
   if (p.M <= 0) return GLP_OK;
   if (p.K % 64 || p.N % bn || p.K <= 0) return fail(GLP_ERR_INVALID_ARG, "GEMM needs K % 64 == 0 and N % tile == 0");
+  const bool f16 = std::is_same<T, __half>::value;
+  if (bn == 256 && mb_pair && use_pair_gemm(epi)) {
+    if ((epi == glp::kEpiQkv || epi == glp::kEpiGeglu) && !f16)
+      return fail(GLP_ERR_INVALID_ARG, "fused epilogues run on f16 operands");
+    p.m_tiles = (p.M + 255) / 256;  // 256-row pair tiles
+    const int pairs = std::min(p.m_tiles * p.n_tiles, sm_count() / 2);
+    const size_t smem = glp::GemmPairCfg::SMEM;
+    const dim3 grid(static_cast<unsigned>(2 * pairs));
+    switch (epi) {
+      case glp::kEpiStore16: glp::gemm_pair_kernel<glp::kEpiStore16, T><<<grid, glp::kGemmThreads, smem, st>>>(ma, *mb_pair, p); break;
+      case glp::kEpiF32: glp::gemm_pair_kernel<glp::kEpiF32, T><<<grid, glp::kGemmThreads, smem, st>>>(ma, *mb_pair, p); break;
+      case glp::kEpiQkv: glp::gemm_pair_kernel<glp::kEpiQkv, __half><<<grid, glp::kGemmThreads, smem, st>>>(ma, *mb_pair, p); break;
+      case glp::kEpiGeglu: glp::gemm_pair_kernel<glp::kEpiGeglu, __half><<<grid, glp::kGemmThreads, smem, st>>>(ma, *mb_pair, p); break;
+      default: return fail(GLP_ERR_INVALID_ARG, "bad epilogue");
+    }
+    GLP_CUDA(cudaGetLastError());
+    return GLP_OK;
+  }
   const int tiles = p.m_tiles * p.n_tiles;
   const int grid = std::min(tiles, sm_count());
-  const bool f16 = std::is_same<T, __half>::value;
   if (bn == 256) {
     const size_t smem = glp::GemmCfg<256>::SMEM;
     switch (epi) {
@@ -351,12 +394,13 @@ struct LayerW {
   float layer_scalar = 1.0f;
   bool sliding = true;
   CUtensorMap m_qkv, m_o, m_gu, m_down;
+  CUtensorMap p_qkv, p_o, p_gu, p_down;  // the same weights, 128-row boxes for CTA pairs
 };
 
 struct HeadW {
   __half* w = nullptr;
   int n = 0, k = 0, bn = 256;
-  CUtensorMap map;
+  CUtensorMap map, map_pair;
 };
 
 struct Device {
@@ -649,6 +693,10 @@ int setup_device(Device& d, const Config& c, const glp::GgufFile& g, int64_t cap
     GLP_TRY(make_map16(&L.m_o, L.o, H, AW, AW, bn_for(H), true));
     GLP_TRY(make_map16(&L.m_gu, L.gu, 2 * F, H, H, 256, true));
     GLP_TRY(make_map16(&L.m_down, L.down, H, F, F, bn_for(H), true));
+    GLP_TRY(make_map16(&L.p_qkv, L.qkv, QKV, H, H, 128, true));
+    GLP_TRY(make_map16(&L.p_o, L.o, H, AW, AW, 128, true));
+    GLP_TRY(make_map16(&L.p_gu, L.gu, 2 * F, H, H, 128, true));
+    GLP_TRY(make_map16(&L.p_down, L.down, H, F, F, 128, true));
   }
   GLP_TRY(upload_gain(d, g, "output_norm.weight", H, &d.out_norm));
   // dense head: dense.0 .. dense.N (BASELINE two-stage 768->3072->768), else output.weight
@@ -665,6 +713,7 @@ int setup_device(Device& d, const Config& c, const glp::GgufFile& g, int64_t cap
     GLP_TRY(d.alloc(&hw.w, static_cast<size_t>(hw.n) * hw.k));
     GLP_TRY(upload_linear(d, g, nm, hw.n, hw.k, hw.w, 0, 0, 0, staging, staging_bytes));
     GLP_TRY(make_map16(&hw.map, hw.w, hw.n, hw.k, hw.k, hw.bn, true));
+    GLP_TRY(make_map16(&hw.map_pair, hw.w, hw.n, hw.k, hw.k, 128, true));
     d.head.push_back(hw);
     prev = hw.n;
   }
@@ -679,6 +728,7 @@ int setup_device(Device& d, const Config& c, const glp::GgufFile& g, int64_t cap
     GLP_TRY(d.alloc(&hw.w, static_cast<size_t>(hw.n) * hw.k));
     GLP_TRY(upload_linear(d, g, "output.weight", hw.n, hw.k, hw.w, 0, 0, 0, staging, staging_bytes));
     GLP_TRY(make_map16(&hw.map, hw.w, hw.n, hw.k, hw.k, hw.bn, true));
+    GLP_TRY(make_map16(&hw.map_pair, hw.w, hw.n, hw.k, hw.k, 128, true));
     d.head.push_back(hw);
   }
   if (d.head.back().n != c.emb_out) return fail(GLP_ERR_FORMAT, "head output dim != embedding_length_out");
@@ -772,7 +822,7 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
       p.n_kv_heads = c.n_kv;
       p.eps = eps;
       GLP_TRY(prof_launch(d, st, kProfGemmQkv, gemm_flops(Td, QKV, H), gemm_bytes(Td, QKV, H, 2.0),
-                          [&] { return launch_gemm<__half>(m_x, L.m_qkv, 256, glp::kEpiQkv, p, st); }));
+                          [&] { return launch_gemm<__half>(m_x, L.m_qkv, 256, glp::kEpiQkv, p, st, &L.p_qkv); }));
       // attention
       const double pairs = L.sliding ? pairs_local : pairs_global;
       GLP_TRY(prof_launch(d, st, kProfAttention, 4.0 * D * c.n_heads * pairs, attn_bytes, [&] {
@@ -788,7 +838,7 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
       po.ldc = H;
       po.status = d.status;
       GLP_TRY(prof_launch(d, st, kProfGemmO, gemm_flops(Td, H, AW), gemm_bytes(Td, H, AW, 2.0),
-                          [&] { return launch_gemm<__half>(m_attn, L.m_o, bn_for(H), glp::kEpiStore16, po, st); }));
+                          [&] { return launch_gemm<__half>(m_attn, L.m_o, bn_for(H), glp::kEpiStore16, po, st, &L.p_o); }));
       GLP_TRY(prof_launch(d, st, kProfPostNorm, 0.0, post_bytes, [&] {
         glp::post_norm_residual_kernel<false><<<rows_grid, 256, 0, st>>>(d.y, d.h, L.post_attn, 1.0f, L.ffn_norm,
                                                                          eps, T, d.x, nullptr);
@@ -805,7 +855,7 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
       pg.status = d.status;
       GLP_TRY(prof_launch(d, st, kProfGemmGateUp, gemm_flops(Td, 2.0 * F, H),
                           2.0 * Td * H + 2.0 * 2.0 * F * H + 2.0 * Td * F,
-                          [&] { return launch_gemm<__half>(m_x, L.m_gu, 256, glp::kEpiGeglu, pg, st); }));
+                          [&] { return launch_gemm<__half>(m_x, L.m_gu, 256, glp::kEpiGeglu, pg, st, &L.p_gu); }));
       // down projection
       GemmParams pd{};
       pd.M = T;
@@ -815,7 +865,7 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
       pd.ldc = H;
       pd.status = d.status;
       GLP_TRY(prof_launch(d, st, kProfGemmDown, gemm_flops(Td, H, F), gemm_bytes(Td, H, F, 2.0),
-                          [&] { return launch_gemm<__half>(m_a, L.m_down, bn_for(H), glp::kEpiStore16, pd, st); }));
+                          [&] { return launch_gemm<__half>(m_a, L.m_down, bn_for(H), glp::kEpiStore16, pd, st, &L.p_down); }));
       const bool last = l + 1 == c.n_layers;
       GLP_TRY(prof_launch(d, st, kProfPostNorm, 0.0, last ? Td * 8.0 * H : post_bytes, [&] {
         if (!last)
@@ -851,7 +901,7 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
     ph.status = d.status;
     GLP_TRY(prof_launch(d, st, kProfHeadGemm, gemm_flops(n_seq, hw.n, hw.k),
                         gemm_bytes(n_seq, hw.n, hw.k, last ? 4.0 : 2.0),
-                        [&] { return launch_gemm<__half>(m_in, hw.map, hw.bn, last ? glp::kEpiF32 : glp::kEpiStore16, ph, st); }));
+                        [&] { return launch_gemm<__half>(m_in, hw.map, hw.bn, last ? glp::kEpiF32 : glp::kEpiStore16, ph, st, &hw.map_pair); }));
     cur = static_cast<const __half*>(ph.C);
     cur_k = hw.n;
   }
@@ -988,9 +1038,10 @@ int run_bf16_gemm(const __nv_bfloat16* w, int N, int K, const void* x, int M, vo
   GLP_TRY(device_status_word(dev, &status));
   if (M == 0) return GLP_OK;
   const int bn = bn_for(N);
-  CUtensorMap ma, mb;
+  CUtensorMap ma, mb, mbp;
   GLP_TRY(make_map16(&ma, x, M, K, K, 128, false));
   GLP_TRY(make_map16(&mb, w, N, K, K, bn, false));
+  GLP_TRY(make_map16(&mbp, w, N, K, K, 128, false));
   GemmParams p{};
   p.M = M;
   p.N = N;
@@ -998,7 +1049,7 @@ int run_bf16_gemm(const __nv_bfloat16* w, int N, int K, const void* x, int M, vo
   p.C = y;
   p.ldc = N;
   p.status = status;
-  return launch_gemm<__nv_bfloat16>(ma, mb, bn, y_is_f32 ? glp::kEpiF32 : glp::kEpiStore16, p, st);
+  return launch_gemm<__nv_bfloat16>(ma, mb, bn, y_is_f32 ? glp::kEpiF32 : glp::kEpiStore16, p, st, &mbp);
 }
 
 }  // namespace

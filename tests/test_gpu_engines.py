@@ -1,0 +1,89 @@
+"""Both GEMM engines produce the same results.
+
+The library runs 256-wide GEMM tiles either on CTA pairs (tcgen05.mma.cta_group::2, the
+default for the plain-store epilogues) or on one CTA per tile (the default for the fused QKV
+and GeGLU epilogues); GLP_GEMM=pair / single forces one engine everywhere.  The engine is
+chosen once per process, so each engine runs in a child process here, and the tests compare:
+
+* the kernel-level GEMM (f32 and bf16 outputs, M tails) against the f32 product;
+* the whole forward of the small conditioned model: both forced engines against the
+  default mix (the engines round identically: f32 accumulation in the same K order).
+"""
+from __future__ import annotations
+
+import os
+import subprocess
+import sys
+import textwrap
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+GEMM_SCRIPT = textwrap.dedent("""
+    import sys, numpy as np, torch
+    from glypr_b200 import api
+    out = sys.argv[1]
+    res = {}
+    rng = np.random.default_rng(5)
+    for (m, n, k) in [(300, 768, 1152), (1000, 2304, 768), (64, 256, 64)]:
+        w = torch.from_numpy((rng.standard_normal((n, k)) * 0.05).astype(np.float32)).to(torch.bfloat16).cuda()
+        x = torch.from_numpy(rng.standard_normal((m, k)).astype(np.float32)).to(torch.bfloat16).cuda()
+        for f32 in (True, False):
+            y = torch.full((m, n), float("nan"), device="cuda", dtype=torch.float32 if f32 else torch.bfloat16)
+            api.bf16_gemm(w.data_ptr(), n, k, x.data_ptr(), m, y.data_ptr(), f32)
+            torch.cuda.synchronize()
+            res[f"y_{m}_{n}_{k}_{int(f32)}"] = y.float().cpu().numpy()
+            res[f"ref_{m}_{n}_{k}"] = (x.double() @ w.double().T).cpu().numpy()
+    np.savez(out, **res)
+""")
+
+MODEL_SCRIPT = textwrap.dedent("""
+    import sys, numpy as np
+    from glypr_b200 import api, synth
+    path, out = sys.argv[1], sys.argv[2]
+    with api.GlyprEmbedder.load_gguf(path, [0]) as emb:
+        ids, lens = synth.make_batch(5, 600, emb.info.vocab, lengths=[600, 257, 31, 512, 1])
+        np.save(out, emb.embed_tokens(ids, lens))
+""")
+
+
+def _run(script, args, engine, tmp_path):
+    env = dict(os.environ)
+    if engine is None:
+        env.pop("GLP_GEMM", None)
+    else:
+        env["GLP_GEMM"] = engine
+    env["PYTHONPATH"] = ROOT + os.pathsep + env.get("PYTHONPATH", "")
+    r = subprocess.run([sys.executable, "-c", script, *args], env=env, cwd=ROOT, capture_output=True, text=True,
+                       timeout=600)
+    assert r.returncode == 0, r.stdout + r.stderr
+
+
+@pytest.mark.parametrize("engine", ["pair", "single"])
+def test_gemm_engine_matches_f32_product(engine, tmp_path):
+    out = str(tmp_path / f"gemm_{engine}.npz")
+    _run(GEMM_SCRIPT, [out], engine, tmp_path)
+    d = np.load(out)
+    for key in d.files:
+        if not key.startswith("y_"):
+            continue
+        _, m, n, k, f32 = key.split("_")
+        got = d[key].astype(np.float64)
+        ref = d[f"ref_{m}_{n}_{k}"]
+        assert np.isfinite(got).all(), key
+        tol = 2e-5 if f32 == "1" else 8e-3  # f32 accumulation; bf16 output rounding
+        assert np.abs(got - ref).max() <= tol * np.abs(ref).max(), key
+
+
+def test_model_forward_identical_across_engines(small_cond_gguf, tmp_path):
+    outs = {}
+    for engine in (None, "pair", "single"):
+        out = str(tmp_path / f"emb_{engine}.npy")
+        _run(MODEL_SCRIPT, [small_cond_gguf, out], engine, tmp_path)
+        outs[engine] = np.load(out)
+    for engine in ("pair", "single"):
+        np.testing.assert_array_equal(outs[engine], outs[None])
