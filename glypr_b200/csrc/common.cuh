@@ -103,7 +103,7 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
 }
 
 // 2-D tiled bulk tensor load global -> shared, completion signalled on `bar` (tx bytes).
-// No cluster multicast: every CTA fetches its own tiles.
+// Every CTA fetches its own tiles into its own shared memory.
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int x,
                                             int y) {
   asm volatile(
@@ -362,7 +362,7 @@ struct Half16<__nv_bfloat16> {
 // A cluster of two CTAs on two SMs computes one 256-row tile: rank 0 (the leader) issues the
 // MMAs for both, each CTA holds its 128 rows of A and half of B in its own shared memory and
 // its 128 accumulator rows in its own tensor memory.  Shared-memory addresses of the other CTA
-// come from mapa; no load or commit is multicast.
+// come from mapa; every load and commit names exactly one destination CTA.
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));

@@ -449,7 +449,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // holding its 128 accumulator rows.  Per SM and K step that is 32 KB instead of the 48 KB of a
 // 128 x 256 tile of its own, so the same 192 KB of stages cover 6 K steps of load latency
 // instead of 4.  Roles per CTA as above; the MMA warp of the leader (rank 0) issues for both,
-// signals both CTAs' empty / tfull barriers (one commit per CTA, no multicast), and owns the
+// signals both CTAs' empty / tfull barriers (one commit per destination CTA), and owns the
 // tempty barriers that the epilogue warps of both CTAs release.  The loads of both CTAs
 // complete on the leader's full barriers (its producer expects the bytes of both).
 struct GemmPairCfg {
