@@ -34,8 +34,7 @@ struct GemmParams {
   // kEpiQkv
   const float* q_gain;    // [head_dim]
   const float* k_gain;    // [head_dim]
-  const float* rope_cos;  // [head_dim/2, rope_stride] frequency-major (the table's halves are equal)
-  const float* rope_sin;  // [head_dim/2, rope_stride]
+  const float2* rope_cs;  // [head_dim/2, rope_stride] {cos, sin}, frequency-major
   const int* pos;         // [M] position of each row inside its sequence
   int rope_stride;        // positions per frequency row (the model's context length)
   int n_q_heads, n_kv_heads;
@@ -193,17 +192,18 @@ __device__ __forceinline__ bool gemm_epilogue_tile(const GemmParams& p, uint32_t
     const float* gain = is_q ? p.q_gain : (is_k ? p.k_gain : nullptr);
     const bool rope = is_q || is_k;
     const int pos = live ? p.pos[row] : 0;
-    // frequency-major tables: lanes (consecutive rows) read consecutive positions
-    const float* cs = p.rope_cos + pos;
-    const float* sn = p.rope_sin + pos;
+    // frequency-major {cos, sin} table: lanes (consecutive rows) read consecutive positions,
+    // one 8-byte load per frequency
+    const float2* tab = p.rope_cs + pos;
     const size_t fstride = static_cast<size_t>(p.rope_stride);
     const int f0 = half * 64;  // this warp's frequencies [f0, f0 + 64), 8 chunks of 8
     float cva[8], sva[8], cvb[8], svb[8];
     auto load_tab = [&](int k, float (&cv)[8], float (&sv)[8]) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        cv[j] = __ldg(cs + static_cast<size_t>(f0 + 8 * k + j) * fstride);
-        sv[j] = __ldg(sn + static_cast<size_t>(f0 + 8 * k + j) * fstride);
+        const float2 t = __ldg(tab + static_cast<size_t>(f0 + 8 * k + j) * fstride);
+        cv[j] = t.x;
+        sv[j] = t.y;
       }
     };
     if (rope) load_tab(0, cva, sva);  // in flight during pass 1
@@ -236,22 +236,32 @@ __device__ __forceinline__ bool gemm_epilogue_tile(const GemmParams& p, uint32_t
     // The lower halves go straight into the staging tile; the upper halves are parked in
     // accumulator columns this warp has already consumed (chunk k's 4 words at columns
     // f0 + 4k, which chunks <= k have read) and staged after the lower slice is out.
+    // The next chunk's accumulator columns are loaded while this chunk is converted (none of
+    // the parked columns is read again).
     const uint32_t park = tacc + f0;
-    auto chunk = [&](int k, const float (&cv)[8], const float (&sv)[8]) {
-      uint32_t lo[8], hi[8], plo[4], phi[4];
+    uint32_t loA[8], hiA[8], loB[8], hiB[8];
+    auto issue = [&](int k, uint32_t (&lo)[8], uint32_t (&hi)[8]) {
       tmem_ld8(tacc + f0 + 8 * k, lo);
       tmem_ld8(tacc + 128 + f0 + 8 * k, hi);
-      tmem_ld_wait_tied8(lo, hi);
+    };
+    auto finish = [&](int k, const uint32_t (&lo)[8], const uint32_t (&hi)[8], const float (&cv)[8],
+                      const float (&sv)[8]) {
+      uint32_t plo[4], phi[4];
       epi_qkv_chunk8(f0 + 8 * k, inv, gain, rope, lo, hi, cv, sv, plo, phi);
       stage_chunk(stage, k, make_uint4(plo[0], plo[1], plo[2], plo[3]));
       tmem_st4(park + 4 * k, phi);
     };
+    issue(0, loA, hiA);
 #pragma unroll
     for (int k = 0; k < 8; k += 2) {
       if (rope) load_tab(k + 1, cvb, svb);
-      chunk(k, cva, sva);
+      tmem_ld_wait_tied8(loA, hiA);
+      issue(k + 1, loB, hiB);
+      finish(k, loA, hiA, cva, sva);
       if (rope && k + 2 < 8) load_tab(k + 2, cva, sva);
-      chunk(k + 1, cvb, svb);
+      tmem_ld_wait_tied8(loB, hiB);
+      if (k + 2 < 8) issue(k + 2, loA, hiA);
+      finish(k + 1, loB, hiB, cvb, svb);
     }
     const size_t ld_bytes = static_cast<size_t>(p.ldc) * 2;
     uint8_t* dst0 = reinterpret_cast<uint8_t*>(p.C) +

@@ -413,7 +413,7 @@ struct Device {
   std::vector<LayerW> layers;
   float* out_norm = nullptr;
   std::vector<HeadW> head;
-  float *cos_swa = nullptr, *sin_swa = nullptr, *cos_full = nullptr, *sin_full = nullptr;
+  float2 *cs_swa = nullptr, *cs_full = nullptr;  // RoPE tables (sliding / global layers)
   int64_t cap_tokens = 0;
   int cap_seqs = 0;
   __nv_bfloat16* h = nullptr;  // residual stream
@@ -601,20 +601,20 @@ int upload_linear(Device& d, const glp::GgufFile& g, const std::string& name, in
 // freqs = f32(pos) * inv_freq (f32), cos/sin in f32.  Only the first half is stored (the
 // reference table is cat(freqs, freqs)), frequency-major [half][max_pos] so that the GEMM
 // epilogue's 32 lanes (consecutive rows = consecutive positions) read one coalesced line.
-int upload_rope(Device& d, double theta, int d_head, int max_pos, float** cs, float** sn) {
+// RoPE table, frequency-major with cos and sin of one (frequency, position) side by side:
+// cs[i * max_pos + p] = {cos(p * inv_freq_i), sin(p * inv_freq_i)} (rope.rs:14-76 values)
+int upload_rope(Device& d, double theta, int d_head, int max_pos, float2** cs) {
   const int half = d_head / 2;
-  std::vector<float> inv(half), c(static_cast<size_t>(max_pos) * half), s(static_cast<size_t>(max_pos) * half);
+  std::vector<float> inv(half);
+  std::vector<float2> c(static_cast<size_t>(max_pos) * half);
   for (int i = 0; i < half; ++i) inv[i] = static_cast<float>(1.0 / std::pow(theta, (2.0 * i) / d_head));
   for (int i = 0; i < half; ++i)
     for (int p = 0; p < max_pos; ++p) {
       const float f = static_cast<float>(p) * inv[i];
-      c[static_cast<size_t>(i) * max_pos + p] = std::cos(f);
-      s[static_cast<size_t>(i) * max_pos + p] = std::sin(f);
+      c[static_cast<size_t>(i) * max_pos + p] = make_float2(std::cos(f), std::sin(f));
     }
   GLP_TRY(d.alloc(cs, c.size()));
-  GLP_TRY(d.alloc(sn, s.size()));
-  GLP_CUDA(cudaMemcpy(*cs, c.data(), c.size() * 4, cudaMemcpyHostToDevice));
-  GLP_CUDA(cudaMemcpy(*sn, s.data(), s.size() * 4, cudaMemcpyHostToDevice));
+  GLP_CUDA(cudaMemcpy(*cs, c.data(), c.size() * sizeof(float2), cudaMemcpyHostToDevice));
   return GLP_OK;
 }
 
@@ -732,8 +732,8 @@ int setup_device(Device& d, const Config& c, const glp::GgufFile& g, int64_t cap
     d.head.push_back(hw);
   }
   if (d.head.back().n != c.emb_out) return fail(GLP_ERR_FORMAT, "head output dim != embedding_length_out");
-  GLP_TRY(upload_rope(d, c.theta_swa, D, c.max_pos, &d.cos_swa, &d.sin_swa));
-  GLP_TRY(upload_rope(d, c.theta_full, D, c.max_pos, &d.cos_full, &d.sin_full));
+  GLP_TRY(upload_rope(d, c.theta_swa, D, c.max_pos, &d.cs_swa));
+  GLP_TRY(upload_rope(d, c.theta_full, D, c.max_pos, &d.cs_full));
 
   // activations for one launch chunk
   d.cap_tokens = cap_tokens;
@@ -814,8 +814,7 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
       p.ldc = QKV;
       p.q_gain = L.q_norm;
       p.k_gain = L.k_norm;
-      p.rope_cos = L.sliding ? d.cos_swa : d.cos_full;
-      p.rope_sin = L.sliding ? d.sin_swa : d.sin_full;
+      p.rope_cs = L.sliding ? d.cs_swa : d.cs_full;
       p.pos = d.pos;
       p.rope_stride = c.max_pos;
       p.n_q_heads = c.n_heads;
