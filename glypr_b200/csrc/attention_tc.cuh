@@ -504,17 +504,30 @@ __global__ void __launch_bounds__(kFaThreads, 1)
             break;
           }
           tc_fence_after();
+          // this half's 128 O columns, two 32-column chunks in flight per round (the stores
+          // complete at the wait that follows the P store below)
+          const uint64_t f2x = f2(factor, factor);
 #pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
-            uint32_t o[32];
+          for (int c = 0; c < 4; c += 2) {
+            uint32_t oa[32], ob[32];
             const uint32_t ta = lane_base + kFaTmemO + half * 128 + c * 32;
-            tmem_ld32(ta, o);
-            tmem_ld_wait_tied(o);
+            tmem_ld32(ta, oa);
+            tmem_ld32(ta + 32, ob);
+            tmem_ld_wait_tied(oa);
+            tmem_ld_wait_tied(ob);
 #pragma unroll
-            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(u2f(o[e]) * factor);
-            tmem_st32(ta, o);
+            for (int e = 0; e < 32; e += 2) {
+              float a, b;
+              f2_split(f2_mul(f2(u2f(oa[e]), u2f(oa[e + 1])), f2x), a, b);
+              oa[e] = __float_as_uint(a);
+              oa[e + 1] = __float_as_uint(b);
+              f2_split(f2_mul(f2(u2f(ob[e]), u2f(ob[e + 1])), f2x), a, b);
+              ob[e] = __float_as_uint(a);
+              ob[e + 1] = __float_as_uint(b);
+            }
+            tmem_st32(ta, oa);
+            tmem_st32(ta + 32, ob);
           }
-          tmem_st_wait();
         }
         // P row r, this half's 32 keys: 16 columns of f16 pairs over the S slot
         tmem_st16(lane_base + st * kFaBKV + half * 16, pk);
