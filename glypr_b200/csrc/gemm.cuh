@@ -459,8 +459,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // holding its 128 accumulator rows.  Per SM and K step that is 32 KB instead of the 48 KB of a
 // 128 x 256 tile of its own, so the same 192 KB of stages cover 6 K steps of load latency
 // instead of 4.  Roles per CTA as above; the MMA warp of the leader (rank 0) issues for both,
-// signals both CTAs' empty / tfull barriers (one commit per destination CTA), and owns the
-// tempty barriers that the epilogue warps of both CTAs release.  The loads of both CTAs
+// signals both CTAs' empty / tfull barriers (one commit per destination CTA), and waits on
+// tempty barriers that the epilogue warps of both CTAs release (the peer's through one
+// forwarded arrive: a cluster-scope release by every epilogue warp would make each of them
+// wait for its output stores, which measured 1.8x slower epilogues).  The loads of both CTAs
 // complete on the leader's full barriers (its producer expects the bytes of both).
 struct GemmPairCfg {
   static constexpr int BM = 128;  // rows per CTA (256 per pair)
@@ -496,7 +498,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * Cfg::B_BYTES);  // used in the leader
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
-  uint64_t* tempty = tfull + 2;  // used in the leader: 8 local + 8 peer epilogue warps
+  // accumulator buffer released: in the leader 8 local epilogue warps + 1 arrive forwarded from
+  // the peer; in the peer its 8 epilogue warps (forwarded by its warp 1)
+  uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
   uint64_t* xbar = drain + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xbar + 4);
@@ -518,7 +522,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 16);
+      mbar_init(&tempty[b], leader ? 9 : 8);
     }
     mbar_init(drain, 1);
     for (int q = 0; q < 4; ++q) mbar_init(&xbar[q], 2);
@@ -611,6 +615,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
         umma_commit_pair(smem_u32(drain));
         if (!mbar_wait(drain, 0, abort_flag) && !*abort_flag) record_error(p.status, kErrTimeoutDrain);
       }
+    } else if (lane == 0) {
+      // ------------------------------------------------------------ release forwarder (peer)
+      // The peer's epilogue warps release an accumulator buffer on a barrier of their own CTA
+      // (a CTA-scope arrive does not wait for their output stores); this thread carries that
+      // as one cluster-scope arrive to the leader, whose MMA waits for both CTAs.
+      const uint32_t lead_tempty0 = mapa_shared(smem_u32(&tempty[0]), 0);
+      int ab = 0;
+      uint32_t aph = 0;
+      for (int tile = pair; tile < num_tiles; tile += n_pairs) {
+        if (!mbar_wait(&tempty[ab], aph, abort_flag)) {
+          record_error(p.status, kErrTimeoutEpilogue);
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        tc_fence_before();
+        mbar_arrive_cluster(lead_tempty0 + static_cast<uint32_t>(ab * sizeof(uint64_t)));
+        ab ^= 1;
+        if (ab == 0) aph ^= 1;
+      }
     }
   } else {
     // -------------------------------------------------------------- epilogue warps (both CTAs)
@@ -618,7 +642,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     const int half = (warp - 2) >> 2;
     const int row_in_tile = quad * 32 + lane;
     uint8_t* stage = smem + Cfg::STAGE_OFFSET + (warp - 2) * (32 * 128);
-    const uint32_t tempty_leader0 = mapa_shared(smem_u32(&tempty[0]), 0);
     uint32_t xph = 0;
     int ab = 0;
     uint32_t aph = 0;
@@ -647,7 +670,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(tempty_leader0 + static_cast<uint32_t>(ab * sizeof(uint64_t)));
+      if (lane == 0) mbar_arrive(&tempty[ab]);  // this CTA's barrier (the peer's is forwarded)
       ab ^= 1;
       if (ab == 0) aph ^= 1;
     }
