@@ -155,34 +155,23 @@ __device__ __forceinline__ bool gemm_epilogue_tile(const GemmParams& p, uint32_t
     }
   } else if constexpr (EPI == kEpiGeglu) {
     static_assert(BN == 256, "GeGLU tiles pair 128 gate with 128 up columns");
-    const int c0 = half * 4;  // 16-column output chunks [c0, c0 + 4)
-    uint32_t ga[16], ua[16], gb[16], ub[16];
+    const int c0 = half * 64;  // this warp's 64 outputs: gate columns c0.., up columns 128 + c0..
     uint32_t w[32];
-    auto chunk = [&](int c, const uint32_t(&g)[16], const uint32_t(&u)[16]) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j)
-        w[(c - c0) * 8 + j] = Half16<T>::pack(geglu_f(u2f(g[2 * j]), u2f(u[2 * j])),
-                                              geglu_f(u2f(g[2 * j + 1]), u2f(u[2 * j + 1])));
-    };
-    tmem_ld16(tacc + c0 * 16, ga);
-    tmem_ld16(tacc + 128 + c0 * 16, ua);
-    tmem_ld_wait_tied16(ga, ua);
+    for (int hh = 0; hh < 2; ++hh) {  // 32 outputs per round, read as two 32-column loads
+      uint32_t g[32], u[32];
+      tmem_ld32(tacc + c0 + hh * 32, g);
+      tmem_ld32(tacc + 128 + c0 + hh * 32, u);
+      tmem_ld_wait_tied(g);
+      tmem_ld_wait_tied(u);
 #pragma unroll
-    for (int c = c0; c < c0 + 4; c += 2) {
-      tmem_ld16(tacc + (c + 1) * 16, gb);
-      tmem_ld16(tacc + 128 + (c + 1) * 16, ub);
-      chunk(c, ga, ua);
-      tmem_ld_wait_tied16(gb, ub);
-      if (c + 2 < c0 + 4) {
-        tmem_ld16(tacc + (c + 2) * 16, ga);
-        tmem_ld16(tacc + 128 + (c + 2) * 16, ua);
-      }
-      chunk(c + 1, gb, ub);
-      if (c + 2 < c0 + 4) tmem_ld_wait_tied16(ga, ua);
+      for (int j = 0; j < 16; ++j)
+        w[hh * 16 + j] = Half16<T>::pack(geglu_f(u2f(g[2 * j]), u2f(u[2 * j])),
+                                         geglu_f(u2f(g[2 * j + 1]), u2f(u[2 * j + 1])));
     }
     stage_words32(stage, w);
     uint8_t* dst0 = reinterpret_cast<uint8_t*>(p.C) +
-                    (static_cast<size_t>(wrow0) * p.ldc + n_blk * 128 + c0 * 16) * sizeof(T);
+                    (static_cast<size_t>(wrow0) * p.ldc + n_blk * 128 + c0) * sizeof(T);
     flush_rows128(stage, dst0, static_cast<size_t>(p.ldc) * sizeof(T), rows_valid);
   } else {  // kEpiQkv: this warp owns frequency pairs (i, i + 128), i in [64 half, 64 half + 64)
     static_assert(BN == 256, "QKV tiles are one 256-wide head");

@@ -185,18 +185,19 @@ int sm_count() {
 
 int bn_for(int n) { return n % 256 == 0 ? 256 : 128; }
 
-// GEMM engine for 256-wide tiles.  Default: CTA pairs for the plain-store epilogues (O, down,
-// head, the kernel-level entry points), whose MMA waits on its loads; one CTA per tile for the
-// fused QKV and GeGLU epilogues, which are bound by their epilogue work and lose when a pair
-// waits for the slower of its two epilogues (measured: O 0.312 -> 0.271 ms, down 0.414 ->
-// 0.371 ms, QKV 0.585 -> 0.624 ms, gate/up 0.906 -> 0.914 ms per 262,144-token launch).
-// GLP_GEMM=pair / single forces one engine for every epilogue.
+// GEMM engine for 256-wide tiles: CTA pairs (default) or one CTA per tile (GLP_GEMM=single).
+// Per kernel the pair is faster for the plain-store GEMMs (O 0.312 -> 0.269 ms, down 0.414 ->
+// 0.372 ms per 262,144-token launch) and 3-6 % slower in cycles for the fused QKV and GeGLU
+// epilogues; but under the 1 kW power cap the pairs' smaller L2 and shared-memory traffic lets
+// the whole forward run at a higher clock (median 1,447-1,470 vs 1,402-1,410 MHz), and
+// all-pairs gave the higher throughput: 6,141-6,191 vs 6,088-6,127 embeddings/s with pairs for
+// the plain-store GEMMs only.  GLP_GEMM=pair-store keeps that mix.
 bool use_pair_gemm(int epi) {
   static const int mode = [] {
     const char* e = std::getenv("GLP_GEMM");
     if (e && std::string(e) == "single") return 0;
-    if (e && std::string(e) == "pair") return 2;
-    return 1;
+    if (e && std::string(e) == "pair-store") return 1;
+    return 2;
   }();
   if (mode != 1) return mode == 2;
   return epi == glp::kEpiStore16 || epi == glp::kEpiF32;

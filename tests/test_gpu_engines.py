@@ -1,13 +1,13 @@
 """Both GEMM engines produce the same results.
 
-The library runs 256-wide GEMM tiles either on CTA pairs (tcgen05.mma.cta_group::2, the
-default for the plain-store epilogues) or on one CTA per tile (the default for the fused QKV
-and GeGLU epilogues); GLP_GEMM=pair / single forces one engine everywhere.  The engine is
-chosen once per process, so each engine runs in a child process here, and the tests compare:
+The library runs 256-wide GEMM tiles on CTA pairs (tcgen05.mma.cta_group::2, the default) or on
+one CTA per tile; GLP_GEMM=single forces the latter everywhere and GLP_GEMM=pair-store uses
+pairs for the plain-store epilogues only.  The engine is chosen once per process, so each
+engine runs in a child process here, and the tests compare:
 
 * the kernel-level GEMM (f32 and bf16 outputs, M tails) against the f32 product;
-* the whole forward of the small conditioned model: both forced engines against the
-  default mix (the engines round identically: f32 accumulation in the same K order).
+* the whole forward of the small conditioned model under every engine choice (the engines
+  round identically: f32 accumulation in the same K order).
 """
 from __future__ import annotations
 
@@ -81,9 +81,9 @@ def test_gemm_engine_matches_f32_product(engine, tmp_path):
 
 def test_model_forward_identical_across_engines(small_cond_gguf, tmp_path):
     outs = {}
-    for engine in (None, "pair", "single"):
+    for engine in (None, "pair-store", "single"):
         out = str(tmp_path / f"emb_{engine}.npy")
         _run(MODEL_SCRIPT, [small_cond_gguf, out], engine, tmp_path)
         outs[engine] = np.load(out)
-    for engine in ("pair", "single"):
+    for engine in ("pair-store", "single"):
         np.testing.assert_array_equal(outs[engine], outs[None])
