@@ -426,6 +426,7 @@ struct Device {
   __half* a = nullptr;
   int* pos = nullptr;
   __half* pooled = nullptr;
+  float* pool_part = nullptr;  // per-segment sums of sequences longer than one pooling segment
   __half* mid = nullptr;
   float* emb = nullptr;
   int* status = nullptr;
@@ -444,6 +445,18 @@ struct Device {
   size_t prof_used = 0;
   std::array<int64_t, GLP_PROFILE_KINDS> prof_launch{};
   std::array<double, GLP_PROFILE_KINDS> prof_flops{}, prof_bytes{};
+  // instantiated CUDA graphs of launch chunks, keyed by everything that reaches a kernel
+  // parameter (see run_packed); each keeps the launch counters its capture added, which every
+  // replay adds again
+  struct ChunkGraph {
+    std::array<int64_t, 8> key{};
+    cudaGraphExec_t exec = nullptr;
+    std::array<int64_t, GLP_PROFILE_KINDS> launches{};
+    std::array<double, GLP_PROFILE_KINDS> flops{}, bytes{};
+    uint64_t last_use = 0;
+  };
+  std::vector<ChunkGraph> graphs;
+  uint64_t graph_clock = 0;
 
   template <class T>
   int alloc(T** p, size_t count) {
@@ -473,6 +486,9 @@ struct Device {
       cudaEventDestroy(e[1]);
     }
     prof_ev.clear();
+    for (auto& g : graphs)
+      if (g.exec) cudaGraphExecDestroy(g.exec);
+    graphs.clear();
     if (ev0) cudaEventDestroy(ev0);
     if (ev1) cudaEventDestroy(ev1);
     if (stream) cudaStreamDestroy(stream);
@@ -750,6 +766,7 @@ int setup_device(Device& d, const Config& c, const glp::GgufFile& g, int64_t cap
   GLP_TRY(d.alloc(&d.a, static_cast<size_t>(cap_tokens) * F));
   GLP_TRY(d.alloc(&d.pos, static_cast<size_t>(cap_tokens)));
   GLP_TRY(d.alloc(&d.pooled, static_cast<size_t>(cap_seqs) * H));
+  GLP_TRY(d.alloc(&d.pool_part, (static_cast<size_t>(cap_tokens) / glp::kPoolSeg + cap_seqs + 1) * H));
   GLP_TRY(d.alloc(&d.mid, static_cast<size_t>(cap_seqs) * max_head));
   GLP_TRY(d.alloc(&d.emb, static_cast<size_t>(cap_seqs) * max_head));
   GLP_TRY(d.alloc(&d.status, 1));
@@ -881,7 +898,11 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
   }
   // masked mean of the final-normed rows, then the dense head on the pooled vectors
   GLP_TRY(prof_launch(d, st, kProfPool, 0.0, 4.0 * Td * H + 2.0 * n_seq * H, [&] {
-    glp::mean_pool_kernel<<<n_seq, 192, 0, st>>>(d.xf, d_cu_chunk, base, n_seq, d.pooled, nullptr);
+    const int segs = std::max(1, (max_len + glp::kPoolSeg - 1) / glp::kPoolSeg);
+    glp::mean_pool_kernel<<<dim3(static_cast<unsigned>(n_seq), static_cast<unsigned>(segs)), 192, 0, st>>>(
+        d.xf, d_cu_chunk, base, n_seq, d.pooled, nullptr, d.pool_part);
+    if (segs > 1)
+      glp::mean_pool_finish_kernel<<<n_seq, 192, 0, st>>>(d_cu_chunk, base, n_seq, d.pool_part, d.pooled, nullptr);
     GLP_CUDA(cudaGetLastError());
     return GLP_OK;
   }));
@@ -913,6 +934,83 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
   return GLP_OK;
 }
 
+// Small launch chunks are bound by launch latency (one 512-token sequence: 174 launches for about
+// a millisecond of GPU work), so each chunk shape runs as an instantiated CUDA graph: captured
+// from run_chunk on its first use, replayed afterwards.  The key holds every value that reaches
+// a kernel parameter (the activation buffers, tensor maps and status word are fixed per device;
+// token ids and sequence offsets are read from device memory at run time).  Not used while the
+// per-kernel profiler records events, or with GLP_GRAPHS=0.
+bool use_graphs() {
+  static const bool on = [] {
+    const char* e = std::getenv("GLP_GRAPHS");
+    return !(e && std::string(e) == "0");
+  }();
+  return on;
+}
+
+constexpr size_t kMaxChunkGraphs = 16;
+
+int run_chunk_graph(const Config& c, Device& d, const int* d_ids_chunk, const int* d_cu_chunk, const int* h_cu_chunk,
+                    int base, int n_seq, int T, int max_len, int out_dim, float* d_out, cudaStream_t st) {
+  // the legacy default stream cannot be captured, and a stream the caller is capturing
+  // already records these launches into the caller's graph
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  const bool capturable = st != nullptr && st != cudaStreamLegacy && st != cudaStreamPerThread &&
+                          cudaStreamIsCapturing(st, &cap) == cudaSuccess && cap == cudaStreamCaptureStatusNone;
+  if (!use_graphs() || d.prof_on || !capturable)
+    return run_chunk(c, d, d_ids_chunk, d_cu_chunk, h_cu_chunk, base, n_seq, T, max_len, out_dim, d_out, st);
+  const std::array<int64_t, 8> key{base, n_seq, T, max_len, out_dim, reinterpret_cast<int64_t>(d_ids_chunk),
+                                   reinterpret_cast<int64_t>(d_cu_chunk), reinterpret_cast<int64_t>(d_out)};
+  ++d.graph_clock;
+  for (auto& g : d.graphs) {
+    if (g.key != key) continue;
+    GLP_CUDA(cudaGraphLaunch(g.exec, st));
+    for (int k = 0; k < GLP_PROFILE_KINDS; ++k) {
+      d.prof_launch[k] += g.launches[k];
+      d.prof_flops[k] += g.flops[k];
+      d.prof_bytes[k] += g.bytes[k];
+    }
+    g.last_use = d.graph_clock;
+    return GLP_OK;
+  }
+  Device::ChunkGraph g;
+  g.key = key;
+  g.launches = d.prof_launch;
+  g.flops = d.prof_flops;
+  g.bytes = d.prof_bytes;
+  GLP_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+  const int rc = run_chunk(c, d, d_ids_chunk, d_cu_chunk, h_cu_chunk, base, n_seq, T, max_len, out_dim, d_out, st);
+  cudaGraph_t graph = nullptr;
+  const cudaError_t ce = cudaStreamEndCapture(st, &graph);  // always ends the capture
+  if (rc != GLP_OK) {
+    if (graph) cudaGraphDestroy(graph);
+    return rc;
+  }
+  if (ce != cudaSuccess) {
+    if (graph) cudaGraphDestroy(graph);
+    return fail(GLP_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(ce));
+  }
+  const cudaError_t ie = cudaGraphInstantiate(&g.exec, graph, 0);
+  cudaGraphDestroy(graph);
+  if (ie != cudaSuccess) return fail(GLP_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(ie));
+  for (int k = 0; k < GLP_PROFILE_KINDS; ++k) {  // what this chunk added to the counters
+    g.launches[k] = d.prof_launch[k] - g.launches[k];
+    g.flops[k] = d.prof_flops[k] - g.flops[k];
+    g.bytes[k] = d.prof_bytes[k] - g.bytes[k];
+  }
+  g.last_use = d.graph_clock;
+  GLP_CUDA(cudaGraphLaunch(g.exec, st));
+  if (d.graphs.size() >= kMaxChunkGraphs) {  // evict the least recently used (after its launches)
+    auto lru = std::min_element(d.graphs.begin(), d.graphs.end(),
+                                [](const Device::ChunkGraph& x, const Device::ChunkGraph& y) { return x.last_use < y.last_use; });
+    GLP_CUDA(cudaStreamSynchronize(st));
+    cudaGraphExecDestroy(lru->exec);
+    d.graphs.erase(lru);
+  }
+  d.graphs.push_back(g);
+  return GLP_OK;
+}
+
 // Run all sequences of a packed input on one device, cutting launch chunks by token count.
 int run_packed(const Config& c, Device& d, const int* d_ids, const int* d_cu, const int* h_cu, int n_seq, int out_dim,
                float* d_out, cudaStream_t st) {
@@ -929,8 +1027,8 @@ int run_packed(const Config& c, Device& d, const int* d_ids, const int* d_cu, co
     if (s1 == s0) return fail(GLP_ERR_INVALID_ARG, "sequence longer than the launch chunk (max_batch_tokens)");
     const int base = h_cu[s0];
     const int T = h_cu[s1] - base;
-    GLP_TRY(run_chunk(c, d, d_ids + base, d_cu + s0, h_cu + s0, base, s1 - s0, T, max_len, out_dim,
-                      d_out + static_cast<size_t>(s0) * out_dim, st));
+    GLP_TRY(run_chunk_graph(c, d, d_ids + base, d_cu + s0, h_cu + s0, base, s1 - s0, T, max_len, out_dim,
+                            d_out + static_cast<size_t>(s0) * out_dim, st));
     s0 = s1;
   }
   return GLP_OK;

@@ -260,24 +260,15 @@ __global__ void positions_kernel(const int* __restrict__ cu_seqlens, int cu_base
 
 // ---------------------------------------------------------------------------- pooling
 // pooled[b] = sum_{t in seq b} xf[t] / max(len_b, 1e-9)   (model.rs:671-680), f32, fixed
-// summation order (deterministic).  Block per sequence, 192 threads x 4 columns.
-__global__ void mean_pool_kernel(const float* __restrict__ xf, const int* __restrict__ cu_seqlens, int cu_base,
-                                 int n_seq, __half* __restrict__ pooled16,
-                                 float* __restrict__ pooled_f32) {
-  const int b = blockIdx.x;
-  if (b >= n_seq) return;
-  const int t0 = cu_seqlens[b] - cu_base, t1 = cu_seqlens[b + 1] - cu_base;
-  const int c = threadIdx.x * 4;
-  if (c >= kHidden) return;
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int t = t0; t < t1; ++t) {
-    const float4 v = *reinterpret_cast<const float4*>(xf + static_cast<size_t>(t) * kHidden + c);
-    acc.x += v.x;
-    acc.y += v.y;
-    acc.z += v.z;
-    acc.w += v.w;
-  }
-  const float cnt = fmaxf(static_cast<float>(t1 - t0), 1e-9f);
+// summation order (deterministic, independent of the other sequences of the batch).
+// Block (sequence b, segment s) sums tokens [512 s, 512 s + 512) of the sequence in order,
+// 192 threads x 4 columns.  A sequence of at most 512 tokens is one segment and is finished in
+// place; longer ones leave per-segment sums in `part` at slot floor(t0 / 512) + b + s (t0 = the
+// sequence's first token in the chunk: distinct for every (b, s), below T / 512 + n_seq), and
+// mean_pool_finish_kernel adds them in segment order.
+constexpr int kPoolSeg = 512;
+
+__device__ __forceinline__ void pool_write(float4 acc, float cnt, int b, int c, __half* pooled16, float* pooled_f32) {
   acc.x /= cnt;
   acc.y /= cnt;
   acc.z /= cnt;
@@ -287,6 +278,54 @@ __global__ void mean_pool_kernel(const float* __restrict__ xf, const int* __rest
   pk.x = pack_f16(acc.x, acc.y);
   pk.y = pack_f16(acc.z, acc.w);
   *reinterpret_cast<uint2*>(pooled16 + static_cast<size_t>(b) * kHidden + c) = pk;
+}
+
+__global__ void mean_pool_kernel(const float* __restrict__ xf, const int* __restrict__ cu_seqlens, int cu_base,
+                                 int n_seq, __half* __restrict__ pooled16, float* __restrict__ pooled_f32,
+                                 float* __restrict__ part) {
+  const int b = blockIdx.x, sg = blockIdx.y;
+  if (b >= n_seq) return;
+  const int t0 = cu_seqlens[b] - cu_base, t1 = cu_seqlens[b + 1] - cu_base;
+  const int n_segs = max(1, (t1 - t0 + kPoolSeg - 1) / kPoolSeg);
+  if (sg >= n_segs) return;
+  const int c = threadIdx.x * 4;
+  if (c >= kHidden) return;
+  const int s0 = t0 + sg * kPoolSeg, s1 = min(t1, s0 + kPoolSeg);
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int t = s0; t < s1; ++t) {
+    const float4 v = *reinterpret_cast<const float4*>(xf + static_cast<size_t>(t) * kHidden + c);
+    acc.x += v.x;
+    acc.y += v.y;
+    acc.z += v.z;
+    acc.w += v.w;
+  }
+  if (n_segs == 1) {
+    pool_write(acc, fmaxf(static_cast<float>(t1 - t0), 1e-9f), b, c, pooled16, pooled_f32);
+  } else {
+    const size_t slot = static_cast<size_t>(t0 / kPoolSeg + b + sg);
+    *reinterpret_cast<float4*>(part + slot * kHidden + c) = acc;
+  }
+}
+
+__global__ void mean_pool_finish_kernel(const int* __restrict__ cu_seqlens, int cu_base, int n_seq,
+                                        const float* __restrict__ part, __half* __restrict__ pooled16,
+                                        float* __restrict__ pooled_f32) {
+  const int b = blockIdx.x;
+  if (b >= n_seq) return;
+  const int t0 = cu_seqlens[b] - cu_base, t1 = cu_seqlens[b + 1] - cu_base;
+  const int n_segs = max(1, (t1 - t0 + kPoolSeg - 1) / kPoolSeg);
+  if (n_segs == 1) return;  // finished by mean_pool_kernel
+  const int c = threadIdx.x * 4;
+  if (c >= kHidden) return;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int sg = 0; sg < n_segs; ++sg) {
+    const float4 v = *reinterpret_cast<const float4*>(part + static_cast<size_t>(t0 / kPoolSeg + b + sg) * kHidden + c);
+    acc.x += v.x;
+    acc.y += v.y;
+    acc.z += v.z;
+    acc.w += v.w;
+  }
+  pool_write(acc, static_cast<float>(t1 - t0), b, c, pooled16, pooled_f32);
 }
 
 // L2-normalise (clamp 1e-12) then MRL: the first out_dim values renormalised

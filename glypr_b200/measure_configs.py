@@ -1,0 +1,231 @@
+"""Measure BASELINE configs 1-4 on one GPU (config 5 is bench.py's line).
+
+    python glypr_b200/measure_configs.py [--model-dir DIR] [--out FILE.md]
+
+* config 1  one 512-token Q8_0 sequence: latency (median of 10 after 3 warm-ups), device-resident
+            ids (glp_embed_packed_device) and host ids -> host embeddings (glp_embed_tokens);
+* config 2  Q8_0 x bf16 GEMM (glp_q8_0_gemm: dequantisation of the Q8_0 weight into the library's
+            scratch + the tcgen05 GEMM), W [N,K] in {768x768, 256x768, 1152x768, 768x1152},
+            M in {512, 4096, 32768, 131072}, bf16 out; % of roofline = max(FLOP / P_tensor,
+            bytes / BW_HBM) / time with the measured peaks of MEASURED_PEAKS.json (burst);
+* config 3  256 Q8_0 sequences, lengths uniform in [64, 512], 768-d and 256-d MRL outputs:
+            embeddings/s and TFLOP/s of valid-token work (padding is not computed);
+* config 4  BF16 weights, one 8192-token sequence (sliding window 512 on local layers, full on
+            global): latency, then per-kernel ms / TFLOP/s / GB/s from the library's own CUDA-event
+            profile (a separate pass, so the latency carries no profiling overhead).
+
+All inputs are the seeded synthetic GGUFs of glypr_b200.synth; times are CUDA events on the
+launching stream.  Prints a markdown report (and writes it with --out).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+from glypr_b200 import api, synth  # noqa: E402
+
+GFLOP_PER_SEQ_512 = 123.21  # linear + attention + head per 512-token sequence (config 1)
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["bf16_tflops"]), float(d["hbm_gbs"]), "measured (MEASURED_PEAKS.json, burst)"
+    return 1590.0, 6650.0, "fallback"
+
+
+def timed(torch, fn, warm=3, reps=10):
+    """Median ms of `fn` over `reps` runs after `warm` warm-ups (CUDA events, current stream)."""
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(reps):
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        e1.synchronize()
+        ts.append(e0.elapsed_time(e1))
+    return float(np.median(ts))
+
+
+def linear_flops_per_token(cfg) -> float:
+    d, h, f = cfg.head_dim, cfg.hidden, cfg.ffn
+    qkv = (cfg.n_heads + 2 * cfg.n_kv_heads) * d
+    per_layer = qkv * h + h * cfg.n_heads * d + 2 * f * h + h * f
+    return 2.0 * per_layer * cfg.n_layers
+
+
+def attention_flops(cfg, lengths, window=512) -> float:
+    """4 * head_dim * heads FLOP per visible (query, key) pair, sliding layers windowed."""
+    total = 0.0
+    for L in lengths:
+        full = float(L) * L
+        if window > 0 and L > window + 1:
+            i = np.arange(L)
+            vis = (np.minimum(L - 1, i + window) - np.maximum(0, i - window) + 1).sum()
+        else:
+            vis = full
+        n_global = sum(1 for li in range(cfg.n_layers) if not cfg.layer_is_sliding(li))
+        total += (cfg.n_layers - n_global) * vis + n_global * full
+    return 4.0 * cfg.head_dim * cfg.n_heads * total
+
+
+def packed_inputs(torch, ids, lengths):
+    valid = np.concatenate([ids[i, : lengths[i]] for i in range(len(lengths))]).astype(np.int32)
+    h_cu = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int32)
+    return torch.from_numpy(valid).cuda(), torch.from_numpy(h_cu).cuda(), h_cu
+
+
+def config1(torch, emb, report):
+    ids, lens = synth.make_batch(1, 512, emb.info.vocab, seed=synth.MASTER_SEED + 11)
+    d_ids, d_cu, h_cu = packed_inputs(torch, ids, lens)
+    d_out = torch.empty((1, 768), dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    dev_ms = timed(torch, lambda: emb.embed_packed_device(d_ids.data_ptr(), d_cu.data_ptr(), h_cu, 1, 768,
+                                                         d_out.data_ptr(), stream))
+    host_ms = timed(torch, lambda: emb.embed_tokens(ids, lens))
+    report.append("## Config 1 — one 512-token Q8_0 sequence\n")
+    report.append("| path | latency (ms, median of 10) | TFLOP/s |\n|---|---:|---:|")
+    for name, ms in (("device-resident ids (`glp_embed_packed_device`)", dev_ms),
+                     ("host ids → host embedding (`glp_embed_tokens`)", host_ms)):
+        report.append(f"| {name} | {ms:.3f} | {GFLOP_PER_SEQ_512 / ms:.1f} |")
+    report.append("")
+
+
+def config2(torch, report):
+    p_t, p_b, src = peaks()
+    report.append("## Config 2 — Q8_0 × bf16 GEMM (`glp_q8_0_gemm`, bf16 out)\n")
+    report.append(f"Peaks: {p_t:.0f} TFLOP/s, {p_b:.0f} GB/s ({src}). Time includes the per-call "
+                  "dequantisation of the Q8_0 weight.\n")
+    report.append("| W [N×K] | M | ms | TFLOP/s | GB/s | % of roofline |\n|---|---:|---:|---:|---:|---:|")
+    rng = np.random.default_rng(synth.MASTER_SEED + 22)
+    for n, k in ((768, 768), (256, 768), (1152, 768), (768, 1152)):
+        w = (rng.standard_normal((n, k), dtype=np.float32) * np.float32(0.02)).astype(np.float32)
+        blocks = synth.quantize_q8_0(w)
+        d_w = torch.from_numpy(blocks.view(np.uint8).reshape(-1).copy()).cuda()
+        for m in (512, 4096, 32768, 131072):
+            x = torch.randn((m, k), device="cuda").to(torch.bfloat16)
+            y = torch.empty((m, n), device="cuda", dtype=torch.bfloat16)
+            ms = timed(torch, lambda: api.q8_0_gemm(d_w.data_ptr(), n, k, x.data_ptr(), m, y.data_ptr(), False))
+            flop = 2.0 * m * n * k
+            byts = n * k / 32 * 34 + 2.0 * m * k + 2.0 * m * n
+            roof_ms = max(flop / (p_t * 1e9), byts / (p_b * 1e6))
+            report.append(f"| {n}×{k} | {m} | {ms:.4f} | {flop / ms / 1e9:.0f} | {byts / ms / 1e6:.0f} | "
+                          f"{100 * roof_ms / ms:.1f} |")
+            del x, y
+    report.append("")
+
+
+def config3(torch, emb, report):
+    rng = np.random.default_rng(synth.MASTER_SEED + 33)
+    lens = rng.integers(64, 513, size=256).astype(np.int32)
+    ids, lens = synth.make_batch(256, 512, emb.info.vocab, seed=synth.MASTER_SEED + 34, lengths=list(lens))
+    d_ids, d_cu, h_cu = packed_inputs(torch, ids, lens)
+    stream = torch.cuda.current_stream().cuda_stream
+    d768 = torch.empty((256, 768), dtype=torch.float32, device="cuda")
+    d256 = torch.empty((256, 256), dtype=torch.float32, device="cuda")
+    ms768 = timed(torch, lambda: emb.embed_packed_device(d_ids.data_ptr(), d_cu.data_ptr(), h_cu, 256, 768,
+                                                        d768.data_ptr(), stream))
+    ms256 = timed(torch, lambda: emb.embed_packed_device(d_ids.data_ptr(), d_cu.data_ptr(), h_cu, 256, 256,
+                                                        d256.data_ptr(), stream))
+    host_ms = timed(torch, lambda: emb.embed_tokens(ids, lens))
+    cfg = synth.BASELINE
+    tok = float(lens.sum())
+    flop = linear_flops_per_token(cfg) * tok + attention_flops(cfg, lens)
+    report.append("## Config 3 — 256 Q8_0 sequences, lengths uniform in [64, 512]\n")
+    report.append(f"Valid tokens {int(tok)} (mean length {tok / 256:.1f}); valid-token work "
+                  f"{flop / 1e12:.2f} TFLOP per batch (padding is never computed: packed by length).\n")
+    report.append("| output | ms per batch | embeddings/s | tokens/s | TFLOP/s |\n|---|---:|---:|---:|---:|")
+    for name, ms in (("768-d (device-resident ids)", ms768), ("256-d MRL (device-resident ids)", ms256),
+                     ("768-d, host ids → host embeddings", host_ms)):
+        report.append(f"| {name} | {ms:.2f} | {256 / ms * 1e3:.0f} | {tok / ms * 1e3 / 1e6:.2f} M | "
+                      f"{flop / ms / 1e9:.0f} |")
+    report.append("")
+
+
+def config4(torch, path, report):
+    with api.GlyprEmbedder.load_gguf(path, [0]) as emb:
+        ids, lens = synth.make_batch(1, 8192, emb.info.vocab, seed=synth.MASTER_SEED + 44)
+        d_ids, d_cu, h_cu = packed_inputs(torch, ids, lens)
+        d_out = torch.empty((1, 768), dtype=torch.float32, device="cuda")
+        stream = torch.cuda.current_stream().cuda_stream
+        run = lambda: emb.embed_packed_device(d_ids.data_ptr(), d_cu.data_ptr(), h_cu, 1, 768, d_out.data_ptr(),
+                                              stream)
+        ms = timed(torch, run)
+        host_ms = timed(torch, lambda: emb.embed_tokens(ids, lens), warm=2, reps=5)
+        emb.profile_enable(True)
+        run()
+        torch.cuda.synchronize()
+        prof = emb.profile_read()
+        emb.profile_enable(False)
+    cfg = synth.BASELINE
+    flop = linear_flops_per_token(cfg) * 8192 + attention_flops(cfg, [8192])
+    report.append("## Config 4 — BF16 weights, one 8192-token sequence\n")
+    report.append(f"Work {flop / 1e12:.3f} TFLOP (linear + windowed local / full global attention). "
+                  f"Latency {ms:.2f} ms device-resident ({flop / ms / 1e9:.0f} TFLOP/s), {host_ms:.2f} ms "
+                  "with host ids in and the host embedding out.\n")
+    report.append("Per kernel (one forward, library CUDA-event profile):\n")
+    report.append("| kernel | launches | ms | TFLOP/s | GB/s |\n|---|---:|---:|---:|---:|")
+    for name, v in sorted(((k, v) for k, v in prof.items() if not k.startswith("_")), key=lambda kv: -kv[1]["ms"]):
+        if v["launches"] == 0:
+            continue
+        tf = f"{v['flops'] / v['ms'] / 1e9:.0f}" if v["flops"] > 0 else "—"
+        gb = f"{v['bytes'] / v['ms'] / 1e6:.0f}" if v["bytes"] > 0 else "—"
+        report.append(f"| {name} | {v['launches']} | {v['ms']:.3f} | {tf} | {gb} |")
+    report.append("")
+
+
+def main(argv=None) -> None:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--model-dir", default=os.environ.get("GLYPR_BENCH_DIR", "/tmp/glypr_models"))
+    ap.add_argument("--out", default=None)
+    ap.add_argument("--configs", default="1,2,3,4")
+    args = ap.parse_args(argv)
+    import torch
+    torch.backends.cuda.matmul.allow_tf32 = False
+    os.makedirs(args.model_dir, exist_ok=True)
+    want = set(int(c) for c in args.configs.split(","))
+    report = [f"# BASELINE configs 1–4 on one {torch.cuda.get_device_name(0)}\n",
+              f"Command: `python glypr_b200/measure_configs.py --configs {args.configs}` "
+              f"({time.strftime('%Y-%m-%d')}); median of 10 runs after 3 warm-ups unless stated.\n"]
+    api.load_library()
+    # a stream of our own: the library runs repeated launch-chunk shapes as CUDA graphs, which
+    # the legacy default stream cannot hold
+    side = torch.cuda.Stream()
+    torch.cuda.set_stream(side)
+    if want & {1, 3}:
+        q8 = synth.ensure_gguf(os.path.join(args.model_dir, "baseline_q8_0.gguf"), synth.BASELINE)
+        with api.GlyprEmbedder.load_gguf(q8, [0]) as emb:
+            if 1 in want:
+                config1(torch, emb, report)
+            if 3 in want:
+                config3(torch, emb, report)
+    if 2 in want:
+        config2(torch, report)
+    if 4 in want:
+        bf = synth.ensure_gguf(os.path.join(args.model_dir, "baseline_bf16.gguf"),
+                               synth.EncoderConfig(weight_type="bf16"))
+        config4(torch, bf, report)
+    text = "\n".join(report)
+    print(text, flush=True)
+    if args.out:
+        with open(args.out, "w") as f:
+            f.write(text + "\n")
+
+
+if __name__ == "__main__":
+    main()
