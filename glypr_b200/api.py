@@ -40,7 +40,15 @@ EXPORTED_SYMBOLS = (
     "glp_open", "glp_close", "glp_last_error", "glp_model_info", "glp_embed_tokens",
     "glp_embed_packed_device", "glp_device_status", "glp_profile_enable", "glp_profile_read",
     "glp_q8_0_dequant", "glp_q8_0_gemm", "glp_q8_0_gemm_noalloc", "glp_bf16_gemm", "glp_flash_attention",
+    "glp_engine_create", "glp_engine_create_with_executor", "glp_engine_embed", "glp_engine_stats",
+    "glp_engine_destroy",
 )
+
+# int (*glp_batch_fn)(void* user, const int32_t* ids, const int32_t* lengths, int n_seq, int max_len,
+#                     int out_dim, float* out)
+BATCH_FN = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.POINTER(ctypes.c_int32),
+                            ctypes.POINTER(ctypes.c_int32), ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                            ctypes.POINTER(ctypes.c_float))
 
 
 class GlyprError(RuntimeError):
@@ -113,6 +121,13 @@ def load_library(path: Optional[str] = None) -> ctypes.CDLL:
         L.glp_q8_0_gemm_noalloc.argtypes = [P, I, I, P, I, P, I, P]
         L.glp_bf16_gemm.argtypes = [P, I, I, P, I, P, I, P]
         L.glp_flash_attention.argtypes = [P, P, I, I, I, I, I, I, P, P]
+        L.glp_engine_create.argtypes = [P, I, I, ctypes.POINTER(P)]
+        L.glp_engine_create_with_executor.argtypes = [BATCH_FN, P, I, I, I, ctypes.POINTER(P)]
+        L.glp_engine_embed.argtypes = [P, P, I, I, P]
+        L.glp_engine_stats.argtypes = [P, ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int64),
+                                       ctypes.POINTER(ctypes.c_int)]
+        L.glp_engine_destroy.argtypes = [P]
+        L.glp_engine_destroy.restype = None
         _lib = L
         return L
 
@@ -297,3 +312,86 @@ def flash_attention(d_qkv: int, d_cu: int, n_seq: int, max_len: int, n_q_heads: 
     check(load_library().glp_flash_attention(ctypes.c_void_p(d_qkv), ctypes.c_void_p(d_cu), n_seq, max_len,
                                              n_q_heads, n_kv_heads, head_dim, window, ctypes.c_void_p(d_out),
                                              ctypes.c_void_p(stream)))
+
+
+# ---------------------------------------------------------------------------------------
+# dynamic-batching engine (glypr-server's inference engine, engine.rs:157-325)
+# ---------------------------------------------------------------------------------------
+
+class InferenceEngine:
+    """Blocking, thread-safe embedding of single sequences, batched by one worker thread.
+
+    ``InferenceEngine(embedder, max_batch_size)`` runs batches through the model context
+    (glp_engine_create); ``InferenceEngine.with_executor(fn, dim, max_batch_size)`` through a
+    Python batch function ``fn(ids [n, max_len] int32, lengths [n], out_dim) -> [n, out_dim]``
+    (glp_engine_create_with_executor; it raises to fail the batch).  ``embed(ids, truncate_dim)``
+    may be called from many threads at once and mirrors EngineHandle::embed (engine.rs:120-150).
+    """
+
+    def __init__(self, embedder: Optional["GlyprEmbedder"] = None, max_batch_size: int = 32,
+                 queue_capacity: int = 0, _executor=None, _dim: int = 0):
+        L = load_library()
+        self._h = ctypes.c_void_p()
+        self._keep = None
+        self._cv = threading.Condition()
+        self._active = 0      # calls between the closed check and their return
+        self._closed = False
+        self._embedder = embedder  # the context must outlive the engine
+        if embedder is not None:
+            check(L.glp_engine_create(embedder._h, max_batch_size, queue_capacity, ctypes.byref(self._h)))
+            self.dim = embedder.embedding_dim
+        else:
+            def trampoline(user, ids, lengths, n, max_len, out_dim, out):
+                try:
+                    a = np.ctypeslib.as_array(ids, shape=(n * max(max_len, 1),)).reshape(n, max(max_len, 1))
+                    lens = np.ctypeslib.as_array(lengths, shape=(n,))
+                    res = np.asarray(_executor(a[:, :max_len].copy(), lens.copy(), out_dim), dtype=np.float32)
+                    np.ctypeslib.as_array(out, shape=(n * out_dim,))[:] = res.reshape(-1)
+                    return GLP_OK
+                except Exception:  # the batch fails; every request of it gets the error
+                    return GLP_ERR_INVALID_ARG
+            self._keep = BATCH_FN(trampoline)  # the callback must outlive the engine
+            check(L.glp_engine_create_with_executor(self._keep, None, _dim, max_batch_size, queue_capacity,
+                                                    ctypes.byref(self._h)))
+            self.dim = _dim
+
+    @classmethod
+    def with_executor(cls, fn, dim: int, max_batch_size: int = 32, queue_capacity: int = 0) -> "InferenceEngine":
+        return cls(None, max_batch_size, queue_capacity, _executor=fn, _dim=dim)
+
+    def embed(self, ids, truncate_dim: Optional[int] = None) -> np.ndarray:
+        ids = np.ascontiguousarray(ids, dtype=np.int32).reshape(-1)
+        d = self.dim if not truncate_dim or truncate_dim >= self.dim else int(truncate_dim)
+        out = np.empty(d, dtype=np.float32)
+        with self._cv:
+            if self._closed:
+                raise GlyprError(GLP_ERR_INVALID_ARG, "Inference worker is not running")
+            self._active += 1
+        try:
+            check(load_library().glp_engine_embed(self._h, _ptr(ids), ids.size, 0 if d == self.dim else d,
+                                                  _ptr(out)))
+        finally:
+            with self._cv:
+                self._active -= 1
+                self._cv.notify_all()
+        return out
+
+    def stats(self) -> dict:
+        r, b, m = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_int()
+        check(load_library().glp_engine_stats(self._h, ctypes.byref(r), ctypes.byref(b), ctypes.byref(m)))
+        return {"requests": r.value, "batches": b.value, "largest_batch": m.value}
+
+    def close(self) -> None:
+        """Reject new calls, let the calls in flight finish, then stop the worker."""
+        with self._cv:
+            self._closed = True
+            self._cv.wait_for(lambda: self._active == 0)
+        if self._h:
+            load_library().glp_engine_destroy(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()

@@ -1189,6 +1189,11 @@ int noalloc_pointers(int dev, __nv_bfloat16** weight, int** status) {
 }  // namespace
 
 // ================================================================================= C ABI
+namespace glp {
+// for the engine (engine.cpp): set the calling thread's glp_last_error() message
+void set_last_error(const std::string& msg) { t_err = msg; }
+}  // namespace glp
+
 extern "C" {
 
 const char* glp_last_error(void) { return t_err.c_str(); }

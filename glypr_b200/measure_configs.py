@@ -10,6 +10,9 @@
             bytes / BW_HBM) / time with the measured peaks of MEASURED_PEAKS.json (burst);
 * config 3  256 Q8_0 sequences, lengths uniform in [64, 512], 768-d and 256-d MRL outputs:
             embeddings/s and TFLOP/s of valid-token work (padding is not computed);
+* serving   the dynamic-batching engine (glp_engine_*): client threads each embedding single
+            512-token Q8_0 sequences through InferenceEngine; requests/s, batch sizes and
+            per-request latency percentiles (host wall clock: end to end);
 * config 4  BF16 weights, one 8192-token sequence (sliding window 512 on local layers, full on
             global): latency, then per-kernel ms / TFLOP/s / GB/s from the library's own CUDA-event
             profile (a separate pass, so the latency carries no profiling overhead).
@@ -189,16 +192,54 @@ def config4(torch, path, report):
     report.append("")
 
 
+def serving(emb, report, clients=64, per_client=64, max_batch=512):
+    import threading
+    ids, lens = synth.make_batch(clients * per_client, 512, emb.info.vocab, seed=synth.MASTER_SEED + 55)
+    lat = []
+    lock = threading.Lock()
+    with api.InferenceEngine(emb, max_batch_size=max_batch) as eng:
+        eng.embed(ids[0])  # warm-up (graph capture of the first shapes)
+
+        def client(c):
+            mine = []
+            for k in range(per_client):
+                i = c * per_client + k
+                t0 = time.perf_counter()
+                eng.embed(ids[i])
+                mine.append(time.perf_counter() - t0)
+            with lock:
+                lat.extend(mine)
+
+        threads = [threading.Thread(target=client, args=(c,)) for c in range(clients)]
+        t0 = time.perf_counter()
+        for t in threads:
+            t.start()
+        for t in threads:
+            t.join()
+        wall = time.perf_counter() - t0
+        st = eng.stats()
+    n = clients * per_client
+    lat_ms = np.sort(np.array(lat)) * 1e3
+    report.append("## Serving — dynamic-batching engine, single 512-token requests\n")
+    report.append(f"{clients} client threads x {per_client} requests, max_batch {max_batch} "
+                  f"(glp_engine_embed: the reference server's batching policy, engine.rs:216-245).\n")
+    report.append("| requests/s | batches | mean batch | largest batch | latency p50 (ms) | p99 (ms) |\n"
+                  "|---:|---:|---:|---:|---:|---:|")
+    report.append(f"| {n / wall:.0f} | {st['batches'] - 1} | {(st['requests'] - 1) / max(st['batches'] - 1, 1):.1f} | "
+                  f"{st['largest_batch']} | {lat_ms[len(lat_ms) // 2]:.1f} | {lat_ms[int(len(lat_ms) * 0.99)]:.1f} |")
+    report.append("")
+
+
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--model-dir", default=os.environ.get("GLYPR_BENCH_DIR", "/tmp/glypr_models"))
     ap.add_argument("--out", default=None)
-    ap.add_argument("--configs", default="1,2,3,4")
+    ap.add_argument("--configs", default="1,2,3,4,serving")
     args = ap.parse_args(argv)
     import torch
     torch.backends.cuda.matmul.allow_tf32 = False
     os.makedirs(args.model_dir, exist_ok=True)
-    want = set(int(c) for c in args.configs.split(","))
+    want = set(int(c) if c.isdigit() else c for c in args.configs.split(","))
     report = [f"# BASELINE configs 1–4 on one {torch.cuda.get_device_name(0)}\n",
               f"Command: `python glypr_b200/measure_configs.py --configs {args.configs}` "
               f"({time.strftime('%Y-%m-%d')}); median of 10 runs after 3 warm-ups unless stated.\n"]
@@ -207,13 +248,15 @@ def main(argv=None) -> None:
     # the legacy default stream cannot hold
     side = torch.cuda.Stream()
     torch.cuda.set_stream(side)
-    if want & {1, 3}:
+    if want & {1, 3, "serving"}:
         q8 = synth.ensure_gguf(os.path.join(args.model_dir, "baseline_q8_0.gguf"), synth.BASELINE)
         with api.GlyprEmbedder.load_gguf(q8, [0]) as emb:
             if 1 in want:
                 config1(torch, emb, report)
             if 3 in want:
                 config3(torch, emb, report)
+            if "serving" in want:
+                serving(emb, report)
     if 2 in want:
         config2(torch, report)
     if 4 in want:

@@ -118,6 +118,43 @@ int glp_profile_enable(glp_ctx* ctx, int dev_index, int enable);
  * enable/read, then reset them. */
 int glp_profile_read(glp_ctx* ctx, int dev_index, glp_profile* out);
 
+/* ---- dynamic-batching engine (glypr-server's inference engine, engine.rs:157-325) ---- */
+
+typedef struct glp_engine glp_engine;
+
+/* A batch executor: embed n_seq right-padded sequences (ids [n_seq * max_len], lengths
+ * [n_seq]) into out [n_seq * out_dim] f32; returns GLP_OK or an error status. */
+typedef int (*glp_batch_fn)(void* user, const int32_t* ids, const int32_t* lengths, int n_seq, int max_len,
+                            int out_dim, float* out);
+
+/* Start an engine over a model context: one worker thread forms batches of up to max_batch
+ * requests as the reference's worker does (block for the first, drain what is pending, yield
+ * once, drain again; engine.rs:216-245) and runs each through glp_embed_tokens, which shards
+ * it across the context's devices.  queue_capacity bounds the waiting requests (0 = 1024,
+ * the reference's channel size).  While the engine runs, it is the context's only caller. */
+int glp_engine_create(glp_ctx* ctx, int max_batch, int queue_capacity, glp_engine** out);
+
+/* The same engine over a caller-supplied executor of width embedding_dim (other backends;
+ * the host tests drive the batching logic through it). */
+int glp_engine_create_with_executor(glp_batch_fn fn, void* user, int embedding_dim, int max_batch,
+                                    int queue_capacity, glp_engine** out);
+
+/* Embed one sequence of len token ids through the engine; blocks until its batch is done and
+ * may be called from any number of threads at once (EngineHandle::embed, engine.rs:120-150).
+ * truncate_dim in (0, embedding_dim) returns the Matryoshka truncation (first truncate_dim
+ * values renormalised, util.rs:6-29) in out [truncate_dim]; 0 (or >= embedding_dim) the full
+ * out [embedding_dim].  A failed batch fails each of its requests ("Batch inference error:
+ * ..."); after glp_engine_destroy has begun, calls fail with "Inference worker is not
+ * running". */
+int glp_engine_embed(glp_engine* e, const int32_t* ids, int len, int truncate_dim, float* out);
+
+/* Requests answered, batches run and the largest batch so far. */
+int glp_engine_stats(glp_engine* e, int64_t* requests, int64_t* batches, int* largest_batch);
+
+/* Answer every queued request, stop the worker and free the engine (NULL is a no-op).  No
+ * call may use the engine after this returns. */
+void glp_engine_destroy(glp_engine* e);
+
 /* ---- kernel-level entry points (microbenchmarks and tests; current device) ---- */
 
 /* Bit-exact Q8_0 dequantisation: out[32*b + j] = f32(d_b) * q_b[j] for n_blocks 34-byte
