@@ -82,24 +82,6 @@ __device__ __forceinline__ void store_f32x8(float* p, const float* v) {
   reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
   reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
 }
-__device__ __forceinline__ void load_f16x8(const __half* p, float* v) {
-  const uint4 u = *reinterpret_cast<const uint4*>(p);
-  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const __half2 h = *reinterpret_cast<const __half2*>(&w[i]);
-    const float2 f = __half22float2(h);
-    v[2 * i] = f.x;
-    v[2 * i + 1] = f.y;
-  }
-}
-template <typename T>
-__device__ __forceinline__ void load16x8(const T* p, float* v) {
-  const uint4 u = *reinterpret_cast<const uint4*>(p);
-  const T* e = reinterpret_cast<const T*>(&u);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) v[i] = Half16<T>::to_f32(e[i]);
-}
 template <typename T>
 __device__ __forceinline__ void store16x8(T* p, const float* v) {
   uint4 u;
@@ -107,14 +89,6 @@ __device__ __forceinline__ void store16x8(T* p, const float* v) {
   u.y = Half16<T>::pack(v[2], v[3]);
   u.z = Half16<T>::pack(v[4], v[5]);
   u.w = Half16<T>::pack(v[6], v[7]);
-  *reinterpret_cast<uint4*>(p) = u;
-}
-__device__ __forceinline__ void store_f16x8(__half* p, const float* v) {
-  uint4 u;
-  u.x = pack_f16(v[0], v[1]);
-  u.y = pack_f16(v[2], v[3]);
-  u.z = pack_f16(v[4], v[5]);
-  u.w = pack_f16(v[6], v[7]);
   *reinterpret_cast<uint4*>(p) = u;
 }
 
