@@ -41,8 +41,16 @@ EXPORTED_SYMBOLS = (
     "glp_embed_packed_device", "glp_device_status", "glp_profile_enable", "glp_profile_read",
     "glp_q8_0_dequant", "glp_q8_0_gemm", "glp_q8_0_gemm_noalloc", "glp_bf16_gemm", "glp_flash_attention",
     "glp_engine_create", "glp_engine_create_with_executor", "glp_engine_embed", "glp_engine_stats",
-    "glp_engine_destroy",
+    "glp_engine_destroy", "glp_tokenizer_from_gguf", "glp_tokenizer_from_vocab", "glp_tokenizer_free",
+    "glp_tokenizer_info", "glp_tokenize", "glp_tokenize_batch", "glp_format_query", "glp_format_document",
+    "glp_task_format", "glp_embed_texts", "glp_engine_embed_text",
 )
+
+# sequence forms of a text (include/glypr_cuda.h GLP_TOKENS_*)
+GLP_TOKENS_BARE = 0      # the BPE ids alone
+GLP_TOKENS_SINGLE = 1    # GlyprTokenizer::encode: BOS/EOS added unless already there (tokenizer.rs:162-177)
+GLP_TOKENS_SEQUENCE = 2  # encode_modality_sequence for a text: BOS + ids + EOS (tokenizer.rs:454-566)
+GLP_DEFAULT_MAX_SEQ_LEN = 8320
 
 # int (*glp_batch_fn)(void* user, const int32_t* ids, const int32_t* lengths, int n_seq, int max_len,
 #                     int out_dim, float* out)
@@ -128,6 +136,19 @@ def load_library(path: Optional[str] = None) -> ctypes.CDLL:
                                        ctypes.POINTER(ctypes.c_int)]
         L.glp_engine_destroy.argtypes = [P]
         L.glp_engine_destroy.restype = None
+        CP, SZ = ctypes.c_char_p, ctypes.c_size_t
+        L.glp_tokenizer_from_gguf.argtypes = [CP, ctypes.POINTER(P)]
+        L.glp_tokenizer_from_vocab.argtypes = [P, I, P, I, ctypes.POINTER(P)]
+        L.glp_tokenizer_free.argtypes = [P]
+        L.glp_tokenizer_free.restype = None
+        L.glp_tokenizer_info.argtypes = [P, ctypes.POINTER(I), ctypes.POINTER(I)]
+        L.glp_tokenize.argtypes = [P, CP, SZ, I, P, I, ctypes.POINTER(I)]
+        L.glp_tokenize_batch.argtypes = [P, P, P, I, I, I, I, P, SZ, P]
+        L.glp_format_query.argtypes = [CP, SZ, CP, P, SZ, ctypes.POINTER(SZ)]
+        L.glp_format_document.argtypes = [CP, SZ, CP, P, SZ, ctypes.POINTER(SZ)]
+        L.glp_task_format.argtypes = [CP, CP, CP, SZ, P, SZ, ctypes.POINTER(SZ)]
+        L.glp_embed_texts.argtypes = [P, P, P, P, I, I, I, I, P]
+        L.glp_engine_embed_text.argtypes = [P, P, CP, SZ, CP, CP, I, P]
         _lib = L
         return L
 
@@ -258,6 +279,52 @@ class GlyprEmbedder:
     def embed_text_ids(self, ids: Sequence[int], truncate_dim: Optional[int] = None) -> np.ndarray:
         return self.embed_batch([ids], truncate_dim)[0]
 
+    # text entry points (lib.rs:504-517, 655-723): prompt formatting + tokenisation on the host,
+    # then the same device path as embed_tokens
+    def embed_texts(self, tokenizer: "Tokenizer", texts: Sequence[str], form: int = GLP_TOKENS_SEQUENCE,
+                    truncate_dim: Optional[int] = None, max_seq_len: int = 0) -> np.ndarray:
+        """Formatted texts -> [n, dim] (glp_embed_texts).  ``form``: GLP_TOKENS_SINGLE as the
+        reference's single-text calls tokenise, GLP_TOKENS_SEQUENCE as its batch calls do."""
+        enc = [t.encode("utf-8") for t in texts]
+        if not enc:
+            return np.zeros((0, int(truncate_dim or self.embedding_dim)), dtype=np.float32)
+        bufs = (ctypes.c_char_p * len(enc))(*enc)
+        lens = (ctypes.c_size_t * len(enc))(*[len(b) for b in enc])
+        od = int(truncate_dim or self.embedding_dim)
+        out = np.empty((len(enc), od), dtype=np.float32)
+        check(load_library().glp_embed_texts(self._h, tokenizer._h, ctypes.cast(bufs, ctypes.c_void_p),
+                                             ctypes.cast(lens, ctypes.c_void_p), len(enc), form, max_seq_len, od,
+                                             _ptr(out)))
+        return out
+
+    def embed_text(self, tokenizer: "Tokenizer", text: str, task: Optional[str] = None,
+                   title: Optional[str] = None, truncate_dim: Optional[int] = None) -> np.ndarray:
+        """``embed_text(text, Task)`` (lib.rs:506-509): task.rs formatting, single-text tokens."""
+        return self.embed_texts(tokenizer, [task_format(task, title, text)], GLP_TOKENS_SINGLE, truncate_dim)[0]
+
+    def embed_query(self, tokenizer: "Tokenizer", query: str, task: str = "search_query",
+                    truncate_dim: Optional[int] = None) -> np.ndarray:
+        """lib.rs:663-671: GlyprTokenizer::format_query, single-text tokens."""
+        return self.embed_texts(tokenizer, [format_query(query, task)], GLP_TOKENS_SINGLE, truncate_dim)[0]
+
+    def embed_document(self, tokenizer: "Tokenizer", content: str, title: Optional[str] = None,
+                       truncate_dim: Optional[int] = None) -> np.ndarray:
+        """lib.rs:673-681: GlyprTokenizer::format_document, single-text tokens."""
+        return self.embed_texts(tokenizer, [format_document(content, title)], GLP_TOKENS_SINGLE, truncate_dim)[0]
+
+    def embed_batch_queries(self, tokenizer: "Tokenizer", queries: Sequence[str], task: str = "search_query",
+                            truncate_dim: Optional[int] = None) -> np.ndarray:
+        """lib.rs:693-705: formatted queries through the batch path."""
+        return self.embed_texts(tokenizer, [format_query(q, task) for q in queries], GLP_TOKENS_SEQUENCE,
+                                truncate_dim)
+
+    def embed_batch_documents(self, tokenizer: "Tokenizer", contents: Sequence[str],
+                              titles: Optional[Sequence[str]] = None,
+                              truncate_dim: Optional[int] = None) -> np.ndarray:
+        """lib.rs:707-723: formatted documents through the batch path."""
+        docs = [format_document(c, titles[i] if titles is not None else None) for i, c in enumerate(contents)]
+        return self.embed_texts(tokenizer, docs, GLP_TOKENS_SEQUENCE, truncate_dim)
+
     # device-resident path (stream-ordered; pointers are raw device addresses)
     def embed_packed_device(self, d_ids: int, d_cu: int, h_cu: np.ndarray, n_seq: int, out_dim: int,
                             d_out: int, stream: int = 0, dev_index: int = 0) -> None:
@@ -376,6 +443,27 @@ class InferenceEngine:
                 self._cv.notify_all()
         return out
 
+    def embed_text(self, tokenizer: "Tokenizer", text: str, task: Optional[str] = None,
+                   title: Optional[str] = None, truncate_dim: Optional[int] = None) -> np.ndarray:
+        """A server-style text request (glp_engine_embed_text): task.rs formatting, sequence
+        tokens on this thread, then the batching queue."""
+        d = self.dim if not truncate_dim or truncate_dim >= self.dim else int(truncate_dim)
+        out = np.empty(d, dtype=np.float32)
+        b = text.encode("utf-8")
+        with self._cv:
+            if self._closed:
+                raise GlyprError(GLP_ERR_INVALID_ARG, "Inference worker is not running")
+            self._active += 1
+        try:
+            check(load_library().glp_engine_embed_text(
+                self._h, tokenizer._h, b, len(b), task.encode("utf-8") if task is not None else None,
+                title.encode("utf-8") if title is not None else None, 0 if d == self.dim else d, _ptr(out)))
+        finally:
+            with self._cv:
+                self._active -= 1
+                self._cv.notify_all()
+        return out
+
     def stats(self) -> dict:
         r, b, m = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_int()
         check(load_library().glp_engine_stats(self._h, ctypes.byref(r), ctypes.byref(b), ctypes.byref(m)))
@@ -395,3 +483,131 @@ class InferenceEngine:
 
     def __exit__(self, *exc):
         self.close()
+
+
+# ---------------------------------------------------------------------------------------
+# text front end (tokenizer.rs, task.rs)
+# ---------------------------------------------------------------------------------------
+
+def _format(fn, *args) -> str:
+    n = ctypes.c_size_t()
+    cap = 256
+    while True:
+        buf = ctypes.create_string_buffer(cap)
+        rc = fn(*args, buf, cap, ctypes.byref(n))
+        if rc == GLP_OK:
+            return buf.raw[:n.value].decode("utf-8")
+        if n.value + 1 <= cap:
+            check(rc)
+        cap = n.value + 1
+
+
+def format_query(query: str, task: str) -> str:
+    """GlyprTokenizer::format_query (tokenizer.rs:144-152)."""
+    q = query.encode("utf-8")
+    return _format(load_library().glp_format_query, q, len(q), task.encode("utf-8"))
+
+
+def format_document(content: str, title: Optional[str] = None) -> str:
+    """GlyprTokenizer::format_document (tokenizer.rs:154-160)."""
+    c = content.encode("utf-8")
+    return _format(load_library().glp_format_document, c, len(c),
+                   title.encode("utf-8") if title is not None else None)
+
+
+def task_format(task: Optional[str], title: Optional[str], text: str) -> str:
+    """Task::from_name_and_title(task, title).format_text(text) (task.rs:21-73); None = Raw."""
+    t = text.encode("utf-8")
+    return _format(load_library().glp_task_format, task.encode("utf-8") if task is not None else None,
+                   title.encode("utf-8") if title is not None else None, t, len(t))
+
+
+class Tokenizer:
+    """GlyprTokenizer over the library's C++ BPE (glp_tokenizer_*).
+
+    ``Tokenizer.from_gguf(path)`` reads ``tokenizer.ggml.tokens`` / ``tokenizer.ggml.merges``
+    (tokenizer.rs:77-138); ``Tokenizer.from_vocab(tokens, merges)`` takes the two arrays.
+    ``encode(text)`` is GlyprTokenizer::encode (BOS/EOS unless present); ``encode(text, form)``
+    gives the other sequence forms; ``encode_batch`` tokenises on all host threads;
+    ``encode_batch_padded`` mirrors encode_batch_padded_with_limit (tokenizer.rs:182-222).
+    """
+
+    def __init__(self, handle: ctypes.c_void_p):
+        self._h = handle
+
+    @classmethod
+    def from_gguf(cls, path: str) -> "Tokenizer":
+        h = ctypes.c_void_p()
+        check(load_library().glp_tokenizer_from_gguf(path.encode(), ctypes.byref(h)))
+        return cls(h)
+
+    @classmethod
+    def from_vocab(cls, tokens: Sequence[str], merges: Sequence[str]) -> "Tokenizer":
+        tb = [t.encode("utf-8") for t in tokens]
+        mb = [m.encode("utf-8") for m in merges]
+        ta = (ctypes.c_char_p * max(len(tb), 1))(*tb)
+        ma = (ctypes.c_char_p * max(len(mb), 1))(*mb)
+        h = ctypes.c_void_p()
+        check(load_library().glp_tokenizer_from_vocab(ctypes.cast(ta, ctypes.c_void_p), len(tb),
+                                                      ctypes.cast(ma, ctypes.c_void_p), len(mb), ctypes.byref(h)))
+        return cls(h)
+
+    def close(self) -> None:
+        if self._h:
+            load_library().glp_tokenizer_free(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def info(self) -> dict:
+        n, m = ctypes.c_int(), ctypes.c_int()
+        check(load_library().glp_tokenizer_info(self._h, ctypes.byref(n), ctypes.byref(m)))
+        return {"tokens": n.value, "merges": m.value}
+
+    def encode(self, text: str, form: int = GLP_TOKENS_SINGLE) -> List[int]:
+        b = text.encode("utf-8")
+        ids = np.empty(3 * len(b) + 2, dtype=np.int32)
+        n = ctypes.c_int()
+        check(load_library().glp_tokenize(self._h, b, len(b), form, _ptr(ids), ids.size, ctypes.byref(n)))
+        return ids[:n.value].tolist()
+
+    def encode_batch(self, texts: Sequence[str], form: int = GLP_TOKENS_SINGLE, limit: int = 0,
+                     n_threads: int = 0) -> List[np.ndarray]:
+        enc = [t.encode("utf-8") for t in texts]
+        n = len(enc)
+        bufs = (ctypes.c_char_p * max(n, 1))(*enc)
+        lens = (ctypes.c_size_t * max(n, 1))(*[len(b) for b in enc])
+        cap = 3 * sum(len(b) for b in enc) + 2 * n
+        ids = np.empty(max(cap, 1), dtype=np.int32)
+        off = np.zeros(n + 1, dtype=np.int64)
+        check(load_library().glp_tokenize_batch(self._h, ctypes.cast(bufs, ctypes.c_void_p),
+                                                ctypes.cast(lens, ctypes.c_void_p), n, form, limit, n_threads,
+                                                _ptr(ids), cap, _ptr(off)))
+        return [ids[off[i]:off[i + 1]].copy() for i in range(n)]
+
+    def encode_batch_padded(self, texts: Sequence[str], limit: int = 0):
+        """(ids [B, L] right-padded with 0, mask [B, L]) like encode_batch_padded_with_limit."""
+        rows = self.encode_batch(texts, GLP_TOKENS_SINGLE, limit)
+        width = max(len(r) for r in rows)
+        ids = np.zeros((len(rows), width), dtype=np.int32)
+        mask = np.zeros((len(rows), width), dtype=np.int32)
+        for i, r in enumerate(rows):
+            ids[i, :len(r)] = r
+            mask[i, :len(r)] = 1
+        return ids, mask
+
+    def format_query(self, query: str, task: str) -> str:
+        return format_query(query, task)
+
+    def format_document(self, content: str, title: Optional[str] = None) -> str:
+        return format_document(content, title)

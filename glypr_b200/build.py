@@ -10,8 +10,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libglypr_cuda.so")
-SOURCES = ["glypr_cuda.cu", "gguf.cpp", "engine.cpp"]
-HEADERS = ["common.cuh", "gemm.cuh", "attention.cuh", "attention_tc.cuh", "rowops.cuh", "gguf.h"]
+SOURCES = ["glypr_cuda.cu", "gguf.cpp", "engine.cpp", "tokenizer.cpp"]
+HEADERS = ["common.cuh", "gemm.cuh", "attention.cuh", "attention_tc.cuh", "rowops.cuh", "gguf.h", "unicode_case.inc"]
 
 
 def nvcc() -> str:

@@ -23,6 +23,7 @@
 #include <deque>
 #include <mutex>
 #include <string>
+#include <string_view>
 #include <thread>
 #include <vector>
 
@@ -30,6 +31,10 @@
 
 namespace glp {
 void set_last_error(const std::string& msg);  // glypr_cuda.cu: this thread's glp_last_error()
+// tokenizer.cpp
+std::string tokenize_text(const glp_tokenizer* tok, std::string_view text, int form, std::vector<int32_t>* ids);
+std::string format_task(const char* task, const char* title, std::string_view text);
+bool valid_utf8(const char* s, size_t n);
 }
 
 namespace {
@@ -216,6 +221,34 @@ int glp_engine_embed(glp_engine* e, const int32_t* ids, int len, int truncate_di
   lk.unlock();
   if (r.rc != GLP_OK) glp::set_last_error(r.err);
   return r.rc;
+}
+
+int glp_engine_embed_text(glp_engine* e, const glp_tokenizer* tok, const char* text, size_t text_len, const char* task,
+                          const char* title, int truncate_dim, float* out) {
+  if (!e || !tok || (text_len && !text) || !out) {
+    glp::set_last_error("bad engine text request (NULL engine, tokenizer or buffer)");
+    return GLP_ERR_INVALID_ARG;
+  }
+  if (!glp::valid_utf8(text, text_len) || (task && !glp::valid_utf8(task, std::strlen(task))) ||
+      (title && !glp::valid_utf8(title, std::strlen(title)))) {
+    glp::set_last_error("not valid UTF-8");
+    return GLP_ERR_INVALID_ARG;
+  }
+  // handlers.rs:88-92 -> MultimodalInput::text -> encode_modality_sequence (tokenizer.rs:454-566)
+  std::vector<int32_t> ids;
+  const std::string formatted = glp::format_task(task, title, std::string_view(text, text_len));
+  const std::string err = glp::tokenize_text(tok, formatted, GLP_TOKENS_SEQUENCE, &ids);
+  if (!err.empty()) {
+    glp::set_last_error(err);
+    return GLP_ERR_INVALID_ARG;
+  }
+  if (ids.size() > static_cast<size_t>(GLP_DEFAULT_MAX_SEQ_LEN)) {
+    glp::set_last_error("Text sequence length (" + std::to_string(ids.size()) +
+                        " tokens) exceeds maximum context limit (" + std::to_string(GLP_DEFAULT_MAX_SEQ_LEN) +
+                        " tokens)");
+    return GLP_ERR_CONTEXT_LIMIT;
+  }
+  return glp_engine_embed(e, ids.data(), static_cast<int>(ids.size()), truncate_dim, out);
 }
 
 int glp_engine_stats(glp_engine* e, int64_t* requests, int64_t* batches, int* largest_batch) {

@@ -120,13 +120,23 @@ bool GgufFile::open(const char* path, std::string* err) {
         break;
       }
       for (uint64_t j = 0; j < v.arr_len; ++j) {
+        if (v.arr_type == 8) {  // strings stay in the mapping
+          const uint64_t n = c.get<uint64_t>();
+          if (!c.ok || static_cast<uint64_t>(c.end - c.p) < n) {
+            c.ok = false;
+            break;
+          }
+          v.strs.emplace_back(reinterpret_cast<const char*>(c.p), n);
+          c.p += n;
+          continue;
+        }
         double x = 0;
         std::string s;
         if (!read_scalar(c, v.arr_type, &x, &s)) {
           c.ok = false;
           break;
         }
-        if (v.arr_type != 8) v.arr.push_back(x);
+        v.arr.push_back(x);
       }
     } else if (!read_scalar(c, v.type, &v.num, &v.str)) {
       c.ok = false;

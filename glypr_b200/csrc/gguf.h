@@ -7,6 +7,7 @@
 #include <cstring>
 #include <map>
 #include <string>
+#include <string_view>
 #include <vector>
 
 namespace glp {
@@ -19,7 +20,8 @@ struct GgufValue {
   std::string str;
   int arr_type = -1;
   uint64_t arr_len = 0;
-  std::vector<double> arr;  // numeric / bool array elements (string arrays keep only the length)
+  std::vector<double> arr;  // numeric / bool array elements
+  std::vector<std::string_view> strs;  // string array elements (views into the mapped file)
 };
 
 struct GgufTensor {

@@ -13,6 +13,10 @@
 * serving   the dynamic-batching engine (glp_engine_*): client threads each embedding single
             512-token Q8_0 sequences through InferenceEngine; requests/s, batch sizes and
             per-request latency percentiles (host wall clock: end to end);
+* text      texts -> embeddings (glp_embed_texts): the host tokenizer's throughput on 1 and all
+            cores (and the `tokenizers` library's per-text loop, the reference's sequential
+            tokenisation, when importable), then 256 synthetic ~512-token texts end to end with the
+            BPE vocabulary of tests/golden/tokenizer_golden.json written into the model file;
 * config 4  BF16 weights, one 8192-token sequence (sliding window 512 on local layers, full on
             global): latency, then per-kernel ms / TFLOP/s / GB/s from the library's own CUDA-event
             profile (a separate pass, so the latency carries no profiling overhead).
@@ -230,6 +234,76 @@ def serving(emb, report, clients=64, per_client=64, max_batch=512):
     report.append("")
 
 
+def _synthetic_texts(n, n_words, seed):
+    rng = np.random.default_rng(seed)
+    syl = ["ka", "lo", "mi", "ne", "ru", "sta", "tion", "er", "ing", "the", "and", "qu", "str", "ph", "ed",
+           "é", "ü", "ß", "κα", "σο", "при", "вет", "東京", "研究", "3.14", "(a,b)", "->", "🙂"]
+    out = []
+    for _ in range(n):
+        words = ["".join(rng.choice(syl, size=rng.integers(1, 4))) for _ in range(n_words)]
+        out.append(" ".join(words))
+    return out
+
+
+def text_path(torch, model_dir, report, n_texts=256):
+    golden = os.path.join(ROOT, "tests", "golden", "tokenizer_golden.json")
+    vocab = next(s for s in json.load(open(golden, encoding="utf-8"))["sets"] if s["name"] == "trained")
+    path = os.path.join(model_dir, "baseline_q8_0_bpe.gguf")
+    if not os.path.exists(path):
+        synth.write_gguf(path, synth.BASELINE, tokenizer=(vocab["tokens"], vocab["merges"]))
+    texts = _synthetic_texts(n_texts, 220, synth.MASTER_SEED + 77)
+    nbytes = sum(len(t.encode()) for t in texts)
+
+    def best(fn, reps=5):
+        t = []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            fn()
+            t.append(time.perf_counter() - t0)
+        return min(t)
+
+    with api.Tokenizer.from_gguf(path) as tok:
+        ids = tok.encode_batch(texts, api.GLP_TOKENS_SEQUENCE)
+        n_ids = sum(len(r) for r in ids)
+        rows = [("glp_tokenize_batch, 1 thread", best(lambda: tok.encode_batch(texts, 2, n_threads=1)))]
+        rows.append((f"glp_tokenize_batch, all {os.cpu_count()} host threads",
+                     best(lambda: tok.encode_batch(texts, 2, n_threads=0))))
+        try:
+            from tokenizers import Tokenizer, models, normalizers, pre_tokenizers
+            v = {}
+            for i, t in enumerate(vocab["tokens"]):
+                v[t] = i
+            lib = Tokenizer(models.BPE(vocab=v, merges=[tuple(m.split(" ")) for m in vocab["merges"]],
+                                       unk_token="<unk>", fuse_unk=True, byte_fallback=True))
+            lib.normalizer = normalizers.Replace(" ", "\u2581")
+            lib.pre_tokenizer = pre_tokenizers.Split(" ", behavior="merged_with_previous", invert=False)
+            rows.append(("`tokenizers` 0.22 per-text loop (the reference's tokenisation), 1 thread",
+                         best(lambda: [lib.encode(t) for t in texts], 3)))
+        except ImportError:
+            pass
+        report.append("## Text front end — host tokenizer and texts -> embeddings\n")
+        report.append(f"{n_texts} synthetic texts, {nbytes / n_texts:.0f} bytes and {n_ids / n_texts:.0f} ids each "
+                      f"(BPE vocabulary of {len(vocab['tokens'])} tokens, {len(vocab['merges'])} merges).\n")
+        report.append("| tokenizer | ms per batch | MB/s | ids/s |\n|---|---:|---:|---:|")
+        for name, t in rows:
+            report.append(f"| {name} | {t * 1e3:.1f} | {nbytes / t / 1e6:.1f} | {n_ids / t / 1e6:.2f} M |")
+        report.append("")
+        with api.GlyprEmbedder.load_gguf(path, [0]) as emb:
+            for _ in range(3):
+                emb.embed_texts(tok, texts)
+            t_all = best(lambda: emb.embed_texts(tok, texts), 5)
+            lens = np.array([len(r) for r in ids], np.int32)
+            padded = np.zeros((n_texts, int(lens.max())), np.int32)
+            for i, r in enumerate(ids):
+                padded[i, :len(r)] = r
+            t_ids = best(lambda: emb.embed_tokens(padded, lens), 5)
+        report.append("| path | ms per batch | embeddings/s |\n|---|---:|---:|")
+        report.append(f"| glp_embed_texts (tokenise on all host threads + embed) | {t_all * 1e3:.1f} | "
+                      f"{n_texts / t_all:.0f} |")
+        report.append(f"| glp_embed_tokens on the same ids | {t_ids * 1e3:.1f} | {n_texts / t_ids:.0f} |")
+        report.append("")
+
+
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--model-dir", default=os.environ.get("GLYPR_BENCH_DIR", "/tmp/glypr_models"))
@@ -257,6 +331,8 @@ def main(argv=None) -> None:
                 config3(torch, emb, report)
             if "serving" in want:
                 serving(emb, report)
+    if "text" in want:
+        text_path(torch, args.model_dir, report)
     if 2 in want:
         config2(torch, report)
     if 4 in want:

@@ -243,8 +243,15 @@ def generate_tensor(cfg: EncoderConfig, seed: int, index: int, shape, kind: str)
     raise ValueError(cfg.weight_type)
 
 
-def metadata(cfg: EncoderConfig) -> List[bytes]:
+def metadata(cfg: EncoderConfig, tokenizer: Optional[Tuple[Sequence[str], Sequence[str]]] = None) -> List[bytes]:
+    """GGUF key/values; ``tokenizer`` = (tokens, merges) stores a real BPE vocabulary (padded
+    with filler tokens to ``cfg.vocab``) instead of the filler-only token table."""
     a = "gemma-embedding2."
+    tokens = [f"<t{i}>" for i in range(cfg.vocab)]
+    if tokenizer is not None:
+        if len(tokenizer[0]) > cfg.vocab:
+            raise ValueError("tokenizer vocabulary larger than the model's")
+        tokens = list(tokenizer[0]) + tokens[len(tokenizer[0]):]
     kvs = [
         _kv("general.architecture", _STR, "gemma-embedding2"),
         _kv("general.name", _STR, "glypr-b200 synthetic encoder"),
@@ -264,11 +271,13 @@ def metadata(cfg: EncoderConfig) -> List[bytes]:
         _kv(a + "attention.sliding_window_pattern", _ARR,
             (_BOOL, [cfg.layer_is_sliding(i) for i in range(cfg.n_layers)])),
         _kv("tokenizer.ggml.model", _STR, "synthetic"),
-        _kv("tokenizer.ggml.tokens", _ARR, (_STR, [f"<t{i}>" for i in range(cfg.vocab)])),
+        _kv("tokenizer.ggml.tokens", _ARR, (_STR, tokens)),
         _kv("tokenizer.ggml.padding_token_id", _U32, 0),
         _kv("tokenizer.ggml.bos_token_id", _U32, 2),
         _kv("tokenizer.ggml.eos_token_id", _U32, 1),
     ]
+    if tokenizer is not None:
+        kvs.append(_kv("tokenizer.ggml.merges", _ARR, (_STR, list(tokenizer[1]))))
     return kvs
 
 
@@ -285,12 +294,14 @@ def _nbytes(shape, ggml_type) -> int:
 
 def write_gguf(path: str, cfg: EncoderConfig = BASELINE, seed: int = MASTER_SEED,
                drop: Iterable[str] = (), extra_f32: Sequence[Tuple[str, Tuple[int, ...]]] = (),
-               f32_mats: Iterable[str] = ()) -> str:
+               f32_mats: Iterable[str] = (),
+               tokenizer: Optional[Tuple[Sequence[str], Sequence[str]]] = None) -> str:
     """Write the synthetic encoder to ``path`` (returns ``path``).
 
     ``drop`` omits metadata keys or tensors by name, ``extra_f32`` appends zero F32 tensors
     and ``f32_mats`` stores the named matrices as F32 instead of Q8_0/BF16 -- used by the
-    host-side fault-injection tests to build malformed files."""
+    host-side fault-injection tests to build malformed files; ``tokenizer`` = (tokens,
+    merges) writes a BPE vocabulary into the tokenizer keys."""
     drop = set(drop)
     f32_mats = set(f32_mats)
     order = [o for o in _tensor_order(cfg) if o[0] not in drop]
@@ -308,7 +319,7 @@ def write_gguf(path: str, cfg: EncoderConfig = BASELINE, seed: int = MASTER_SEED
         order.append((name, shape, "zero"))
         offset += _nbytes(shape, GGML_F32)
         offset = (offset + ALIGNMENT - 1) // ALIGNMENT * ALIGNMENT
-    kvs = [kv for kv in metadata(cfg) if _kv_key(kv) not in drop]
+    kvs = [kv for kv in metadata(cfg, tokenizer) if _kv_key(kv) not in drop]
     header = struct.pack("<IIQQ", GGUF_MAGIC, GGUF_VERSION, len(infos), len(kvs)) + b"".join(kvs)
     tinfo = b""
     for name, shape, t, off in infos:

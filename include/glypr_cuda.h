@@ -19,6 +19,7 @@
 #define GLYPR_CUDA_H_
 
 #include <stdint.h>
+#include <stddef.h>
 
 #ifdef __cplusplus
 extern "C" {
@@ -154,6 +155,77 @@ int glp_engine_stats(glp_engine* e, int64_t* requests, int64_t* batches, int* la
 /* Answer every queued request, stop the worker and free the engine (NULL is a no-op).  No
  * call may use the engine after this returns. */
 void glp_engine_destroy(glp_engine* e);
+
+/* ---- text front end: GGUF tokenizer and task prompts (tokenizer.rs, task.rs) ---- */
+
+typedef struct glp_tokenizer glp_tokenizer;
+
+/* Sequence forms of a text (token ids 0 = pad, 1 = EOS, 2 = BOS, tokenizer.rs:588-590). */
+#define GLP_TOKENS_BARE 0     /* the BPE ids alone (Tokenizer::encode on the text) */
+#define GLP_TOKENS_SINGLE 1   /* BOS + ids + EOS, BOS only when the first id is not 2 and EOS only
+                               * when the last is not 1: GlyprTokenizer::encode (tokenizer.rs:162-177),
+                               * the single-text path (embed_text / embed_query, lib.rs:967-968) */
+#define GLP_TOKENS_SEQUENCE 2 /* BOS + ids + EOS always: encode_modality_sequence for a text part
+                               * (tokenizer.rs:454-566), the batch and server path (lib.rs:833) */
+#define GLP_DEFAULT_MAX_SEQ_LEN 8320 /* DEFAULT_MAX_SEQ_LEN = 8192 + 128 (lib.rs:47) */
+
+/* The tokenizer GlyprTokenizer::from_gguf_metadata builds (tokenizer.rs:77-138) from the
+ * GGUF's tokenizer.ggml.tokens and tokenizer.ggml.merges: BPE with byte fallback and fused
+ * "<unk>", spaces normalised to U+2581.  Errors: a missing key or a non-array value
+ * (GLP_ERR_FORMAT, the reference's messages), a merge whose parts or concatenation are not
+ * tokens ("BPE build error: Token `x` out of vocabulary"). */
+int glp_tokenizer_from_gguf(const char* gguf_path, glp_tokenizer** out);
+
+/* The same from in-memory arrays (NUL-terminated UTF-8 tokens; merges as "left right"). */
+int glp_tokenizer_from_vocab(const char* const* tokens, int n_tokens, const char* const* merges, int n_merges,
+                             glp_tokenizer** out);
+
+void glp_tokenizer_free(glp_tokenizer* tok);
+
+/* Vocabulary entries and merges in use. */
+int glp_tokenizer_info(const glp_tokenizer* tok, int* n_tokens, int* n_merges);
+
+/* Token ids of one UTF-8 text in a GLP_TOKENS_* form into ids[cap]; *n_ids = the count (also
+ * when the buffer is too small, which fails with GLP_ERR_INVALID_ARG).  A form never yields
+ * more than 3 * text_len + 2 ids (a space with no token falls back to the 3 bytes of
+ * U+2581).  A character with no token, no byte tokens and no "<unk>" fails with
+ * "Encode error: Unk token `<unk>` not found in the vocabulary". */
+int glp_tokenize(const glp_tokenizer* tok, const char* text, size_t text_len, int form, int32_t* ids, int cap,
+                 int* n_ids);
+
+/* A batch of texts tokenised on n_threads host threads (0 = all cores), packed back to back:
+ * text i's ids are ids[offsets[i] .. offsets[i+1]) (offsets [n_texts + 1]).  ids_cap =
+ * 3 * sum(text_lens) + 2 * n_texts always suffices.  limit > 0 fails the first text (in order)
+ * with more ids with GLP_ERR_CONTEXT_LIMIT ("Batch item i sequence length (n tokens) exceeds
+ * maximum context limit (limit tokens)", encode_batch_padded_with_limit, tokenizer.rs:182-222);
+ * an empty batch fails with "Cannot encode an empty batch". */
+int glp_tokenize_batch(const glp_tokenizer* tok, const char* const* texts, const size_t* text_lens, int n_texts,
+                       int form, int limit, int n_threads, int32_t* ids, size_t ids_cap, int64_t* offsets);
+
+/* Prompt formatting into out[cap] (NUL-terminated; *n_out = the length without the NUL, also
+ * when out is too small).  glp_format_query: the task's prompt from GlyprTokenizer's table,
+ * else "task: <task lowercased> | query: " (tokenizer.rs:13-64, 144-152); glp_format_document:
+ * "title: <title or none> | text: " (tokenizer.rs:154-160); glp_task_format:
+ * Task::from_name_and_title(task, title).format_text(text) (task.rs:21-73), task NULL = Raw. */
+int glp_format_query(const char* query, size_t query_len, const char* task, char* out, size_t cap, size_t* n_out);
+int glp_format_document(const char* content, size_t content_len, const char* title, char* out, size_t cap,
+                        size_t* n_out);
+int glp_task_format(const char* task, const char* title, const char* text, size_t text_len, char* out, size_t cap,
+                    size_t* n_out);
+
+/* Texts -> embeddings: tokenise in `form` (GLP_TOKENS_SINGLE for the reference's single-text
+ * calls, GLP_TOKENS_SEQUENCE for its batch calls), check max_seq_len (0 = 8320) with the
+ * reference's message for that path (lib.rs:969-976, 837-844, 551-558), then glp_embed_tokens.
+ * Texts are embedded as given: apply the prompt formatters first. */
+int glp_embed_texts(glp_ctx* ctx, const glp_tokenizer* tok, const char* const* texts, const size_t* text_lens,
+                    int n_texts, int form, int max_seq_len, int out_dim, float* out);
+
+/* One text request through the engine, as the server's text items go (handlers.rs:88-92,
+ * engine.rs:296-325): Task::from_name_and_title(task, title) formats it (task NULL = Raw),
+ * GLP_TOKENS_SEQUENCE tokenises it on the calling thread, then glp_engine_embed.  Longer than
+ * 8320 ids: GLP_ERR_CONTEXT_LIMIT before it is queued. */
+int glp_engine_embed_text(glp_engine* e, const glp_tokenizer* tok, const char* text, size_t text_len, const char* task,
+                          const char* title, int truncate_dim, float* out);
 
 /* ---- kernel-level entry points (microbenchmarks and tests; current device) ---- */
 
