@@ -365,6 +365,37 @@ __device__ __forceinline__ void cluster_sync_all() {
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
+// 32-bit store into another CTA's shared memory whose completion is counted (4 bytes of
+// transaction) on an mbarrier of that CTA; the count carries release semantics at cluster scope
+__device__ __forceinline__ void st_async_b32(uint32_t cluster_addr, uint32_t v, uint32_t cluster_mbar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(cluster_addr),
+               "r"(v), "r"(cluster_mbar)
+               : "memory");
+}
+// Bounded wait with acquire at cluster scope: data that other CTAs of the cluster stored into
+// this CTA's shared memory (st_async_b32 on this barrier) is visible after it returns true.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  auto try_wait = [&]() {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+  };
+  if (try_wait()) return true;
+  const uint64_t t0 = globaltimer();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 32; ++i)
+      if (try_wait()) return true;
+    if (*abort) return false;
+    if (globaltimer() - t0 > GLP_WAIT_TIMEOUT_NS) return false;
+  }
+}
 // 2-D tile load into this CTA's shared memory whose completion is counted on an mbarrier of
 // either CTA of the pair (here: the leader's full barrier)
 __device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map, uint32_t mbar_cluster,

@@ -40,6 +40,13 @@ struct GemmParams {
   int n_q_heads, n_kv_heads;
   float eps;
   int* status;  // device status word (error codes above)
+  // gemm_rownorm_kernel: residual rows (updated in place), next pre-normed rows, norm gains
+  __nv_bfloat16* h;
+  __half* x_next;
+  const float* w_post;
+  const float* w_next;
+  float layer_scalar;
+  int rownorm_direct;  // 1: always the exact two-exchange row scale (testing)
 };
 
 template <int BN>
@@ -667,6 +674,463 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
 
   // neither CTA leaves (or frees tensor memory) while the other may still touch its shared
   // memory, barriers or tensor memory
+  tc_fence_before();
+  cluster_sync_all();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------- row-norm GEMM
+// y = A * B^T with N == 768 (three 256-column blocks), fused with the post-norm + residual +
+// next pre-norm that follows the O and down projections (norm.rs:22-94, layer.rs:20-50):
+//   s  = rsqrt(mean(y^2) + eps),  hv = (h + y * s * w_post) * lambda,  h <- bf16(hv),
+//   x  = f16(hv * rsqrt(mean(hv^2) + eps) * w_next)
+// so y never goes to HBM and the row pass over h happens in the GEMM's shadow.
+// A cluster of 6 CTAs = 3 CTA pairs: pair j computes columns [256 j, 256 j + 256) of a
+// 256-row tile exactly as gemm_pair_kernel does (cta_group::2, leader = the even rank), so the
+// three CTAs with the same in-pair rank hold the same 128 rows' 768 columns.  Both row scales
+// come from one exchange per tile: with u = y * w_post, sum(hv^2) = lambda^2 (sum h^2 +
+// 2 s sum(h u) + s^2 sum u^2), so every CTA sends the four partial sums (y^2, h^2, h u, u^2) of
+// its columns to the other two (st.async into their slots, counted on their exchange
+// mbarrier) and each adds the three in pair order: all three derive bit-identical scales.
+// When the expansion cancels for a row (sum hv^2 below 2^-8 of its positive terms, where its
+// rounding would show), that row's quad of 32 rows in the three CTAs -- deciding on identical
+// totals -- takes a second exchange of the directly summed hv^2, which that row then uses
+// (GemmParams::rownorm_direct selects it for every row).
+// The residual rows of the next tile are fetched by TMA into each epilogue warp's two 4 KB
+// boxes while the MMAs run; the output rows are staged through the same boxes.  Epilogue warp
+// (quad q, half c) owns rows 32q..32q+31 and the 128 columns 128c.. of its CTA's 256.
+struct GemmRowCfg {
+  static constexpr int STAGES = 4;
+  static constexpr uint32_t A_BYTES = 128 * 64 * 2;
+  static constexpr uint32_t B_BYTES = 128 * 64 * 2;
+  static constexpr uint32_t TMEM_COLS = 512;
+  static constexpr uint32_t HBUF_OFFSET = STAGES * (A_BYTES + B_BYTES);  // 1024-aligned
+  static constexpr uint32_t HBUF_WARP = 2 * 32 * 128;                     // two 32-row x 128-B boxes
+  static constexpr uint32_t BAR_OFFSET = HBUF_OFFSET + 8 * HBUF_WARP;
+  static constexpr uint32_t RED4_OFFSET = BAR_OFFSET + 512;   // float4 [acc buf][half][row]
+  static constexpr uint32_t RED1_OFFSET = RED4_OFFSET + 2 * 2 * 128 * 16;  // float [buf][half][row]
+  static constexpr uint32_t XV_OFFSET = RED1_OFFSET + 2 * 2 * 128 * 4;     // float4 [buf][pair][row]
+  static constexpr uint32_t XT_OFFSET = XV_OFFSET + 2 * 3 * 128 * 16;      // float [buf][pair][row]
+  static constexpr uint32_t XS_OFFSET = XT_OFFSET + 2 * 3 * 128 * 4;       // float [buf][pair][half][row]
+  static constexpr uint32_t W_OFFSET = XS_OFFSET + 2 * 3 * 2 * 128 * 4;    // float [post | next][256]
+  static constexpr size_t SMEM = W_OFFSET + 2 * 256 * 4;
+  // bytes each CTA receives per exchange from the other two: sums (half-0 warps, 16 B a row)
+  // and arrival tokens (half-1 warps, 4 B a row); a quad's direct exchange: 4 B from both of
+  // the quad's warps
+  static constexpr uint32_t XCH_TX = 2 * (128 * 16 + 128 * 4);
+  static constexpr uint32_t XS_TX = 2 * (2 * 32 * 4);
+};
+
+__device__ __forceinline__ void st_async_v4(uint32_t cluster_addr, float4 v, uint32_t cluster_mbar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+                   cluster_addr),
+               "r"(__float_as_uint(v.x)), "r"(__float_as_uint(v.y)), "r"(__float_as_uint(v.z)),
+               "r"(__float_as_uint(v.w)), "r"(cluster_mbar)
+               : "memory");
+}
+
+// p.m_tiles counts 256-row tiles; p.N == 768; p.C is unused (outputs go to p.h and p.x_next).
+template <typename T>
+__global__ void __cluster_dims__(6, 1, 1) __launch_bounds__(kGemmThreads, 1)
+    gemm_rownorm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmH, const GemmParams p) {
+  using Cfg = GemmRowCfg;
+  constexpr int STAGES = Cfg::STAGES;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  if (smem_u32(smem_raw) & 1023) {  // the same in every CTA: all leave before any cluster step
+    if (threadIdx.x == 0) record_error(p.status, kErrBadArgs);
+    return;
+  }
+  uint8_t* smem = smem_raw;
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * Cfg::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::BAR_OFFSET);  // used in the pair leader
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;  // leader: 8 local + 1 forwarded from the peer; peer: 8 local
+  uint64_t* drain = tempty + 2;
+  uint64_t* xbar = drain + 1;    // [4] rendezvous of a quad's two column halves
+  uint64_t* xf0 = xbar + 4;      // [2] per accumulator buffer: the tile's sums exchange
+  uint64_t* xf1 = xf0 + 2;       // [2][4] per buffer and quad: the direct exchange (rare)
+  uint64_t* hbar = xf1 + 8;      // [8] residual-row loads, one per epilogue warp
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(hbar + 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const uint32_t prank = rank & 1u;            // which 128 rows of the pair tile
+  const uint32_t lead = rank & ~1u;            // the pair's leader
+  const int pj = static_cast<int>(rank >> 1);  // column block
+  const bool leader = prank == 0;
+  const int cl = static_cast<int>(cluster_id_x());
+  const int ncl = static_cast<int>(n_clusters_x());
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], leader ? 9 : 8);
+      mbar_init(&xf0[b], 1);
+      for (int q = 0; q < 4; ++q) mbar_init(&xf1[b * 4 + q], 1);
+    }
+    mbar_init(drain, 1);
+    for (int q = 0; q < 4; ++q) mbar_init(&xbar[q], 2);
+    for (int w = 0; w < 8; ++w) mbar_init(&hbar[w], 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmH);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ TMA producer (every CTA)
+      int s = 0;
+      uint32_t ph = 0;
+      for (int mt = cl; mt < p.m_tiles && !*abort_flag; mt += ncl) {
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) {
+            record_error(p.status, kErrTimeoutProducer);
+            *abort_flag = 1;
+            break;
+          }
+          if (leader) mbar_arrive_expect_tx(&full[s], 2 * (Cfg::A_BYTES + Cfg::B_BYTES));
+          const uint32_t fbar = mapa_shared(smem_u32(&full[s]), lead);
+          tma_load_2d_pair(sA + s * Cfg::A_BYTES, &tmA, fbar, kb * 64, mt * 256 + static_cast<int>(prank) * 128);
+          tma_load_2d_pair(sB + s * Cfg::B_BYTES, &tmB, fbar, kb * 64, pj * 256 + static_cast<int>(prank) * 128);
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ------------------------------------------------------------ MMA issuer (pair leaders)
+      constexpr uint32_t idesc = idesc_f16(256, 256, Half16<T>::kIsBf16);
+      const uint32_t peer = rank | 1u;
+      int s = 0;
+      uint32_t ph = 0;
+      int ab = 0;
+      uint32_t aph = 0;
+      bool issued = false;
+      for (int mt = cl; mt < p.m_tiles && !*abort_flag; mt += ncl) {
+        if (!mbar_wait(&tempty[ab], aph ^ 1, abort_flag)) {
+          record_error(p.status, kErrTimeoutMma);
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(ab * 256);
+        bool ok = true;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&full[s], ph, abort_flag)) {
+            record_error(p.status, kErrTimeoutMma);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t adesc = desc_kmajor_sw128(smem_u32(sA + s * Cfg::A_BYTES));
+          const uint64_t bdesc = desc_kmajor_sw128(smem_u32(sB + s * Cfg::B_BYTES));
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            umma_f16_pair(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
+          issued = true;
+          umma_commit_pair(smem_u32(&empty[s]));
+          umma_commit_pair(mapa_shared(smem_u32(&empty[s]), peer));
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(smem_u32(&tfull[ab]));
+        umma_commit_pair(mapa_shared(smem_u32(&tfull[ab]), peer));
+        ab ^= 1;
+        if (ab == 0) aph ^= 1;
+      }
+      if (issued) {
+        umma_commit_pair(smem_u32(drain));
+        if (!mbar_wait(drain, 0, abort_flag) && !*abort_flag) record_error(p.status, kErrTimeoutDrain);
+      }
+    } else if (lane == 0) {
+      // ------------------------------------------------------------ release forwarder (peers)
+      const uint32_t lead_tempty0 = mapa_shared(smem_u32(&tempty[0]), lead);
+      int ab = 0;
+      uint32_t aph = 0;
+      for (int mt = cl; mt < p.m_tiles; mt += ncl) {
+        if (!mbar_wait(&tempty[ab], aph, abort_flag)) {
+          record_error(p.status, kErrTimeoutEpilogue);
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        tc_fence_before();
+        mbar_arrive_cluster(lead_tempty0 + static_cast<uint32_t>(ab * sizeof(uint64_t)));
+        ab ^= 1;
+        if (ab == 0) aph ^= 1;
+      }
+    }
+  } else {
+    // -------------------------------------------------------------- epilogue warps
+    const int ew = warp - 2;
+    const int quad = warp & 3;
+    const int half = ew >> 2;
+    const int row_in_tile = quad * 32 + lane;
+    const int col0 = pj * 256 + half * 128;  // this warp's first column of the 768
+    uint8_t* hb = smem + Cfg::HBUF_OFFSET + ew * Cfg::HBUF_WARP;
+    float4* red4 = reinterpret_cast<float4*>(smem + Cfg::RED4_OFFSET);
+    float* red1 = reinterpret_cast<float*>(smem + Cfg::RED1_OFFSET);
+    float4* xv = reinterpret_cast<float4*>(smem + Cfg::XV_OFFSET);
+    float* xt = reinterpret_cast<float*>(smem + Cfg::XT_OFFSET);
+    float* xs = reinterpret_cast<float*>(smem + Cfg::XS_OFFSET);
+    float* wsm = reinterpret_cast<float*>(smem + Cfg::W_OFFSET);
+    {  // this CTA's 256 columns of both gains, once per launch (the 8 epilogue warps)
+      const int t = threadIdx.x - 64;
+      wsm[t] = p.w_post[pj * 256 + t];
+      wsm[256 + t] = p.w_next[pj * 256 + t];
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+    }
+    const float* wp = wsm + half * 128;
+    const float* wn = wsm + 256 + half * 128;
+    const size_t ldb = static_cast<size_t>(p.N) * 2;
+    const float inv_n = 1.0f / static_cast<float>(p.N);
+    const float lam = p.layer_scalar;
+    auto prefetch_h = [&](int mt) {  // this warp's 32 rows x 128 columns of the residual
+      if (lane == 0) {
+        const int r0 = mt * 256 + static_cast<int>(prank) * 128 + quad * 32;
+        mbar_arrive_expect_tx(&hbar[ew], Cfg::HBUF_WARP);
+        tma_load_2d(hb, &tmH, &hbar[ew], col0, r0);
+        tma_load_2d(hb + 4096, &tmH, &hbar[ew], col0 + 64, r0);
+      }
+    };
+    // the residual chunk k (8 columns) of box g for this lane's row
+    auto h_chunk = [&](int g, int k) {
+      return *reinterpret_cast<const uint4*>(hb + g * 4096 + lane * 128 + ((k ^ (lane & 7)) << 4));
+    };
+    uint32_t xph = 0, xf1ph = 0;
+    int ab = 0;
+    uint32_t aph = 0, hph = 0;
+    bool h_pending = false, aborted = false, direct_armed = false;
+    if (cl < p.m_tiles) {
+      prefetch_h(cl);
+      h_pending = true;
+    }
+    for (int mt = cl; mt < p.m_tiles; mt += ncl) {
+      if (ew == 0 && lane == 0) mbar_arrive_expect_tx(&xf0[ab], Cfg::XCH_TX);
+      direct_armed = false;
+      bool ok = __all_sync(0xffffffffu, mbar_wait(&tfull[ab], aph, abort_flag));
+      if (ok) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&hbar[ew], hph, abort_flag));
+        hph ^= 1;
+        h_pending = false;
+      }
+      const uint32_t tacc =
+          tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(ab * 256 + half * 128);
+      float s = 0.f, inv_h = 0.f;
+      if (ok) {
+        tc_fence_after();
+        // pass A: partial sums of y^2, h^2, h u, u^2 over this warp's 128 columns
+        float y2 = 0.f, h2 = 0.f, hu = 0.f, u2 = 0.f;
+#pragma unroll 1
+        for (int q = 0; q < 4; ++q) {  // 32 columns: box q / 2, chunks 4 (q % 2) ..
+          uint32_t a[32];
+          tmem_ld32(tacc + 32 * q, a);
+          tmem_ld_wait_tied(a);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint4 hq = h_chunk(q >> 1, 4 * (q & 1) + k);
+            const __nv_bfloat16* he = reinterpret_cast<const __nv_bfloat16*>(&hq);
+            const float4 w0 = *reinterpret_cast<const float4*>(wp + 32 * q + 8 * k);
+            const float4 w1 = *reinterpret_cast<const float4*>(wp + 32 * q + 8 * k + 4);
+            const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float y = u2f(a[8 * k + j]);
+              const float h = __bfloat162float(he[j]);
+              const float u = y * wv[j];
+              y2 = fmaf(y, y, y2);
+              h2 = fmaf(h, h, h2);
+              hu = fmaf(h, u, hu);
+              u2 = fmaf(u, u, u2);
+            }
+          }
+        }
+        // exchange: quad halves -> this CTA's sums -> the other two CTAs of the row triple
+        red4[(ab * 2 + half) * 128 + row_in_tile] = make_float4(y2, h2, hu, u2);
+        ok = pair_rendezvous(&xbar[quad], xph, abort_flag);
+        if (ok) {
+          const float4 r0 = red4[(ab * 2) * 128 + row_in_tile], r1 = red4[(ab * 2 + 1) * 128 + row_in_tile];
+          const float4 mine = make_float4(r0.x + r1.x, r0.y + r1.y, r0.z + r1.z, r0.w + r1.w);
+          const uint32_t bar = smem_u32(&xf0[ab]);
+#pragma unroll
+          for (int k = 1; k <= 2; ++k) {
+            const uint32_t dst = static_cast<uint32_t>(((pj + k) % 3) * 2) + prank;
+            if (half == 0)
+              st_async_v4(mapa_shared(smem_u32(xv + (ab * 3 + pj) * 128 + row_in_tile), dst), mine,
+                          mapa_shared(bar, dst));
+            else
+              st_async_b32(mapa_shared(smem_u32(xt + (ab * 3 + pj) * 128 + row_in_tile), dst), 0u,
+                           mapa_shared(bar, dst));
+          }
+          ok = __all_sync(0xffffffffu, mbar_wait_cluster(&xf0[ab], aph, abort_flag));
+          if (ok) {
+            float4 tot = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int j = 0; j < 3; ++j) {
+              const float4 v = j == pj ? mine : xv[(ab * 3 + j) * 128 + row_in_tile];
+              tot.x += v.x;
+              tot.y += v.y;
+              tot.z += v.z;
+              tot.w += v.w;
+            }
+            s = 1.0f / sqrtf(tot.x * inv_n + p.eps);
+            const float pos = fmaf(s * s, tot.w, tot.y);
+            float ss2 = lam * lam * fmaf(s, fmaf(s, tot.w, 2.0f * tot.z), tot.y);
+            // identical totals (and rows) in the three CTAs, so all of them decide alike; each
+            // row keeps its own choice, so a row's result never depends on its neighbours
+            const bool live = mt * 256 + static_cast<int>(prank) * 128 + row_in_tile < p.M;
+            const bool direct = live && (p.rownorm_direct || !(ss2 > pos * lam * lam * 0.00390625f));
+            // (the same vote in both warps of the quad and in the three CTAs)
+            if (__any_sync(0xffffffffu, direct)) {
+              // exact sum of hv^2 for the quad's rows, second exchange on the quad's barrier
+              uint64_t* qbar = &xf1[ab * 4 + quad];
+              if (half == 0 && lane == 0) mbar_arrive_expect_tx(qbar, Cfg::XS_TX);
+              direct_armed = true;
+              float sq = 0.f;
+#pragma unroll 1
+              for (int q = 0; q < 4; ++q) {
+                uint32_t a[32];
+                tmem_ld32(tacc + 32 * q, a);
+                tmem_ld_wait_tied(a);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                  const uint4 hq = h_chunk(q >> 1, 4 * (q & 1) + k);
+                  const __nv_bfloat16* he = reinterpret_cast<const __nv_bfloat16*>(&hq);
+#pragma unroll
+                  for (int j = 0; j < 8; ++j) {
+                    const float hv = (__bfloat162float(he[j]) + u2f(a[8 * k + j]) * s * wp[32 * q + 8 * k + j]) * lam;
+                    sq = fmaf(hv, hv, sq);
+                  }
+                }
+              }
+              red1[(ab * 2 + half) * 128 + row_in_tile] = sq;
+              ok = pair_rendezvous(&xbar[quad], xph, abort_flag);
+              if (ok) {
+                const float m1 = red1[(ab * 2) * 128 + row_in_tile] + red1[(ab * 2 + 1) * 128 + row_in_tile];
+                const uint32_t bar1 = smem_u32(qbar);
+#pragma unroll
+                for (int k = 1; k <= 2; ++k) {
+                  const uint32_t dst = static_cast<uint32_t>(((pj + k) % 3) * 2) + prank;
+                  st_async_b32(mapa_shared(smem_u32(xs + ((ab * 3 + pj) * 2 + half) * 128 + row_in_tile), dst),
+                               __float_as_uint(m1), mapa_shared(bar1, dst));
+                }
+                const uint32_t par = (xf1ph >> (ab * 4 + quad)) & 1u;
+                ok = __all_sync(0xffffffffu, mbar_wait_cluster(qbar, par, abort_flag));
+                if (ok) {
+                  xf1ph ^= 1u << (ab * 4 + quad);
+                  direct_armed = false;
+                  float sd = 0.f;
+#pragma unroll
+                  for (int j = 0; j < 3; ++j) sd += j == pj ? m1 : xs[((ab * 3 + j) * 2) * 128 + row_in_tile];
+                  if (direct) ss2 = sd;
+                }
+              }
+            }
+            inv_h = 1.0f / sqrtf(ss2 * inv_n + p.eps);
+          }
+        }
+      }
+      if (ok) {
+        // pass C: hv, x = hv * inv_h * w_next (f16) and h = bf16(hv), 64 columns (one box) at a
+        // time; each box is read into registers before the outputs are staged over it
+        const int wrow0 = mt * 256 + static_cast<int>(prank) * 128 + quad * 32;
+        const int rows_valid = min(32, p.M - wrow0);
+        uint8_t* xdst = reinterpret_cast<uint8_t*>(p.x_next) + (static_cast<size_t>(wrow0) * p.N + col0) * 2;
+        uint8_t* hdst = reinterpret_cast<uint8_t*>(p.h) + (static_cast<size_t>(wrow0) * p.N + col0) * 2;
+#pragma unroll 1
+        for (int g = 0; g < 2; ++g) {
+          uint32_t hw[32];
+          uint8_t* box = hb + g * 4096;
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {  // 32 columns per TMEM load
+            uint32_t a[32];
+            tmem_ld32(tacc + 64 * g + 32 * hh, a);
+            tmem_ld_wait_tied(a);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              const int k = 4 * hh + kk;
+              const uint4 hq = h_chunk(g, k);
+              const __nv_bfloat16* he = reinterpret_cast<const __nv_bfloat16*>(&hq);
+              uint32_t xw[4];
+#pragma unroll
+              for (int j = 0; j < 8; j += 2) {
+                const int c = 64 * g + 8 * k + j;
+                const float hv0 = (__bfloat162float(he[j]) + u2f(a[8 * kk + j]) * s * wp[c]) * lam;
+                const float hv1 = (__bfloat162float(he[j + 1]) + u2f(a[8 * kk + j + 1]) * s * wp[c + 1]) * lam;
+                xw[j / 2] = pack_f16(hv0 * inv_h * wn[c], hv1 * inv_h * wn[c + 1]);
+                hw[4 * k + j / 2] = pack_bf16(hv0, hv1);
+              }
+              stage_chunk(box, k, make_uint4(xw[0], xw[1], xw[2], xw[3]));
+            }
+          }
+          flush_rows128(box, xdst + 128 * g, ldb, rows_valid);
+          stage_words32(box, hw);
+          flush_rows128(box, hdst + 128 * g, ldb, rows_valid);
+        }
+      }
+      if (!ok) {
+        if (lane == 0) {
+          record_error(p.status, kErrTimeoutEpilogue);
+          *abort_flag = 1;
+        }
+        aborted = true;
+        break;
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[ab]);
+      if (mt + ncl < p.m_tiles) {  // the next tile's residual rows, over the staged outputs
+        fence_proxy_async_smem();
+        __syncwarp();
+        prefetch_h(mt + ncl);
+        h_pending = true;
+      }
+      ab ^= 1;
+      if (ab == 0) aph ^= 1;
+    }
+    if (aborted) {
+      // After a failed wait the other CTAs may still deliver this tile's sums (they cannot get
+      // further: each exchange needs this CTA's sums first); let those land.
+      int never = 0;
+      mbar_wait_cluster(&xf0[ab], aph, &never);
+      if (direct_armed) mbar_wait_cluster(&xf1[ab * 4 + quad], (xf1ph >> (ab * 4 + quad)) & 1u, &never);
+    }
+    if (h_pending) {  // no load may still be writing this CTA's shared memory when it leaves
+      int never = 0;
+      mbar_wait(&hbar[ew], hph, &never);
+    }
+  }
+
   tc_fence_before();
   cluster_sync_all();
   if (warp == 1) {

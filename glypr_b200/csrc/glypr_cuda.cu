@@ -168,6 +168,7 @@ int ensure_kernel_attrs() {
   GLP_CUDA(cudaFuncSetAttribute(glp::gemm_pair_kernel<glp::kEpiGeglu, __half>, A, sp));
   GLP_CUDA(cudaFuncSetAttribute(glp::gemm_pair_kernel<glp::kEpiStore16, __nv_bfloat16>, A, sp));
   GLP_CUDA(cudaFuncSetAttribute(glp::gemm_pair_kernel<glp::kEpiF32, __nv_bfloat16>, A, sp));
+  GLP_CUDA(cudaFuncSetAttribute(glp::gemm_rownorm_kernel<__half>, A, static_cast<int>(glp::GemmRowCfg::SMEM)));
   GLP_CUDA(cudaFuncSetAttribute(glp::flash_attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 static_cast<int>(glp::kAttnSmem)));
   GLP_CUDA(cudaFuncSetAttribute(glp::flash_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -201,6 +202,59 @@ bool use_pair_gemm(int epi) {
   }();
   if (mode != 1) return mode == 2;
   return epi == glp::kEpiStore16 || epi == glp::kEpiF32;
+}
+
+// Post-norms fused into the O / down GEMMs (gemm_rownorm_kernel) for 768-wide rows; GLP_FUSED_NORM=0
+// runs them as separate row kernels instead.
+bool use_fused_norm() {
+  static const bool on = [] {
+    const char* e = std::getenv("GLP_FUSED_NORM");
+    return !(e && std::string(e) == "0");
+  }();
+  return on;
+}
+
+// Clusters of 6 that can be resident at once (per device, cached): the persistent row-norm
+// GEMM launches that many.
+int rownorm_clusters() {
+  static std::mutex mu;
+  static std::array<int, 64> cache{};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lk(mu);
+  if (dev >= 0 && dev < 64 && cache[dev] > 0) return cache[dev];
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(6 * 24);
+  cfg.blockDim = dim3(glp::kGemmThreads);
+  cfg.dynamicSmemBytes = glp::GemmRowCfg::SMEM;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, glp::gemm_rownorm_kernel<__half>, &cfg) != cudaSuccess || n <= 0) {
+    cudaGetLastError();
+    n = sm_count() / 6;
+  }
+  if (dev >= 0 && dev < 64) cache[dev] = n;
+  return n;
+}
+
+// y = A * B^T (N == 768) fused with the post-norm + residual + next pre-norm: updates p.h in
+// place and writes p.x_next.  `mb_pair` covers B with 128-row boxes, `mh` the residual rows
+// [M, 768] bf16 with 32-row boxes.
+int launch_rownorm_gemm(const CUtensorMap& ma, const CUtensorMap& mb_pair, const CUtensorMap& mh, GemmParams p,
+                        cudaStream_t st) {
+  if (p.M <= 0) return GLP_OK;
+  if (p.N != 768 || p.K % 64 || p.K <= 0) return fail(GLP_ERR_INVALID_ARG, "row-norm GEMM needs N == 768, K % 64 == 0");
+  p.m_tiles = (p.M + 255) / 256;
+  p.n_tiles = 3;
+  p.k_blocks = p.K / 64;
+  static const bool direct = [] {  // GLP_ROWNORM_DIRECT=1: the exact two-exchange scale everywhere
+    const char* e = std::getenv("GLP_ROWNORM_DIRECT");
+    return e && std::string(e) == "1";
+  }();
+  p.rownorm_direct = direct ? 1 : 0;
+  const int clusters = std::min(p.m_tiles, rownorm_clusters());
+  glp::gemm_rownorm_kernel<__half><<<6 * clusters, glp::kGemmThreads, glp::GemmRowCfg::SMEM, st>>>(ma, mb_pair, mh, p);
+  GLP_CUDA(cudaGetLastError());
+  return GLP_OK;
 }
 
 // Launch C = A * B^T with the given epilogue; T is the 16-bit operand type.  `ma` covers
@@ -820,6 +874,11 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
     }
     const double attn_bytes = 2.0 * Td * QKV + 2.0 * Td * AW;
     const double post_bytes = Td * (2.0 * H + 4.0 * H + 2.0 * H);  // y + h in/out + x (16-bit)
+    const double fused_bytes = Td * (4.0 * H + 2.0 * H);              // h in/out + x, no y
+    // the row-norm GEMM needs 768-wide rows and the CTA-pair weight maps
+    const bool fused = use_fused_norm() && H == 768 && use_pair_gemm(glp::kEpiStore16);
+    CUtensorMap m_h;  // the residual rows, 32-row boxes for the fused epilogue's prefetch
+    if (fused) GLP_TRY(make_map16(&m_h, d.h, T, H, H, 32, false));
     for (int l = 0; l < c.n_layers; ++l) {
       LayerW& L = d.layers[l];
       GemmParams p{};
@@ -854,14 +913,25 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
       po.C = d.y;
       po.ldc = H;
       po.status = d.status;
-      GLP_TRY(prof_launch(d, st, kProfGemmO, gemm_flops(Td, H, AW), gemm_bytes(Td, H, AW, 2.0),
-                          [&] { return launch_gemm<__half>(m_attn, L.m_o, bn_for(H), glp::kEpiStore16, po, st, &L.p_o); }));
-      GLP_TRY(prof_launch(d, st, kProfPostNorm, 0.0, post_bytes, [&] {
-        glp::post_norm_residual_kernel<false><<<rows_grid, 256, 0, st>>>(d.y, d.h, L.post_attn, 1.0f, L.ffn_norm,
-                                                                         eps, T, d.x, nullptr);
-        GLP_CUDA(cudaGetLastError());
-        return GLP_OK;
-      }));
+      if (fused) {
+        po.h = d.h;
+        po.x_next = d.x;
+        po.w_post = L.post_attn;
+        po.w_next = L.ffn_norm;
+        po.layer_scalar = 1.0f;
+        po.eps = eps;
+        GLP_TRY(prof_launch(d, st, kProfGemmO, gemm_flops(Td, H, AW), gemm_bytes(Td, H, AW, 0.0) + fused_bytes,
+                            [&] { return launch_rownorm_gemm(m_attn, L.p_o, m_h, po, st); }));
+      } else {
+        GLP_TRY(prof_launch(d, st, kProfGemmO, gemm_flops(Td, H, AW), gemm_bytes(Td, H, AW, 2.0),
+                            [&] { return launch_gemm<__half>(m_attn, L.m_o, bn_for(H), glp::kEpiStore16, po, st, &L.p_o); }));
+        GLP_TRY(prof_launch(d, st, kProfPostNorm, 0.0, post_bytes, [&] {
+          glp::post_norm_residual_kernel<false><<<rows_grid, 256, 0, st>>>(d.y, d.h, L.post_attn, 1.0f, L.ffn_norm,
+                                                                           eps, T, d.x, nullptr);
+          GLP_CUDA(cudaGetLastError());
+          return GLP_OK;
+        }));
+      }
       // gate|up + GeGLU
       GemmParams pg{};
       pg.M = T;
@@ -881,9 +951,20 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
       pd.C = d.y;
       pd.ldc = H;
       pd.status = d.status;
+      const bool last = l + 1 == c.n_layers;
+      if (fused && !last) {
+        pd.h = d.h;
+        pd.x_next = d.x;
+        pd.w_post = L.post_ffw;
+        pd.w_next = d.layers[l + 1].attn_norm;
+        pd.layer_scalar = L.layer_scalar;
+        pd.eps = eps;
+        GLP_TRY(prof_launch(d, st, kProfGemmDown, gemm_flops(Td, H, F), gemm_bytes(Td, H, F, 0.0) + fused_bytes,
+                            [&] { return launch_rownorm_gemm(m_a, L.p_down, m_h, pd, st); }));
+        continue;
+      }
       GLP_TRY(prof_launch(d, st, kProfGemmDown, gemm_flops(Td, H, F), gemm_bytes(Td, H, F, 2.0),
                           [&] { return launch_gemm<__half>(m_a, L.m_down, bn_for(H), glp::kEpiStore16, pd, st, &L.p_down); }));
-      const bool last = l + 1 == c.n_layers;
       GLP_TRY(prof_launch(d, st, kProfPostNorm, 0.0, last ? Td * 8.0 * H : post_bytes, [&] {
         if (!last)
           glp::post_norm_residual_kernel<false><<<rows_grid, 256, 0, st>>>(
