@@ -700,9 +700,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
 // rounding would show), that row's quad of 32 rows in the three CTAs -- deciding on identical
 // totals -- takes a second exchange of the directly summed hv^2, which that row then uses
 // (GemmParams::rownorm_direct selects it for every row).
-// The residual rows of the next tile are fetched by TMA into each epilogue warp's two 4 KB
-// boxes while the MMAs run; the output rows are staged through the same boxes.  Epilogue warp
-// (quad q, half c) owns rows 32q..32q+31 and the 128 columns 128c.. of its CTA's 256.
+// The residual rows are fetched by TMA into each epilogue warp's two 4 KB boxes (64 columns
+// each, one mbarrier per box); the output rows are staged through the same boxes, and each box
+// is refilled with the next tile's rows as soon as its outputs are out, so the loads overlap
+// the rest of the epilogue.  Epilogue warp (quad q, half c) owns rows 32q..32q+31 and the 128
+// columns 128c.. of its CTA's 256; the row arithmetic runs on packed f32x2 pairs.
 struct GemmRowCfg {
   static constexpr int STAGES = 4;
   static constexpr uint32_t A_BYTES = 128 * 64 * 2;
@@ -756,8 +758,8 @@ __global__ void __cluster_dims__(6, 1, 1) __launch_bounds__(kGemmThreads, 1)
   uint64_t* xbar = drain + 1;    // [4] rendezvous of a quad's two column halves
   uint64_t* xf0 = xbar + 4;      // [2] per accumulator buffer: the tile's sums exchange
   uint64_t* xf1 = xf0 + 2;       // [2][4] per buffer and quad: the direct exchange (rare)
-  uint64_t* hbar = xf1 + 8;      // [8] residual-row loads, one per epilogue warp
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(hbar + 8);
+  uint64_t* hbar = xf1 + 8;      // [8][2] residual-row loads, per epilogue warp and box
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(hbar + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -783,7 +785,7 @@ __global__ void __cluster_dims__(6, 1, 1) __launch_bounds__(kGemmThreads, 1)
     }
     mbar_init(drain, 1);
     for (int q = 0; q < 4; ++q) mbar_init(&xbar[q], 2);
-    for (int w = 0; w < 8; ++w) mbar_init(&hbar[w], 1);
+    for (int w = 0; w < 16; ++w) mbar_init(&hbar[w], 1);
     *abort_flag = 0;
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
@@ -915,12 +917,12 @@ __global__ void __cluster_dims__(6, 1, 1) __launch_bounds__(kGemmThreads, 1)
     const size_t ldb = static_cast<size_t>(p.N) * 2;
     const float inv_n = 1.0f / static_cast<float>(p.N);
     const float lam = p.layer_scalar;
-    auto prefetch_h = [&](int mt) {  // this warp's 32 rows x 128 columns of the residual
+    // this warp's 32 rows x 64 columns (box g) of the residual of tile mt
+    auto prefetch_box = [&](int mt, int g) {
       if (lane == 0) {
         const int r0 = mt * 256 + static_cast<int>(prank) * 128 + quad * 32;
-        mbar_arrive_expect_tx(&hbar[ew], Cfg::HBUF_WARP);
-        tma_load_2d(hb, &tmH, &hbar[ew], col0, r0);
-        tma_load_2d(hb + 4096, &tmH, &hbar[ew], col0 + 64, r0);
+        mbar_arrive_expect_tx(&hbar[2 * ew + g], 4096);
+        tma_load_2d(hb + g * 4096, &tmH, &hbar[2 * ew + g], col0 + 64 * g, r0);
       }
     };
     // the residual chunk k (8 columns) of box g for this lane's row
@@ -932,52 +934,63 @@ __global__ void __cluster_dims__(6, 1, 1) __launch_bounds__(kGemmThreads, 1)
     uint32_t aph = 0, hph = 0;
     bool h_pending = false, aborted = false, direct_armed = false;
     if (cl < p.m_tiles) {
-      prefetch_h(cl);
+      prefetch_box(cl, 0);
+      prefetch_box(cl, 1);
       h_pending = true;
     }
     for (int mt = cl; mt < p.m_tiles; mt += ncl) {
       if (ew == 0 && lane == 0) mbar_arrive_expect_tx(&xf0[ab], Cfg::XCH_TX);
       direct_armed = false;
       bool ok = __all_sync(0xffffffffu, mbar_wait(&tfull[ab], aph, abort_flag));
-      if (ok) {
-        ok = __all_sync(0xffffffffu, mbar_wait(&hbar[ew], hph, abort_flag));
-        hph ^= 1;
-        h_pending = false;
-      }
+      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&hbar[2 * ew], hph, abort_flag));
       const uint32_t tacc =
           tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(ab * 256 + half * 128);
       float s = 0.f, inv_h = 0.f;
       if (ok) {
         tc_fence_after();
         // pass A: partial sums of y^2, h^2, h u, u^2 over this warp's 128 columns
-        float y2 = 0.f, h2 = 0.f, hu = 0.f, u2 = 0.f;
+        uint64_t Y2 = 0, H2 = 0, HU = 0, U2 = 0;  // packed pairs of partial sums
 #pragma unroll 1
         for (int q = 0; q < 4; ++q) {  // 32 columns: box q / 2, chunks 4 (q % 2) ..
           uint32_t a[32];
           tmem_ld32(tacc + 32 * q, a);
+          if (q == 2) {  // the second box (fetched last) is needed from here on
+            if (!__all_sync(0xffffffffu, mbar_wait(&hbar[2 * ew + 1], hph, abort_flag))) ok = false;
+          }
           tmem_ld_wait_tied(a);
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             const uint4 hq = h_chunk(q >> 1, 4 * (q & 1) + k);
-            const __nv_bfloat16* he = reinterpret_cast<const __nv_bfloat16*>(&hq);
+            const uint32_t hw4[4] = {hq.x, hq.y, hq.z, hq.w};
             const float4 w0 = *reinterpret_cast<const float4*>(wp + 32 * q + 8 * k);
             const float4 w1 = *reinterpret_cast<const float4*>(wp + 32 * q + 8 * k + 4);
-            const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+            const uint64_t wv[4] = {f2(w0.x, w0.y), f2(w0.z, w0.w), f2(w1.x, w1.y), f2(w1.z, w1.w)};
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const float y = u2f(a[8 * k + j]);
-              const float h = __bfloat162float(he[j]);
-              const float u = y * wv[j];
-              y2 = fmaf(y, y, y2);
-              h2 = fmaf(h, h, h2);
-              hu = fmaf(h, u, hu);
-              u2 = fmaf(u, u, u2);
+            for (int j = 0; j < 4; ++j) {
+              const uint64_t y = f2(u2f(a[8 * k + 2 * j]), u2f(a[8 * k + 2 * j + 1]));
+              const uint64_t h = f2(__uint_as_float(hw4[j] << 16), __uint_as_float(hw4[j] & 0xffff0000u));
+              const uint64_t u = f2_mul(y, wv[j]);
+              Y2 = f2_fma(y, y, Y2);
+              H2 = f2_fma(h, h, H2);
+              HU = f2_fma(h, u, HU);
+              U2 = f2_fma(u, u, U2);
             }
           }
         }
+        hph ^= 1;
+        h_pending = false;
+        float y2, h2, hu, u2, t0, t1;
+        f2_split(Y2, t0, t1);
+        y2 = t0 + t1;
+        f2_split(H2, t0, t1);
+        h2 = t0 + t1;
+        f2_split(HU, t0, t1);
+        hu = t0 + t1;
+        f2_split(U2, t0, t1);
+        u2 = t0 + t1;
         // exchange: quad halves -> this CTA's sums -> the other two CTAs of the row triple
         red4[(ab * 2 + half) * 128 + row_in_tile] = make_float4(y2, h2, hu, u2);
-        ok = pair_rendezvous(&xbar[quad], xph, abort_flag);
+        if (ok) ok = pair_rendezvous(&xbar[quad], xph, abort_flag);
         if (ok) {
           const float4 r0 = red4[(ab * 2) * 128 + row_in_tile], r1 = red4[(ab * 2 + 1) * 128 + row_in_tile];
           const float4 mine = make_float4(r0.x + r1.x, r0.y + r1.y, r0.z + r1.z, r0.w + r1.w);
@@ -1067,6 +1080,7 @@ __global__ void __cluster_dims__(6, 1, 1) __launch_bounds__(kGemmThreads, 1)
         const int rows_valid = min(32, p.M - wrow0);
         uint8_t* xdst = reinterpret_cast<uint8_t*>(p.x_next) + (static_cast<size_t>(wrow0) * p.N + col0) * 2;
         uint8_t* hdst = reinterpret_cast<uint8_t*>(p.h) + (static_cast<size_t>(wrow0) * p.N + col0) * 2;
+        const uint64_t sl2 = f2(s * lam, s * lam), lam2 = f2(lam, lam), inv2 = f2(inv_h, inv_h);
 #pragma unroll 1
         for (int g = 0; g < 2; ++g) {
           uint32_t hw[32];
@@ -1080,15 +1094,26 @@ __global__ void __cluster_dims__(6, 1, 1) __launch_bounds__(kGemmThreads, 1)
             for (int kk = 0; kk < 4; ++kk) {
               const int k = 4 * hh + kk;
               const uint4 hq = h_chunk(g, k);
-              const __nv_bfloat16* he = reinterpret_cast<const __nv_bfloat16*>(&hq);
+              const uint32_t hw4[4] = {hq.x, hq.y, hq.z, hq.w};
+              const float* pw = wp + 64 * g + 8 * k;
+              const float* nw = wn + 64 * g + 8 * k;
+              const float4 p0 = *reinterpret_cast<const float4*>(pw), p1 = *reinterpret_cast<const float4*>(pw + 4);
+              const float4 n0 = *reinterpret_cast<const float4*>(nw), n1 = *reinterpret_cast<const float4*>(nw + 4);
+              const uint64_t pv[4] = {f2(p0.x, p0.y), f2(p0.z, p0.w), f2(p1.x, p1.y), f2(p1.z, p1.w)};
+              const uint64_t nv[4] = {f2(n0.x, n0.y), f2(n0.z, n0.w), f2(n1.x, n1.y), f2(n1.z, n1.w)};
               uint32_t xw[4];
 #pragma unroll
-              for (int j = 0; j < 8; j += 2) {
-                const int c = 64 * g + 8 * k + j;
-                const float hv0 = (__bfloat162float(he[j]) + u2f(a[8 * kk + j]) * s * wp[c]) * lam;
-                const float hv1 = (__bfloat162float(he[j + 1]) + u2f(a[8 * kk + j + 1]) * s * wp[c + 1]) * lam;
-                xw[j / 2] = pack_f16(hv0 * inv_h * wn[c], hv1 * inv_h * wn[c + 1]);
-                hw[4 * k + j / 2] = pack_bf16(hv0, hv1);
+              for (int j = 0; j < 4; ++j) {
+                const uint64_t y = f2(u2f(a[8 * kk + 2 * j]), u2f(a[8 * kk + 2 * j + 1]));
+                const uint64_t h = f2(__uint_as_float(hw4[j] << 16), __uint_as_float(hw4[j] & 0xffff0000u));
+                // hv = (h + y s w) lam = h lam + y (s lam) w;  x = hv (inv_h w_next)
+                const uint64_t hv = f2_fma(f2_mul(y, sl2), pv[j], f2_mul(h, lam2));
+                const uint64_t xv = f2_mul(hv, f2_mul(inv2, nv[j]));
+                float v0, v1;
+                f2_split(xv, v0, v1);
+                xw[j] = pack_f16(v0, v1);
+                f2_split(hv, v0, v1);
+                hw[4 * k + j] = pack_bf16(v0, v1);
               }
               stage_chunk(box, k, make_uint4(xw[0], xw[1], xw[2], xw[3]));
             }
@@ -1096,6 +1121,12 @@ __global__ void __cluster_dims__(6, 1, 1) __launch_bounds__(kGemmThreads, 1)
           flush_rows128(box, xdst + 128 * g, ldb, rows_valid);
           stage_words32(box, hw);
           flush_rows128(box, hdst + 128 * g, ldb, rows_valid);
+          if (mt + ncl < p.m_tiles) {  // this box is free: the next tile's residual rows
+            fence_proxy_async_smem();
+            __syncwarp();
+            prefetch_box(mt + ncl, g);
+            h_pending = true;
+          }
         }
       }
       if (!ok) {
@@ -1109,12 +1140,6 @@ __global__ void __cluster_dims__(6, 1, 1) __launch_bounds__(kGemmThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[ab]);
-      if (mt + ncl < p.m_tiles) {  // the next tile's residual rows, over the staged outputs
-        fence_proxy_async_smem();
-        __syncwarp();
-        prefetch_h(mt + ncl);
-        h_pending = true;
-      }
       ab ^= 1;
       if (ab == 0) aph ^= 1;
     }
@@ -1127,7 +1152,8 @@ __global__ void __cluster_dims__(6, 1, 1) __launch_bounds__(kGemmThreads, 1)
     }
     if (h_pending) {  // no load may still be writing this CTA's shared memory when it leaves
       int never = 0;
-      mbar_wait(&hbar[ew], hph, &never);
+      mbar_wait(&hbar[2 * ew], hph, &never);
+      mbar_wait(&hbar[2 * ew + 1], hph, &never);
     }
   }
 
