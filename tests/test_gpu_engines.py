@@ -64,9 +64,11 @@ def _run(script, args, engine, tmp_path, fused_norm=True, direct=False):
         env.pop("GLP_GEMM", None)
     else:
         env["GLP_GEMM"] = engine
+    # the small batches here would take the row kernels by default: force the choice (None:
+    # the library's own size rule)
     env.pop("GLP_FUSED_NORM", None)
-    if not fused_norm:
-        env["GLP_FUSED_NORM"] = "0"
+    if fused_norm is not None:
+        env["GLP_FUSED_NORM"] = "1" if fused_norm else "0"
     env["PYTHONPATH"] = ROOT + os.pathsep + env.get("PYTHONPATH", "")
     r = subprocess.run([sys.executable, "-c", script, *args], env=env, cwd=ROOT, capture_output=True, text=True,
                        timeout=600)
@@ -130,3 +132,14 @@ def test_fused_post_norm_matches_row_kernels(small_cond_gguf, deep_cond_gguf, tm
         cos = (fa * fd).sum(axis=1) / np.linalg.norm(fa, axis=1) / np.linalg.norm(fd, axis=1)
         assert cos[long_seq].min() >= 0.99999, cos
         assert cos.min() >= 0.999, cos
+
+
+def test_default_keeps_row_kernels_for_one_wave(small_cond_gguf, tmp_path):
+    """By default the fused kernel runs only for launch chunks of more 256-row tiles than
+    resident clusters; this 1,401-token batch is one wave, so the default path equals the
+    row-kernel path bit for bit."""
+    a = str(tmp_path / "auto.npy")
+    b = str(tmp_path / "rows.npy")
+    _run(MODEL_SCRIPT, [small_cond_gguf, a], None, tmp_path, fused_norm=None)
+    _run(MODEL_SCRIPT, [small_cond_gguf, b], None, tmp_path, fused_norm=False)
+    np.testing.assert_array_equal(np.load(a), np.load(b))
