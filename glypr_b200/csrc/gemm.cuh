@@ -701,9 +701,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
 // totals -- takes a second exchange of the directly summed hv^2, which that row then uses
 // (GemmParams::rownorm_direct selects it for every row).
 // The residual rows are fetched by TMA into each epilogue warp's two 4 KB boxes (64 columns
-// each, one mbarrier per box); the output rows are staged through the same boxes, and each box
-// is refilled with the next tile's rows as soon as its outputs are out, so the loads overlap
-// the rest of the epilogue.  Epilogue warp (quad q, half c) owns rows 32q..32q+31 and the 128
+// each, one mbarrier per box); the output rows are staged through the same boxes and leave by
+// bulk tensor stores (x, then h, rows past M clipped), and each box is refilled with the next
+// tile's rows as soon as the stores have read it, so the loads overlap the rest of the epilogue.  Epilogue warp (quad q, half c) owns rows 32q..32q+31 and the 128
 // columns 128c.. of its CTA's 256; the row arithmetic runs on packed f32x2 pairs.
 struct GemmRowCfg {
   static constexpr int STAGES = 4;
@@ -739,7 +739,8 @@ __device__ __forceinline__ void st_async_v4(uint32_t cluster_addr, float4 v, uin
 template <typename T>
 __global__ void __cluster_dims__(6, 1, 1) __launch_bounds__(kGemmThreads, 1)
     gemm_rownorm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                        const __grid_constant__ CUtensorMap tmH, const GemmParams p) {
+                        const __grid_constant__ CUtensorMap tmH, const __grid_constant__ CUtensorMap tmX,
+                        const GemmParams p) {
   using Cfg = GemmRowCfg;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -791,6 +792,7 @@ __global__ void __cluster_dims__(6, 1, 1) __launch_bounds__(kGemmThreads, 1)
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
     tma_prefetch_desc(&tmH);
+    tma_prefetch_desc(&tmX);
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
@@ -914,7 +916,6 @@ __global__ void __cluster_dims__(6, 1, 1) __launch_bounds__(kGemmThreads, 1)
     }
     const float* wp = wsm + half * 128;
     const float* wn = wsm + 256 + half * 128;
-    const size_t ldb = static_cast<size_t>(p.N) * 2;
     const float inv_n = 1.0f / static_cast<float>(p.N);
     const float lam = p.layer_scalar;
     // this warp's 32 rows x 64 columns (box g) of the residual of tile mt
@@ -1077,9 +1078,6 @@ __global__ void __cluster_dims__(6, 1, 1) __launch_bounds__(kGemmThreads, 1)
         // pass C: hv, x = hv * inv_h * w_next (f16) and h = bf16(hv), 64 columns (one box) at a
         // time; each box is read into registers before the outputs are staged over it
         const int wrow0 = mt * 256 + static_cast<int>(prank) * 128 + quad * 32;
-        const int rows_valid = min(32, p.M - wrow0);
-        uint8_t* xdst = reinterpret_cast<uint8_t*>(p.x_next) + (static_cast<size_t>(wrow0) * p.N + col0) * 2;
-        uint8_t* hdst = reinterpret_cast<uint8_t*>(p.h) + (static_cast<size_t>(wrow0) * p.N + col0) * 2;
         const uint64_t sl2 = f2(s * lam, s * lam), lam2 = f2(lam, lam), inv2 = f2(inv_h, inv_h);
 #pragma unroll 1
         for (int g = 0; g < 2; ++g) {
@@ -1118,11 +1116,24 @@ __global__ void __cluster_dims__(6, 1, 1) __launch_bounds__(kGemmThreads, 1)
               stage_chunk(box, k, make_uint4(xw[0], xw[1], xw[2], xw[3]));
             }
           }
-          flush_rows128(box, xdst + 128 * g, ldb, rows_valid);
+          // bulk tensor stores of x, then h, through the box (rows past M are clipped)
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmX, box, col0 + 64 * g, wrow0);
+            bulk_commit();
+            bulk_wait_read_all();
+          }
+          __syncwarp();
           stage_words32(box, hw);
-          flush_rows128(box, hdst + 128 * g, ldb, rows_valid);
-          if (mt + ncl < p.m_tiles) {  // this box is free: the next tile's residual rows
-            fence_proxy_async_smem();
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmH, box, col0 + 64 * g, wrow0);
+            bulk_commit();
+          }
+          if (mt + ncl < p.m_tiles) {  // once the store has read it: the next tile's residual rows
+            if (lane == 0) bulk_wait_read_all();
             __syncwarp();
             prefetch_box(mt + ncl, g);
             h_pending = true;
@@ -1150,6 +1161,7 @@ __global__ void __cluster_dims__(6, 1, 1) __launch_bounds__(kGemmThreads, 1)
       mbar_wait_cluster(&xf0[ab], aph, &never);
       if (direct_armed) mbar_wait_cluster(&xf1[ab * 4 + quad], (xf1ph >> (ab * 4 + quad)) & 1u, &never);
     }
+    if (lane == 0) bulk_wait_all();  // this warp's output stores are complete
     if (h_pending) {  // no load may still be writing this CTA's shared memory when it leaves
       int never = 0;
       mbar_wait(&hbar[2 * ew], hph, &never);

@@ -241,9 +241,9 @@ int rownorm_clusters() {
 
 // y = A * B^T (N == 768) fused with the post-norm + residual + next pre-norm: updates p.h in
 // place and writes p.x_next.  `mb_pair` covers B with 128-row boxes, `mh` the residual rows
-// [M, 768] bf16 with 32-row boxes.
-int launch_rownorm_gemm(const CUtensorMap& ma, const CUtensorMap& mb_pair, const CUtensorMap& mh, GemmParams p,
-                        cudaStream_t st) {
+// [M, 768] bf16 and `mx` the next pre-normed rows [M, 768] f16, both with 32-row boxes.
+int launch_rownorm_gemm(const CUtensorMap& ma, const CUtensorMap& mb_pair, const CUtensorMap& mh, const CUtensorMap& mx,
+                        GemmParams p, cudaStream_t st) {
   if (p.M <= 0) return GLP_OK;
   if (p.N != 768 || p.K % 64 || p.K <= 0) return fail(GLP_ERR_INVALID_ARG, "row-norm GEMM needs N == 768, K % 64 == 0");
   p.m_tiles = (p.M + 255) / 256;
@@ -255,7 +255,7 @@ int launch_rownorm_gemm(const CUtensorMap& ma, const CUtensorMap& mb_pair, const
   }();
   p.rownorm_direct = direct ? 1 : 0;
   const int clusters = std::min(p.m_tiles, rownorm_clusters());
-  glp::gemm_rownorm_kernel<__half><<<6 * clusters, glp::kGemmThreads, glp::GemmRowCfg::SMEM, st>>>(ma, mb_pair, mh, p);
+  glp::gemm_rownorm_kernel<__half><<<6 * clusters, glp::kGemmThreads, glp::GemmRowCfg::SMEM, st>>>(ma, mb_pair, mh, mx, p);
   GLP_CUDA(cudaGetLastError());
   return GLP_OK;
 }
@@ -885,8 +885,9 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
     const int fmode = fused_norm_mode();
     const bool fused = fmode != 0 && H == 768 && use_pair_gemm(glp::kEpiStore16) &&
                        (fmode == 2 || (T + 255) / 256 > rownorm_clusters());
-    CUtensorMap m_h;  // the residual rows, 32-row boxes for the fused epilogue's prefetch
+    CUtensorMap m_h, m_xo;  // residual rows (loads and stores) and next pre-normed rows, 32-row boxes
     if (fused) GLP_TRY(make_map16(&m_h, d.h, T, H, H, 32, false));
+    if (fused) GLP_TRY(make_map16(&m_xo, d.x, T, H, H, 32, true));
     for (int l = 0; l < c.n_layers; ++l) {
       LayerW& L = d.layers[l];
       GemmParams p{};
@@ -929,7 +930,7 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
         po.layer_scalar = 1.0f;
         po.eps = eps;
         GLP_TRY(prof_launch(d, st, kProfGemmO, gemm_flops(Td, H, AW), gemm_bytes(Td, H, AW, 0.0) + fused_bytes,
-                            [&] { return launch_rownorm_gemm(m_attn, L.p_o, m_h, po, st); }));
+                            [&] { return launch_rownorm_gemm(m_attn, L.p_o, m_h, m_xo, po, st); }));
       } else {
         GLP_TRY(prof_launch(d, st, kProfGemmO, gemm_flops(Td, H, AW), gemm_bytes(Td, H, AW, 2.0),
                             [&] { return launch_gemm<__half>(m_attn, L.m_o, bn_for(H), glp::kEpiStore16, po, st, &L.p_o); }));
@@ -968,7 +969,7 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
         pd.layer_scalar = L.layer_scalar;
         pd.eps = eps;
         GLP_TRY(prof_launch(d, st, kProfGemmDown, gemm_flops(Td, H, F), gemm_bytes(Td, H, F, 0.0) + fused_bytes,
-                            [&] { return launch_rownorm_gemm(m_a, L.p_down, m_h, pd, st); }));
+                            [&] { return launch_rownorm_gemm(m_a, L.p_down, m_h, m_xo, pd, st); }));
         continue;
       }
       GLP_TRY(prof_launch(d, st, kProfGemmDown, gemm_flops(Td, H, F), gemm_bytes(Td, H, F, 2.0),
