@@ -126,7 +126,8 @@ __device__ __forceinline__ void epi_qkv_chunk8(int f0, float inv, const float* g
 template <int BN, int EPI, typename T>
 __device__ __forceinline__ bool gemm_epilogue_tile(const GemmParams& p, uint32_t tacc, int m_blk, int n_blk,
                                                    int row_in_tile, int half, float* red, uint64_t* xbar,
-                                                   uint32_t& xph, volatile int* abort_flag, uint8_t* stage) {
+                                                   uint32_t& xph, volatile int* abort_flag, uint8_t* stage,
+                                                   const CUtensorMap* tmc = nullptr) {
   const int row = m_blk * 128 + row_in_tile;
   const int wrow0 = row - (threadIdx.x & 31);  // first row of this warp's 32
   const int rows_valid = min(32, p.M - wrow0);
@@ -203,6 +204,10 @@ __device__ __forceinline__ bool gemm_epilogue_tile(const GemmParams& p, uint32_t
       }
     };
     if (rope) load_tab(0, cva, sva);  // in flight during pass 1
+    if (tmc) {  // the previous tile's bulk stores have read the staging tile
+      if ((threadIdx.x & 31) == 0) bulk_wait_read_all();
+      __syncwarp();
+    }
     // pass 1: this warp's half of the head's sum of squares (cpu_simd/rmsnorm.rs:13-21)
     float ss = 0.f;
     {
@@ -259,16 +264,39 @@ __device__ __forceinline__ bool gemm_epilogue_tile(const GemmParams& p, uint32_t
       if (k + 2 < 8) issue(k + 2, loA, hiA);
       finish(k + 1, loB, hiB, cvb, svb);
     }
-    const size_t ld_bytes = static_cast<size_t>(p.ldc) * 2;
-    uint8_t* dst0 = reinterpret_cast<uint8_t*>(p.C) +
-                    (static_cast<size_t>(wrow0) * p.ldc + static_cast<size_t>(n_blk) * 256 + f0) * 2;
-    flush_rows128(stage, dst0, ld_bytes, rows_valid);
-    uint32_t w[32];
-    tmem_st_wait();
-    tmem_ld32(park, w);
-    tmem_ld_wait_tied(w);
-    stage_words32(stage, w);
-    flush_rows128(stage, dst0 + 256, ld_bytes, rows_valid);
+    if (tmc) {  // bulk tensor stores (rows past M clipped); the staging tile is 1024-byte aligned
+      const int col = n_blk * 256 + f0;
+      fence_proxy_async_smem();
+      __syncwarp();
+      if ((threadIdx.x & 31) == 0) {
+        tma_store_2d(tmc, stage, col, wrow0);
+        bulk_commit();
+      }
+      uint32_t w[32];
+      tmem_st_wait();
+      tmem_ld32(park, w);
+      tmem_ld_wait_tied(w);
+      if ((threadIdx.x & 31) == 0) bulk_wait_read_all();
+      __syncwarp();
+      stage_words32(stage, w);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if ((threadIdx.x & 31) == 0) {
+        tma_store_2d(tmc, stage, col + 128, wrow0);
+        bulk_commit();
+      }
+    } else {
+      const size_t ld_bytes = static_cast<size_t>(p.ldc) * 2;
+      uint8_t* dst0 = reinterpret_cast<uint8_t*>(p.C) +
+                      (static_cast<size_t>(wrow0) * p.ldc + static_cast<size_t>(n_blk) * 256 + f0) * 2;
+      flush_rows128(stage, dst0, ld_bytes, rows_valid);
+      uint32_t w[32];
+      tmem_st_wait();
+      tmem_ld32(park, w);
+      tmem_ld_wait_tied(w);
+      stage_words32(stage, w);
+      flush_rows128(stage, dst0 + 256, ld_bytes, rows_valid);
+    }
   }
   return true;
 }
@@ -470,16 +498,19 @@ struct GemmPairCfg {
   static constexpr uint32_t TMEM_COLS = 2 * BN;
   static constexpr uint32_t RED_OFFSET = 512;
   static constexpr uint32_t RED_BYTES = 2 * 2 * 128 * 4;
-  static constexpr uint32_t STAGE_OFFSET = STAGES * (A_BYTES + B_BYTES) + RED_OFFSET + RED_BYTES;
+  // 1024-byte aligned: the QKV epilogue's staging tiles are the sources of 128B-swizzled bulk stores
+  static constexpr uint32_t STAGE_OFFSET = (STAGES * (A_BYTES + B_BYTES) + RED_OFFSET + RED_BYTES + 1023) / 1024 * 1024;
   static constexpr uint32_t STAGE_BYTES = 8 * 32 * 128;
   static constexpr size_t SMEM = STAGE_OFFSET + STAGE_BYTES;
+  static_assert(SMEM <= 232448, "shared memory per CTA");
 };
 
-// p.m_tiles counts 256-row pair tiles here.
+// p.m_tiles counts 256-row pair tiles here.  tmC: the output as 32-row x 64-column boxes, for the
+// QKV epilogue's bulk stores (unused by the other epilogues).
 template <int EPI, typename T>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     const GemmParams p) {
+                     const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
   using Cfg = GemmPairCfg;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -657,7 +688,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
           tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(ab * Cfg::BN);
       // this CTA's 128 rows are 128-row block 2 m_blk + rank
       if (!gemm_epilogue_tile<256, EPI, T>(p, tacc, 2 * m_blk + static_cast<int>(rank), n_blk, row_in_tile, half,
-                                           red + ab * 256, &xbar[quad], xph, abort_flag, stage)) {
+                                           red + ab * 256, &xbar[quad], xph, abort_flag, stage,
+                                           EPI == kEpiQkv ? &tmC : nullptr)) {
         if (lane == 0) {
           record_error(p.status, kErrTimeoutEpilogue);
           *abort_flag = 1;
@@ -670,6 +702,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       ab ^= 1;
       if (ab == 0) aph ^= 1;
     }
+    if (EPI == kEpiQkv && lane == 0) bulk_wait_all();  // this warp's bulk stores are complete
   }
 
   // neither CTA leaves (or frees tensor memory) while the other may still touch its shared

@@ -265,7 +265,7 @@ int launch_rownorm_gemm(const CUtensorMap& ma, const CUtensorMap& mb_pair, const
 // box rows 128) lets 256-wide tiles run on CTA pairs.
 template <typename T>
 int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, int bn, int epi, GemmParams p, cudaStream_t st,
-                const CUtensorMap* mb_pair = nullptr) {
+                const CUtensorMap* mb_pair = nullptr, const CUtensorMap* mc = nullptr) {
   p.m_tiles = (p.M + 127) / 128;
   p.n_tiles = p.N / bn;
   p.k_blocks = p.K / 64;
@@ -280,10 +280,13 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, int bn, int epi, G
     const size_t smem = glp::GemmPairCfg::SMEM;
     const dim3 grid(static_cast<unsigned>(2 * pairs));
     switch (epi) {
-      case glp::kEpiStore16: glp::gemm_pair_kernel<glp::kEpiStore16, T><<<grid, glp::kGemmThreads, smem, st>>>(ma, *mb_pair, p); break;
-      case glp::kEpiF32: glp::gemm_pair_kernel<glp::kEpiF32, T><<<grid, glp::kGemmThreads, smem, st>>>(ma, *mb_pair, p); break;
-      case glp::kEpiQkv: glp::gemm_pair_kernel<glp::kEpiQkv, __half><<<grid, glp::kGemmThreads, smem, st>>>(ma, *mb_pair, p); break;
-      case glp::kEpiGeglu: glp::gemm_pair_kernel<glp::kEpiGeglu, __half><<<grid, glp::kGemmThreads, smem, st>>>(ma, *mb_pair, p); break;
+      case glp::kEpiStore16: glp::gemm_pair_kernel<glp::kEpiStore16, T><<<grid, glp::kGemmThreads, smem, st>>>(ma, *mb_pair, ma, p); break;
+      case glp::kEpiF32: glp::gemm_pair_kernel<glp::kEpiF32, T><<<grid, glp::kGemmThreads, smem, st>>>(ma, *mb_pair, ma, p); break;
+      case glp::kEpiQkv:
+        if (!mc) return fail(GLP_ERR_INVALID_ARG, "the QKV epilogue needs the output's tensor map");
+        glp::gemm_pair_kernel<glp::kEpiQkv, __half><<<grid, glp::kGemmThreads, smem, st>>>(ma, *mb_pair, *mc, p);
+        break;
+      case glp::kEpiGeglu: glp::gemm_pair_kernel<glp::kEpiGeglu, __half><<<grid, glp::kGemmThreads, smem, st>>>(ma, *mb_pair, ma, p); break;
       default: return fail(GLP_ERR_INVALID_ARG, "bad epilogue");
     }
     GLP_CUDA(cudaGetLastError());
@@ -865,8 +868,9 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
       return GLP_OK;
     }));
 
-    CUtensorMap m_x, m_attn, m_a;
+    CUtensorMap m_x, m_attn, m_a, m_qkv_out;
     GLP_TRY(make_map16(&m_x, d.x, T, H, H, 128, true));
+    GLP_TRY(make_map16(&m_qkv_out, d.qkv, T, QKV, QKV, 32, true));  // the QKV epilogue's bulk stores
     GLP_TRY(make_map16(&m_attn, d.attn, T, AW, AW, 128, true));
     GLP_TRY(make_map16(&m_a, d.a, T, F, F, 128, true));
     double pairs_local = 0, pairs_global = 0;
@@ -907,7 +911,7 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
       p.n_kv_heads = c.n_kv;
       p.eps = eps;
       GLP_TRY(prof_launch(d, st, kProfGemmQkv, gemm_flops(Td, QKV, H), gemm_bytes(Td, QKV, H, 2.0),
-                          [&] { return launch_gemm<__half>(m_x, L.m_qkv, 256, glp::kEpiQkv, p, st, &L.p_qkv); }));
+                          [&] { return launch_gemm<__half>(m_x, L.m_qkv, 256, glp::kEpiQkv, p, st, &L.p_qkv, &m_qkv_out); }));
       // attention
       const double pairs = L.sliding ? pairs_local : pairs_global;
       GLP_TRY(prof_launch(d, st, kProfAttention, 4.0 * D * c.n_heads * pairs, attn_bytes, [&] {
