@@ -186,22 +186,38 @@ int sm_count() {
 
 int bn_for(int n) { return n % 256 == 0 ? 256 : 128; }
 
-// GEMM engine for 256-wide tiles: CTA pairs (default) or one CTA per tile (GLP_GEMM=single).
+// GEMM engine for 256-wide tiles: CTA pairs or one CTA per tile.
 // Per kernel the pair is faster for the plain-store GEMMs (O 0.312 -> 0.269 ms, down 0.414 ->
 // 0.372 ms per 262,144-token launch) and 3-6 % slower in cycles for the fused QKV and GeGLU
 // epilogues; but under the 1 kW power cap the pairs' smaller L2 and shared-memory traffic lets
 // the whole forward run at a higher clock (median 1,447-1,470 vs 1,402-1,410 MHz), and
 // all-pairs gave the higher throughput: 6,141-6,191 vs 6,088-6,127 embeddings/s with pairs for
-// the plain-store GEMMs only.  GLP_GEMM=pair-store keeps that mix.
-bool use_pair_gemm(int epi) {
+// the plain-store GEMMs only.  A GEMM of fewer 256-row tiles than one wave of pairs (a short
+// launch chunk) runs on single CTAs instead: twice the tiles of half the size finish sooner
+// (one 512-token sequence: 1.70 -> 1.62 ms).  GLP_GEMM=pair forces pairs for every 256-wide
+// GEMM, GLP_GEMM=single single CTAs, GLP_GEMM=pair-store pairs for the plain-store epilogues only.
+int gemm_engine_mode() {  // 0 single, 1 pair-store, 2 pairs for a full wave (default), 3 pairs
   static const int mode = [] {
     const char* e = std::getenv("GLP_GEMM");
     if (e && std::string(e) == "single") return 0;
     if (e && std::string(e) == "pair-store") return 1;
+    if (e && std::string(e) == "pair") return 3;
     return 2;
   }();
-  if (mode != 1) return mode == 2;
+  return mode;
+}
+
+bool use_pair_gemm(int epi) {
+  const int mode = gemm_engine_mode();
+  if (mode != 1) return mode >= 2;
   return epi == glp::kEpiStore16 || epi == glp::kEpiF32;
+}
+
+// pairs for this GEMM: the engine allows them and (by default) its 256-row tiles fill a wave
+bool pair_gemm_for(int epi, int M, int n_tiles) {
+  if (!use_pair_gemm(epi)) return false;
+  if (gemm_engine_mode() != 2) return true;
+  return static_cast<int64_t>((M + 255) / 256) * n_tiles >= sm_count() / 2;
 }
 
 // Post-norms fused into the O / down GEMMs (gemm_rownorm_kernel) for 768-wide rows: by default
@@ -272,7 +288,7 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, int bn, int epi, G
   if (p.M <= 0) return GLP_OK;
   if (p.K % 64 || p.N % bn || p.K <= 0) return fail(GLP_ERR_INVALID_ARG, "GEMM needs K % 64 == 0 and N % tile == 0");
   const bool f16 = std::is_same<T, __half>::value;
-  if (bn == 256 && mb_pair && use_pair_gemm(epi)) {
+  if (bn == 256 && mb_pair && pair_gemm_for(epi, p.M, p.n_tiles)) {
     if ((epi == glp::kEpiQkv || epi == glp::kEpiGeglu) && !f16)
       return fail(GLP_ERR_INVALID_ARG, "fused epilogues run on f16 operands");
     p.m_tiles = (p.M + 255) / 256;  // 256-row pair tiles

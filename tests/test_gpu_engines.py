@@ -1,8 +1,8 @@
 """Both GEMM engines produce the same results.
 
-The library runs 256-wide GEMM tiles on CTA pairs (tcgen05.mma.cta_group::2, the default) or on
-one CTA per tile; GLP_GEMM=single forces the latter everywhere and GLP_GEMM=pair-store uses
-pairs for the plain-store epilogues only.  The engine is chosen once per process, so each
+The library runs 256-wide GEMM tiles on CTA pairs (tcgen05.mma.cta_group::2; by default for
+GEMMs that fill a wave of pairs) or on one CTA per tile; GLP_GEMM=pair / single forces either
+everywhere and GLP_GEMM=pair-store uses pairs for the plain-store epilogues only.  The engine is chosen once per process, so each
 engine runs in a child process here, and the tests compare:
 
 * the kernel-level GEMM (f32 and bf16 outputs, M tails) against the f32 product;
@@ -93,12 +93,13 @@ def test_gemm_engine_matches_f32_product(engine, tmp_path):
 
 def test_model_forward_identical_across_engines(small_cond_gguf, tmp_path):
     # with the post-norms as separate row kernels every engine rounds identically
+    # (None: pairs only for GEMMs that fill a wave of them -- single CTAs for this small batch)
     outs = {}
-    for engine in (None, "pair-store", "single"):
+    for engine in (None, "pair", "pair-store", "single"):
         out = str(tmp_path / f"emb_{engine}.npy")
         _run(MODEL_SCRIPT, [small_cond_gguf, out], engine, tmp_path, fused_norm=False)
         outs[engine] = np.load(out)
-    for engine in ("pair-store", "single"):
+    for engine in ("pair", "pair-store", "single"):
         np.testing.assert_array_equal(outs[engine], outs[None])
 
 
