@@ -220,15 +220,15 @@ bool pair_gemm_for(int epi, int M, int n_tiles) {
   return static_cast<int64_t>((M + 255) / 256) * n_tiles >= sm_count() / 2;
 }
 
-// Post-norms fused into the O / down GEMMs (gemm_rownorm_kernel) for 768-wide rows: by default
-// for launch chunks of more 256-row tiles than resident clusters; GLP_FUSED_NORM=1 for every
-// chunk, GLP_FUSED_NORM=0 never (separate row kernels).
-int fused_norm_mode() {  // 0 never, 1 by size, 2 always
+// Post-norms fused into the O / down GEMMs (gemm_rownorm_kernel) for 768-wide rows, for every
+// launch chunk (GLP_FUSED_NORM=0: separate row kernels).  Not chosen by chunk size, although a
+// single-wave chunk runs the row kernels faster (one 512-token sequence 1.70 vs 1.81 ms): the two
+// paths round differently, and a sequence's embedding stays bit-identical whatever batch it
+// is embedded in only if every chunk takes the same path.
+int fused_norm_mode() {  // 0 never, 2 always
   static const int mode = [] {
     const char* e = std::getenv("GLP_FUSED_NORM");
-    if (e && std::string(e) == "0") return 0;
-    if (e && std::string(e) == "1") return 2;
-    return 1;
+    return (e && std::string(e) == "0") ? 0 : 2;
   }();
   return mode;
 }
@@ -898,13 +898,8 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
     const double attn_bytes = 2.0 * Td * QKV + 2.0 * Td * AW;
     const double post_bytes = Td * (2.0 * H + 4.0 * H + 2.0 * H);  // y + h in/out + x (16-bit)
     const double fused_bytes = Td * (4.0 * H + 2.0 * H);              // h in/out + x, no y
-    // the row-norm GEMM needs 768-wide rows and the CTA-pair weight maps; it pays once its tiles
-    // pipeline (more 256-row tiles than resident clusters): for a single wave its epilogue runs
-    // after the mainloop instead of under the next tile's, and one 512-token sequence measured
-    // 1.72 ms unfused against 1.81 ms fused
-    const int fmode = fused_norm_mode();
-    const bool fused = fmode != 0 && H == 768 && use_pair_gemm(glp::kEpiStore16) &&
-                       (fmode == 2 || (T + 255) / 256 > rownorm_clusters());
+    // the row-norm GEMM needs 768-wide rows and the CTA-pair weight maps
+    const bool fused = fused_norm_mode() != 0 && H == 768 && use_pair_gemm(glp::kEpiStore16);
     CUtensorMap m_h, m_xo;  // residual rows (loads and stores) and next pre-normed rows, 32-row boxes
     if (fused) GLP_TRY(make_map16(&m_h, d.h, T, H, H, 32, false));
     if (fused) GLP_TRY(make_map16(&m_xo, d.x, T, H, H, 32, true));

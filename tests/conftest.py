@@ -12,12 +12,6 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
-# The library fuses the post-norms into the O / down GEMMs only for launch chunks of more than
-# one wave of tiles, which the small test batches never reach: run the fused kernel for every
-# chunk in the test processes so the model gates cover it (tests of the row-kernel path set
-# GLP_FUSED_NORM=0 in their child processes).
-os.environ.setdefault("GLP_FUSED_NORM", "1")
-
 from glypr_b200 import synth  # noqa: E402
 
 

@@ -64,8 +64,7 @@ def _run(script, args, engine, tmp_path, fused_norm=True, direct=False):
         env.pop("GLP_GEMM", None)
     else:
         env["GLP_GEMM"] = engine
-    # the small batches here would take the row kernels by default: force the choice (None:
-    # the library's own size rule)
+    # force the post-norm path (None: the library's default)
     env.pop("GLP_FUSED_NORM", None)
     if fused_norm is not None:
         env["GLP_FUSED_NORM"] = "1" if fused_norm else "0"
@@ -135,12 +134,11 @@ def test_fused_post_norm_matches_row_kernels(small_cond_gguf, deep_cond_gguf, tm
         assert cos.min() >= 0.999, cos
 
 
-def test_default_keeps_row_kernels_for_one_wave(small_cond_gguf, tmp_path):
-    """By default the fused kernel runs only for launch chunks of more 256-row tiles than
-    resident clusters; this 1,401-token batch is one wave, so the default path equals the
-    row-kernel path bit for bit."""
-    a = str(tmp_path / "auto.npy")
-    b = str(tmp_path / "rows.npy")
+def test_default_fuses_every_chunk(small_cond_gguf, tmp_path):
+    """The fused post-norm runs for every launch chunk by default (so a sequence embeds
+    identically in any batch): the default equals the forced fused path bit for bit."""
+    a = str(tmp_path / "default.npy")
+    b = str(tmp_path / "fused.npy")
     _run(MODEL_SCRIPT, [small_cond_gguf, a], None, tmp_path, fused_norm=None)
-    _run(MODEL_SCRIPT, [small_cond_gguf, b], None, tmp_path, fused_norm=False)
+    _run(MODEL_SCRIPT, [small_cond_gguf, b], None, tmp_path, fused_norm=True)
     np.testing.assert_array_equal(np.load(a), np.load(b))
