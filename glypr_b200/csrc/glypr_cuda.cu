@@ -21,6 +21,7 @@
 #include <mutex>
 #include <string>
 #include <thread>
+#include <type_traits>
 #include <vector>
 
 #include "attention.cuh"
@@ -185,6 +186,24 @@ int sm_count() {
 }
 
 int bn_for(int n) { return n % 256 == 0 ? 256 : 128; }
+
+// The row kernels are compiled per hidden size: f(std::integral_constant<int, H>{}) for H a
+// multiple of 256 up to glp::kMaxHidden.
+template <class F>
+int with_hidden(int H, F&& f) {
+  switch (H) {
+    case 256: return f(std::integral_constant<int, 256>{});
+    case 512: return f(std::integral_constant<int, 512>{});
+    case 768: return f(std::integral_constant<int, 768>{});
+    case 1024: return f(std::integral_constant<int, 1024>{});
+    case 1280: return f(std::integral_constant<int, 1280>{});
+    case 1536: return f(std::integral_constant<int, 1536>{});
+    case 1792: return f(std::integral_constant<int, 1792>{});
+    case 2048: return f(std::integral_constant<int, 2048>{});
+    default: return fail(GLP_ERR_UNSUPPORTED, "hidden size must be a multiple of 256 up to 2048");
+  }
+}
+static_assert(glp::kMaxHidden == 2048, "with_hidden covers every supported hidden size");
 
 // GEMM engine for 256-wide tiles: CTA pairs or one CTA per tile.
 // Per kernel the pair is faster for the plain-store GEMMs (O 0.312 -> 0.269 ms, down 0.414 ->
@@ -391,7 +410,8 @@ int parse_config(const glp::GgufFile& g, Config* c) {
                   "per-layer head_dim / kv-head overrides are not supported (all layers must share head_dim and kv heads)");
   }
   c->head_dim = static_cast<int>(hd_swa);
-  if (c->hidden != glp::kHidden) return fail(GLP_ERR_UNSUPPORTED, "hidden size must be 768");
+  if (c->hidden <= 0 || c->hidden % 256 || c->hidden > glp::kMaxHidden)
+    return fail(GLP_ERR_UNSUPPORTED, "hidden size must be a multiple of 256 up to 2048");
   if (c->head_dim != 256) return fail(GLP_ERR_UNSUPPORTED, "head_dim must be 256");
   if (c->n_kv <= 0 || c->n_heads % c->n_kv) return fail(GLP_ERR_FORMAT, "head_count must be a multiple of head_count_kv");
   if (c->ffn % 128) return fail(GLP_ERR_UNSUPPORTED, "feed_forward_length must be a multiple of 128");
@@ -841,7 +861,7 @@ int setup_device(Device& d, const Config& c, const glp::GgufFile& g, int64_t cap
   GLP_TRY(d.alloc(&d.y, static_cast<size_t>(cap_tokens) * H));
   GLP_TRY(d.alloc(&d.a, static_cast<size_t>(cap_tokens) * F));
   GLP_TRY(d.alloc(&d.pos, static_cast<size_t>(cap_tokens)));
-  GLP_TRY(d.alloc(&d.pooled, static_cast<size_t>(cap_seqs) * H));
+  GLP_TRY(d.alloc(&d.pooled, static_cast<size_t>(cap_seqs) * max_head));  // also a head stage's output
   GLP_TRY(d.alloc(&d.pool_part, (static_cast<size_t>(cap_tokens) / glp::kPoolSeg + cap_seqs + 1) * H));
   GLP_TRY(d.alloc(&d.mid, static_cast<size_t>(cap_seqs) * max_head));
   GLP_TRY(d.alloc(&d.emb, static_cast<size_t>(cap_seqs) * max_head));
@@ -873,15 +893,19 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
     const float scale = static_cast<float>(std::sqrt(static_cast<double>(H)));
     const double row_in = d.table_type == glp::kGgmlQ8_0 ? H / 32 * 34.0 : 2.0 * H;
     GLP_TRY(prof_launch(d, st, kProfEmbed, 0.0, Td * (4.0 + row_in + 4.0 * H), [&] {
-      if (d.table_type == glp::kGgmlQ8_0)
-        glp::embed_gather_norm_kernel<<<rows_grid, 256, 0, st>>>(static_cast<const uint8_t*>(d.table), d_ids_chunk,
-                                                                 T, scale, d.layers[0].attn_norm, eps, d.h, d.x);
-      else
-        glp::embed_gather_norm_bf16_kernel<<<rows_grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(d.table),
-                                                                      d_ids_chunk, T, scale, d.layers[0].attn_norm,
-                                                                      eps, d.h, d.x);
-      GLP_CUDA(cudaGetLastError());
-      return GLP_OK;
+      return with_hidden(H, [&](auto hc) {
+        constexpr int kH = decltype(hc)::value;
+        if (d.table_type == glp::kGgmlQ8_0)
+          glp::embed_gather_norm_kernel<kH><<<rows_grid, 256, 0, st>>>(static_cast<const uint8_t*>(d.table),
+                                                                       d_ids_chunk, T, scale, d.layers[0].attn_norm,
+                                                                       eps, d.h, d.x);
+        else
+          glp::embed_gather_norm_bf16_kernel<kH><<<rows_grid, 256, 0, st>>>(
+              static_cast<const __nv_bfloat16*>(d.table), d_ids_chunk, T, scale, d.layers[0].attn_norm, eps, d.h,
+              d.x);
+        GLP_CUDA(cudaGetLastError());
+        return GLP_OK;
+      });
     }));
 
     CUtensorMap m_x, m_attn, m_a, m_qkv_out;
@@ -898,7 +922,8 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
     const double attn_bytes = 2.0 * Td * QKV + 2.0 * Td * AW;
     const double post_bytes = Td * (2.0 * H + 4.0 * H + 2.0 * H);  // y + h in/out + x (16-bit)
     const double fused_bytes = Td * (4.0 * H + 2.0 * H);              // h in/out + x, no y
-    // the row-norm GEMM needs 768-wide rows and the CTA-pair weight maps
+    // the row-norm GEMM needs 768-wide rows (three CTA pairs per cluster) and the CTA-pair weight
+    // maps; other widths run the GEMM then post_norm_residual_kernel
     const bool fused = fused_norm_mode() != 0 && H == 768 && use_pair_gemm(glp::kEpiStore16);
     CUtensorMap m_h, m_xo;  // residual rows (loads and stores) and next pre-normed rows, 32-row boxes
     if (fused) GLP_TRY(make_map16(&m_h, d.h, T, H, H, 32, false));
@@ -950,10 +975,12 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
         GLP_TRY(prof_launch(d, st, kProfGemmO, gemm_flops(Td, H, AW), gemm_bytes(Td, H, AW, 2.0),
                             [&] { return launch_gemm<__half>(m_attn, L.m_o, bn_for(H), glp::kEpiStore16, po, st, &L.p_o); }));
         GLP_TRY(prof_launch(d, st, kProfPostNorm, 0.0, post_bytes, [&] {
-          glp::post_norm_residual_kernel<false><<<rows_grid, 256, 0, st>>>(d.y, d.h, L.post_attn, 1.0f, L.ffn_norm,
-                                                                           eps, T, d.x, nullptr);
-          GLP_CUDA(cudaGetLastError());
-          return GLP_OK;
+          return with_hidden(H, [&](auto hc) {
+            glp::post_norm_residual_kernel<decltype(hc)::value, false>
+                <<<rows_grid, 256, 0, st>>>(d.y, d.h, L.post_attn, 1.0f, L.ffn_norm, eps, T, d.x, nullptr);
+            GLP_CUDA(cudaGetLastError());
+            return GLP_OK;
+          });
         }));
       }
       // gate|up + GeGLU
@@ -990,24 +1017,29 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
       GLP_TRY(prof_launch(d, st, kProfGemmDown, gemm_flops(Td, H, F), gemm_bytes(Td, H, F, 2.0),
                           [&] { return launch_gemm<__half>(m_a, L.m_down, bn_for(H), glp::kEpiStore16, pd, st, &L.p_down); }));
       GLP_TRY(prof_launch(d, st, kProfPostNorm, 0.0, last ? Td * 8.0 * H : post_bytes, [&] {
-        if (!last)
-          glp::post_norm_residual_kernel<false><<<rows_grid, 256, 0, st>>>(
-              d.y, d.h, L.post_ffw, L.layer_scalar, d.layers[l + 1].attn_norm, eps, T, d.x, nullptr);
-        else
-          glp::post_norm_residual_kernel<true><<<rows_grid, 256, 0, st>>>(d.y, d.h, L.post_ffw, L.layer_scalar,
-                                                                          d.out_norm, eps, T, nullptr, d.xf);
-        GLP_CUDA(cudaGetLastError());
-        return GLP_OK;
+        return with_hidden(H, [&](auto hc) {
+          constexpr int kH = decltype(hc)::value;
+          if (!last)
+            glp::post_norm_residual_kernel<kH, false><<<rows_grid, 256, 0, st>>>(
+                d.y, d.h, L.post_ffw, L.layer_scalar, d.layers[l + 1].attn_norm, eps, T, d.x, nullptr);
+          else
+            glp::post_norm_residual_kernel<kH, true><<<rows_grid, 256, 0, st>>>(
+                d.y, d.h, L.post_ffw, L.layer_scalar, d.out_norm, eps, T, nullptr, d.xf);
+          GLP_CUDA(cudaGetLastError());
+          return GLP_OK;
+        });
       }));
     }
   }
   // masked mean of the final-normed rows, then the dense head on the pooled vectors
   GLP_TRY(prof_launch(d, st, kProfPool, 0.0, 4.0 * Td * H + 2.0 * n_seq * H, [&] {
     const int segs = std::max(1, (max_len + glp::kPoolSeg - 1) / glp::kPoolSeg);
-    glp::mean_pool_kernel<<<dim3(static_cast<unsigned>(n_seq), static_cast<unsigned>(segs)), 192, 0, st>>>(
-        d.xf, d_cu_chunk, base, n_seq, d.pooled, nullptr, d.pool_part);
+    const unsigned pool_threads = static_cast<unsigned>(H / 4);
+    glp::mean_pool_kernel<<<dim3(static_cast<unsigned>(n_seq), static_cast<unsigned>(segs)), pool_threads, 0, st>>>(
+        d.xf, d_cu_chunk, base, n_seq, H, d.pooled, nullptr, d.pool_part);
     if (segs > 1)
-      glp::mean_pool_finish_kernel<<<n_seq, 192, 0, st>>>(d_cu_chunk, base, n_seq, d.pool_part, d.pooled, nullptr);
+      glp::mean_pool_finish_kernel<<<n_seq, pool_threads, 0, st>>>(d_cu_chunk, base, n_seq, H, d.pool_part, d.pooled,
+                                                                    nullptr);
     GLP_CUDA(cudaGetLastError());
     return GLP_OK;
   }));

@@ -10,8 +10,9 @@
 
 namespace glp {
 
-constexpr int kHidden = 768;           // row kernels are specialised for hidden 768
-constexpr int kVecPerLane = kHidden / 256;  // 8-element chunks per lane (3)
+// The row kernels are compiled per hidden size H: a multiple of 256 up to kMaxHidden (the
+// BASELINE model has H = 768).
+constexpr int kMaxHidden = 2048;
 
 // ---------------------------------------------------------------------------- Q8_0
 // Exact dequantisation f32(d) * q (the product of an int8 and an fp16 value is exact in
@@ -97,17 +98,18 @@ __device__ __forceinline__ void store16x8(T* p, const float* v) {
 // x[t] = f16(RMSNorm(h[t]) * w)             (first layer's attn_norm, norm.rs:22-63)
 // One warp per token; lane l covers elements l, l+32, ... (coalesced byte reads of the
 // 34-byte blocks).
+template <int H>
 __global__ void embed_gather_norm_kernel(const uint8_t* __restrict__ table, const int* __restrict__ ids,
                                          int n_tokens, float scale, const float* __restrict__ w, float eps,
                                          __nv_bfloat16* __restrict__ h, __half* __restrict__ x) {
   const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (t >= n_tokens) return;
-  const uint8_t* row = table + static_cast<size_t>(ids[t]) * (kHidden / 32) * 34;
-  float v[kHidden / 32];
+  const uint8_t* row = table + static_cast<size_t>(ids[t]) * (H / 32) * 34;
+  float v[H / 32];
   float ss = 0.f;
 #pragma unroll
-  for (int b = 0; b < kHidden / 32; ++b) {
+  for (int b = 0; b < H / 32; ++b) {
     const uint8_t* blk = row + b * 34;
     const float d = __half2float(__ushort_as_half(static_cast<unsigned short>(blk[0] | (blk[1] << 8))));
     const float q = static_cast<float>(static_cast<int8_t>(blk[2 + lane]));
@@ -115,11 +117,11 @@ __global__ void embed_gather_norm_kernel(const uint8_t* __restrict__ table, cons
     ss = fmaf(v[b], v[b], ss);
   }
   ss = warp_sum(ss);
-  const float inv = 1.0f / sqrtf(ss / static_cast<float>(kHidden) + eps);
-  __nv_bfloat16* hr = h + static_cast<size_t>(t) * kHidden;
-  __half* xr = x + static_cast<size_t>(t) * kHidden;
+  const float inv = 1.0f / sqrtf(ss / static_cast<float>(H) + eps);
+  __nv_bfloat16* hr = h + static_cast<size_t>(t) * H;
+  __half* xr = x + static_cast<size_t>(t) * H;
 #pragma unroll
-  for (int b = 0; b < kHidden / 32; ++b) {
+  for (int b = 0; b < H / 32; ++b) {
     const int e = b * 32 + lane;
     hr[e] = __float2bfloat16_rn(v[b]);
     xr[e] = __float2half_rn(v[b] * inv * __ldg(w + e));
@@ -127,26 +129,27 @@ __global__ void embed_gather_norm_kernel(const uint8_t* __restrict__ table, cons
 }
 
 // Same gather for a bf16 token table (BF16 GGUF).
+template <int H>
 __global__ void embed_gather_norm_bf16_kernel(const __nv_bfloat16* __restrict__ table, const int* __restrict__ ids,
                                               int n_tokens, float scale, const float* __restrict__ w, float eps,
                                               __nv_bfloat16* __restrict__ h, __half* __restrict__ x) {
   const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (t >= n_tokens) return;
-  const __nv_bfloat16* row = table + static_cast<size_t>(ids[t]) * kHidden;
-  float v[kHidden / 32];
+  const __nv_bfloat16* row = table + static_cast<size_t>(ids[t]) * H;
+  float v[H / 32];
   float ss = 0.f;
 #pragma unroll
-  for (int b = 0; b < kHidden / 32; ++b) {
+  for (int b = 0; b < H / 32; ++b) {
     v[b] = __bfloat162float(row[b * 32 + lane]) * scale;
     ss = fmaf(v[b], v[b], ss);
   }
   ss = warp_sum(ss);
-  const float inv = 1.0f / sqrtf(ss / static_cast<float>(kHidden) + eps);
-  __nv_bfloat16* hr = h + static_cast<size_t>(t) * kHidden;
-  __half* xr = x + static_cast<size_t>(t) * kHidden;
+  const float inv = 1.0f / sqrtf(ss / static_cast<float>(H) + eps);
+  __nv_bfloat16* hr = h + static_cast<size_t>(t) * H;
+  __half* xr = x + static_cast<size_t>(t) * H;
 #pragma unroll
-  for (int b = 0; b < kHidden / 32; ++b) {
+  for (int b = 0; b < H / 32; ++b) {
     const int e = b * 32 + lane;
     hr[e] = __float2bfloat16_rn(v[b]);
     xr[e] = __float2half_rn(v[b] * inv * __ldg(w + e));
@@ -158,28 +161,30 @@ __global__ void embed_gather_norm_bf16_kernel(const __nv_bfloat16* __restrict__ 
 // then the next pre-norm:  x = RMSNorm(h) * w_next
 //   FINAL = false: h is updated (bf16) and x is f16 (the next GEMM's input)
 //   FINAL = true : the normalised row is written to xf in f32 (output_norm, model.rs:576)
-// All arithmetic in f32.  One warp per row; lane owns elements [c*256 + lane*8, +8).  Capped
-// at 64 registers (4 blocks of 8 rows per SM) for more rows in flight: 5.26 -> 5.56 TB/s.
-template <bool FINAL>
-__global__ void __launch_bounds__(256, 4) post_norm_residual_kernel(const __half* __restrict__ y, __nv_bfloat16* __restrict__ h,
+// All arithmetic in f32.  One warp per row; lane owns elements [c*256 + lane*8, +8).  Up to
+// H = 768 capped at 64 registers (4 blocks of 8 rows per SM) for more rows in flight (H = 768:
+// 5.26 -> 5.56 TB/s); wider rows keep 2 blocks per SM (1 above 1536, no spills).
+template <int H, bool FINAL>
+__global__ void __launch_bounds__(256, H <= 768 ? 4 : (H <= 1536 ? 2 : 1)) post_norm_residual_kernel(const __half* __restrict__ y, __nv_bfloat16* __restrict__ h,
                                           const float* __restrict__ w_post, float layer_scalar,
                                           const float* __restrict__ w_next, float eps, int n_tokens,
                                           __half* __restrict__ x, float* __restrict__ xf) {
   const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
+  constexpr int kVec = H / 256;  // 8-element chunks per lane
   if (t >= n_tokens) return;
-  const __half* yr = y + static_cast<size_t>(t) * kHidden;
-  __nv_bfloat16* hr = h + static_cast<size_t>(t) * kHidden;
+  const __half* yr = y + static_cast<size_t>(t) * H;
+  __nv_bfloat16* hr = h + static_cast<size_t>(t) * H;
   // raw 16-bit rows (12 + 12 registers): converted where used, so 4 blocks fit an SM
-  uint4 yu[kVecPerLane], hu[kVecPerLane];
+  uint4 yu[kVec], hu[kVec];
 #pragma unroll
-  for (int c = 0; c < kVecPerLane; ++c) {
+  for (int c = 0; c < kVec; ++c) {
     yu[c] = *reinterpret_cast<const uint4*>(yr + c * 256 + lane * 8);
     hu[c] = *reinterpret_cast<const uint4*>(hr + c * 256 + lane * 8);
   }
   float ss = 0.f;
 #pragma unroll
-  for (int c = 0; c < kVecPerLane; ++c) {
+  for (int c = 0; c < kVec; ++c) {
     const __half* e = reinterpret_cast<const __half*>(&yu[c]);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
@@ -188,11 +193,11 @@ __global__ void __launch_bounds__(256, 4) post_norm_residual_kernel(const __half
     }
   }
   ss = warp_sum(ss);
-  const float inv_y = 1.0f / sqrtf(ss / static_cast<float>(kHidden) + eps);
+  const float inv_y = 1.0f / sqrtf(ss / static_cast<float>(H) + eps);
   float ss2 = 0.f;
-  float hv[kVecPerLane][8];
+  float hv[kVec][8];
 #pragma unroll
-  for (int c = 0; c < kVecPerLane; ++c) {
+  for (int c = 0; c < kVec; ++c) {
     const int e0 = c * 256 + lane * 8;
     float wv[8];
     load_f32x8(w_post + e0, wv);
@@ -205,19 +210,19 @@ __global__ void __launch_bounds__(256, 4) post_norm_residual_kernel(const __half
     }
   }
   ss2 = warp_sum(ss2);
-  const float inv_h = 1.0f / sqrtf(ss2 / static_cast<float>(kHidden) + eps);
+  const float inv_h = 1.0f / sqrtf(ss2 / static_cast<float>(H) + eps);
 #pragma unroll
-  for (int c = 0; c < kVecPerLane; ++c) {
+  for (int c = 0; c < kVec; ++c) {
     const int e0 = c * 256 + lane * 8;
     float wv[8], o[8];
     load_f32x8(w_next + e0, wv);
 #pragma unroll
     for (int j = 0; j < 8; ++j) o[j] = hv[c][j] * inv_h * wv[j];
     if constexpr (FINAL) {
-      store_f32x8(xf + static_cast<size_t>(t) * kHidden + e0, o);
+      store_f32x8(xf + static_cast<size_t>(t) * H + e0, o);
     } else {
       store16x8<__nv_bfloat16>(hr + e0, hv[c]);
-      store16x8<__half>(x + static_cast<size_t>(t) * kHidden + e0, o);
+      store16x8<__half>(x + static_cast<size_t>(t) * H + e0, o);
     }
   }
 }
@@ -236,26 +241,27 @@ __global__ void positions_kernel(const int* __restrict__ cu_seqlens, int cu_base
 // pooled[b] = sum_{t in seq b} xf[t] / max(len_b, 1e-9)   (model.rs:671-680), f32, fixed
 // summation order (deterministic, independent of the other sequences of the batch).
 // Block (sequence b, segment s) sums tokens [512 s, 512 s + 512) of the sequence in order,
-// 192 threads x 4 columns.  A sequence of at most 512 tokens is one segment and is finished in
+// H / 4 threads x 4 columns.  A sequence of at most 512 tokens is one segment and is finished in
 // place; longer ones leave per-segment sums in `part` at slot floor(t0 / 512) + b + s (t0 = the
 // sequence's first token in the chunk: distinct for every (b, s), below T / 512 + n_seq), and
 // mean_pool_finish_kernel adds them in segment order.
 constexpr int kPoolSeg = 512;
 
-__device__ __forceinline__ void pool_write(float4 acc, float cnt, int b, int c, __half* pooled16, float* pooled_f32) {
+__device__ __forceinline__ void pool_write(float4 acc, float cnt, int b, int c, int H, __half* pooled16,
+                                           float* pooled_f32) {
   acc.x /= cnt;
   acc.y /= cnt;
   acc.z /= cnt;
   acc.w /= cnt;
-  if (pooled_f32) *reinterpret_cast<float4*>(pooled_f32 + static_cast<size_t>(b) * kHidden + c) = acc;
+  if (pooled_f32) *reinterpret_cast<float4*>(pooled_f32 + static_cast<size_t>(b) * H + c) = acc;
   uint2 pk;
   pk.x = pack_f16(acc.x, acc.y);
   pk.y = pack_f16(acc.z, acc.w);
-  *reinterpret_cast<uint2*>(pooled16 + static_cast<size_t>(b) * kHidden + c) = pk;
+  *reinterpret_cast<uint2*>(pooled16 + static_cast<size_t>(b) * H + c) = pk;
 }
 
 __global__ void mean_pool_kernel(const float* __restrict__ xf, const int* __restrict__ cu_seqlens, int cu_base,
-                                 int n_seq, __half* __restrict__ pooled16, float* __restrict__ pooled_f32,
+                                 int n_seq, int H, __half* __restrict__ pooled16, float* __restrict__ pooled_f32,
                                  float* __restrict__ part) {
   const int b = blockIdx.x, sg = blockIdx.y;
   if (b >= n_seq) return;
@@ -263,25 +269,25 @@ __global__ void mean_pool_kernel(const float* __restrict__ xf, const int* __rest
   const int n_segs = max(1, (t1 - t0 + kPoolSeg - 1) / kPoolSeg);
   if (sg >= n_segs) return;
   const int c = threadIdx.x * 4;
-  if (c >= kHidden) return;
+  if (c >= H) return;
   const int s0 = t0 + sg * kPoolSeg, s1 = min(t1, s0 + kPoolSeg);
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int t = s0; t < s1; ++t) {
-    const float4 v = *reinterpret_cast<const float4*>(xf + static_cast<size_t>(t) * kHidden + c);
+    const float4 v = *reinterpret_cast<const float4*>(xf + static_cast<size_t>(t) * H + c);
     acc.x += v.x;
     acc.y += v.y;
     acc.z += v.z;
     acc.w += v.w;
   }
   if (n_segs == 1) {
-    pool_write(acc, fmaxf(static_cast<float>(t1 - t0), 1e-9f), b, c, pooled16, pooled_f32);
+    pool_write(acc, fmaxf(static_cast<float>(t1 - t0), 1e-9f), b, c, H, pooled16, pooled_f32);
   } else {
     const size_t slot = static_cast<size_t>(t0 / kPoolSeg + b + sg);
-    *reinterpret_cast<float4*>(part + slot * kHidden + c) = acc;
+    *reinterpret_cast<float4*>(part + slot * H + c) = acc;
   }
 }
 
-__global__ void mean_pool_finish_kernel(const int* __restrict__ cu_seqlens, int cu_base, int n_seq,
+__global__ void mean_pool_finish_kernel(const int* __restrict__ cu_seqlens, int cu_base, int n_seq, int H,
                                         const float* __restrict__ part, __half* __restrict__ pooled16,
                                         float* __restrict__ pooled_f32) {
   const int b = blockIdx.x;
@@ -290,16 +296,16 @@ __global__ void mean_pool_finish_kernel(const int* __restrict__ cu_seqlens, int 
   const int n_segs = max(1, (t1 - t0 + kPoolSeg - 1) / kPoolSeg);
   if (n_segs == 1) return;  // finished by mean_pool_kernel
   const int c = threadIdx.x * 4;
-  if (c >= kHidden) return;
+  if (c >= H) return;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int sg = 0; sg < n_segs; ++sg) {
-    const float4 v = *reinterpret_cast<const float4*>(part + static_cast<size_t>(t0 / kPoolSeg + b + sg) * kHidden + c);
+    const float4 v = *reinterpret_cast<const float4*>(part + static_cast<size_t>(t0 / kPoolSeg + b + sg) * H + c);
     acc.x += v.x;
     acc.y += v.y;
     acc.z += v.z;
     acc.w += v.w;
   }
-  pool_write(acc, static_cast<float>(t1 - t0), b, c, pooled16, pooled_f32);
+  pool_write(acc, static_cast<float>(t1 - t0), b, c, H, pooled16, pooled_f32);
 }
 
 // L2-normalise (clamp 1e-12) then MRL: the first out_dim values renormalised

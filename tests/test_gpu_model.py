@@ -170,3 +170,31 @@ def test_baseline_init_one_layer(gguf_dir):
     ref_gap = 1.0 - cosine_rows(m1, m2)
     print("1-layer BASELINE init: 1-cos(gpu, exact) =", gpu_gap, " 1-cos(M1, exact) =", ref_gap)
     assert (gpu_gap <= np.maximum(2.0 * ref_gap, 1e-4)).all()
+
+
+@pytest.mark.parametrize("hidden,n_heads,n_kv,ffn,head_dims,weight_type,n_layers", [
+    (512, 4, 2, 2048, (2048, 1024, 512), "q8_0", 6),  # EmbeddingGemma 2 widths; a head stage wider than H
+    (1536, 6, 2, 1536, (768,), "q8_0", 2),
+    (1024, 4, 1, 1536, (1024,), "bf16", 2),
+    (2048, 8, 2, 2048, (2048,), "q8_0", 2),
+])
+def test_other_hidden_sizes(gguf_dir, hidden, n_heads, n_kv, ffn, head_dims, weight_type, n_layers):
+    """Hidden sizes other than 768 (the row kernels instantiated per width, the post-norm as a
+    row kernel after the O and down GEMMs): parity with the oracle on ragged sequences (one
+    longer than a pooling segment), a six-layer model with its global layer, and batch == single."""
+    import os
+    cfg = synth.small_config(n_layers=n_layers, hidden=hidden, n_heads=n_heads, n_kv_heads=n_kv, ffn=ffn,
+                             head_dims=head_dims, weight_type=weight_type, qk_gain_scale=0.25)
+    path = synth.ensure_gguf(os.path.join(str(gguf_dir), f"h{hidden}_{weight_type}.gguf"), cfg)
+    orc = oracle.OracleModel(path)
+    ids, lens = synth.make_batch(4, 600, orc.vocab, lengths=[600, 513, 64, 1])
+    with GlyprEmbedder.load_gguf(path, [0]) as emb:
+        assert emb.info.hidden == hidden and emb.info.embedding_dim == head_dims[-1]
+        got = emb.embed_tokens(ids, lens)
+        one = emb.embed_tokens(ids[2:3, : lens[2]], lens[2:3])
+        mrl = emb.embed_tokens(ids, lens, out_dim=128)
+        assert emb.device_status() == 0
+    np.testing.assert_array_equal(one[0], got[2])
+    np.testing.assert_allclose(mrl, np.stack([api.truncate_mrl(g, 128) for g in got]), atol=2e-6)
+    np.testing.assert_allclose(np.linalg.norm(got, axis=1), 1.0, atol=1e-5)
+    _check_both(got, orc, ids, lens)

@@ -95,11 +95,22 @@ def test_open_rejects_f32_linear(tmp_path, tiny_cfg):
     assert rc == api.GLP_ERR_UNSUPPORTED and "attn_k" in msg
 
 
-def test_open_rejects_other_hidden(tmp_path):
-    cfg = synth.small_config(n_layers=1, vocab=256, hidden=512, head_dims=(512,))
-    p = synth.write_gguf(str(tmp_path / "h512.gguf"), cfg)
+@pytest.mark.parametrize("hidden", [640, 2304])
+def test_open_rejects_other_hidden(tmp_path, hidden):
+    cfg = synth.small_config(n_layers=1, vocab=256, hidden=hidden, head_dims=(hidden,))
+    p = synth.write_gguf(str(tmp_path / f"h{hidden}.gguf"), cfg)
     rc, msg = _open(p)
-    assert rc == api.GLP_ERR_UNSUPPORTED and "768" in msg
+    assert rc == api.GLP_ERR_UNSUPPORTED and msg == "hidden size must be a multiple of 256 up to 2048"
+
+
+@pytest.mark.parametrize("hidden", [256, 512, 1024, 2048])
+def test_open_accepts_hidden_multiples_of_256(tmp_path, hidden):
+    """Hidden sizes the row kernels are compiled for pass the config checks; without a GPU the
+    open then stops at the first CUDA call, never at a format or support check."""
+    cfg = synth.small_config(n_layers=1, vocab=256, hidden=hidden, head_dims=(hidden,))
+    p = synth.write_gguf(str(tmp_path / f"h{hidden}.gguf"), cfg)
+    rc, msg = _open(p)
+    assert rc not in (api.GLP_ERR_UNSUPPORTED, api.GLP_ERR_FORMAT), msg
 
 
 def test_open_rejects_head_dim_override(tmp_path):
