@@ -33,7 +33,7 @@ GLP_ERR_DEVICE = 7
 GLP_ERR_CONTEXT_LIMIT = 8
 GLP_MAX_DEVICES = 16
 
-GLP_PROFILE_KINDS = 12
+GLP_PROFILE_KINDS = 14
 
 # Every symbol include/glypr_cuda.h declares (checked by the CPU test suite).
 EXPORTED_SYMBOLS = (

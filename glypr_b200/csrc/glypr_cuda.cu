@@ -29,6 +29,7 @@
 #include "gemm.cuh"
 #include "gguf.h"
 #include "glypr_cuda.h"
+#include "ple.cuh"
 #include "rowops.cuh"
 
 using glp::GemmParams;
@@ -363,6 +364,7 @@ struct Config {
   double eps = 1e-6, theta_swa = 1e4, theta_full = 1e6;
   std::vector<bool> sliding;
   uint32_t linear_type = glp::kGgmlQ8_0;
+  int ple_dim = 0;  // per-layer-embedding width D; 0 = no PLE tensors (model.rs:257-275)
 };
 
 int parse_config(const glp::GgufFile& g, Config* c) {
@@ -416,6 +418,12 @@ int parse_config(const glp::GgufFile& g, Config* c) {
   if (c->n_kv <= 0 || c->n_heads % c->n_kv) return fail(GLP_ERR_FORMAT, "head_count must be a multiple of head_count_kv");
   if (c->ffn % 128) return fail(GLP_ERR_UNSUPPORTED, "feed_forward_length must be a multiple of 128");
   if ((c->n_heads * c->head_dim) % 64) return fail(GLP_ERR_UNSUPPORTED, "attention width must be a multiple of 64");
+  if (g.tensor("per_layer_model_proj.weight")) {
+    // config.rs:100-102: embedding_length_per_layer_input, default 512
+    c->ple_dim = g.get_u32(a + "embedding_length_per_layer_input", &u) ? static_cast<int>(u) : 512;
+    if (c->ple_dim <= 0 || c->ple_dim % 128)
+      return fail(GLP_ERR_UNSUPPORTED, "embedding_length_per_layer_input must be a multiple of 128");
+  }
   return GLP_OK;
 }
 
@@ -439,12 +447,23 @@ int validate_tensors(const glp::GgufFile& g, const Config& c) {
     return fail(GLP_ERR_FORMAT, "bad shape for token_embd.weight");
   if (te->type != glp::kGgmlQ8_0 && te->type != glp::kGgmlBF16)
     return fail(GLP_ERR_UNSUPPORTED, "token_embd.weight must be Q8_0 or BF16");
-  if (g.tensor("per_layer_model_proj.weight"))
-    return fail(GLP_ERR_UNSUPPORTED, "per-layer embeddings (PLE) are not supported by this backend");
+  // per-layer embeddings (model.rs:257-275, 418-453): all of them or none
+  const int64_t PD = c.ple_dim;
+  if (PD) {
+    GLP_TRY(need("per_layer_model_proj.weight", {H, c.n_layers * PD}, true));
+    GLP_TRY(need("per_layer_proj_norm.weight", {PD}, false));
+  }
   for (int l = 0; l < c.n_layers; ++l) {
     const std::string p = "blk." + std::to_string(l) + ".";
-    if (g.tensor(p + "proj.weight") || g.tensor(p + "inp_gate.weight"))
-      return fail(GLP_ERR_UNSUPPORTED, "per-layer embeddings (PLE) are not supported by this backend");
+    if (PD) {
+      GLP_TRY(need(p + "inp_gate.weight", {H, PD}, true));
+      GLP_TRY(need(p + "proj.weight", {PD, H}, true));
+      GLP_TRY(need(p + "post_norm.weight", {H}, false));
+      const glp::GgufTensor* s = g.tensor(p + "layer_output_scale.weight");
+      if (!s) return fail(GLP_ERR_FORMAT, "missing tensor " + p + "layer_output_scale.weight");
+    } else if (g.tensor(p + "proj.weight") || g.tensor(p + "inp_gate.weight")) {
+      return fail(GLP_ERR_FORMAT, "missing tensor per_layer_model_proj.weight");
+    }
     GLP_TRY(need(p + "attn_norm.weight", {H}, false));
     GLP_TRY(need(p + "attn_q_norm.weight", {D}, false));
     GLP_TRY(need(p + "attn_k_norm.weight", {D}, false));
@@ -492,6 +511,10 @@ struct LayerW {
   bool sliding = true;
   CUtensorMap m_qkv, m_o, m_gu, m_down;
   CUtensorMap p_qkv, p_o, p_gu, p_down;  // the same weights, 128-row boxes for CTA pairs
+  // per-layer-embedding block (ple.rs:96-145): gate [D, H], projection [H, D], post-norm
+  __half *ple_gate = nullptr, *ple_proj = nullptr;
+  float* ple_post = nullptr;
+  CUtensorMap m_pg, m_pp, p_pg, p_pp;
 };
 
 struct HeadW {
@@ -510,6 +533,10 @@ struct Device {
   std::vector<LayerW> layers;
   float* out_norm = nullptr;
   std::vector<HeadW> head;
+  // per-layer embeddings: projection [L * D, H] and its norm gain [D]
+  __half* ple_w = nullptr;
+  float* ple_norm = nullptr;
+  CUtensorMap m_plew, p_plew;
   float2 *cs_swa = nullptr, *cs_full = nullptr;  // RoPE tables (sliding / global layers)
   int64_t cap_tokens = 0;
   int cap_seqs = 0;
@@ -525,6 +552,8 @@ struct Device {
   float* pool_part = nullptr;  // per-segment sums of sequences longer than one pooling segment
   __half* mid = nullptr;
   float* emb = nullptr;
+  __half* ple = nullptr;     // per-layer inputs [T, L, D] (PLE models)
+  __half* ple_g = nullptr;   // the PLE block's gate activations [T, D]
   int* status = nullptr;
   // host-API staging (device + pinned host), grown on demand
   int* d_ids = nullptr;
@@ -606,10 +635,13 @@ enum ProfKind : int {
   kProfL2,
   kProfMisc,
   kProfKernelApi,
+  kProfPleGemm,  // per-layer-embedding projections (PLE models only)
+  kProfPleRows,  // per-layer-embedding norm and GeGLU
 };
 const char* const kProfNames[GLP_PROFILE_KINDS] = {
     "embed_gather_norm", "gemm_qkv_norm_rope", "flash_attention", "gemm_o", "post_norm_residual",
-    "gemm_gate_up_geglu", "gemm_down", "mean_pool", "gemm_head", "l2_mrl", "positions", "kernel_api"};
+    "gemm_gate_up_geglu", "gemm_down", "mean_pool", "gemm_head", "l2_mrl", "positions", "kernel_api",
+    "ple_gemm", "ple_rows"};
 
 // Bracket one kernel launch: counts it and, when profiling is on, records an event pair on
 // the launching stream.  Returns the launch's status.
@@ -765,6 +797,11 @@ int setup_device(Device& d, const Config& c, const glp::GgufFile& g, int64_t cap
     staging_bytes = std::max(staging_bytes, t->nbytes);
   }
   if (const glp::GgufTensor* t = g.tensor("output.weight")) staging_bytes = std::max(staging_bytes, t->nbytes);
+  if (const glp::GgufTensor* t = g.tensor("per_layer_model_proj.weight"))
+    staging_bytes = std::max(staging_bytes, t->nbytes);
+  for (const auto* nm : {"inp_gate", "proj"})
+    if (const glp::GgufTensor* t = g.tensor(std::string("blk.0.") + nm + ".weight"))
+      staging_bytes = std::max(staging_bytes, t->nbytes);
   staging_bytes = std::max(staging_bytes, static_cast<size_t>(4) * F * std::max(H, F));
   void* staging = nullptr;
   GLP_CUDA(cudaMalloc(&staging, staging_bytes));
@@ -778,8 +815,6 @@ int setup_device(Device& d, const Config& c, const glp::GgufFile& g, int64_t cap
     LayerW& L = d.layers[l];
     const std::string p = "blk." + std::to_string(l) + ".";
     L.sliding = c.sliding[l];
-    if (g.tensor(p + "proj.weight") || g.tensor(p + "inp_gate.weight"))
-      return fail(GLP_ERR_UNSUPPORTED, "per-layer embeddings (PLE) are not supported by this backend");
     GLP_TRY(upload_gain(d, g, p + "attn_norm.weight", H, &L.attn_norm));
     GLP_TRY(upload_gain(d, g, p + "attn_q_norm.weight", D, &L.q_norm));
     GLP_TRY(upload_gain(d, g, p + "attn_k_norm.weight", D, &L.k_norm));
@@ -810,6 +845,26 @@ int setup_device(Device& d, const Config& c, const glp::GgufFile& g, int64_t cap
     GLP_TRY(make_map16(&L.p_o, L.o, H, AW, AW, 128, true));
     GLP_TRY(make_map16(&L.p_gu, L.gu, 2 * F, H, H, 128, true));
     GLP_TRY(make_map16(&L.p_down, L.down, H, F, F, 128, true));
+    if (c.ple_dim) {
+      const int PD = c.ple_dim;
+      GLP_TRY(upload_gain(d, g, p + "post_norm.weight", H, &L.ple_post));
+      GLP_TRY(d.alloc(&L.ple_gate, static_cast<size_t>(PD) * H));
+      GLP_TRY(d.alloc(&L.ple_proj, static_cast<size_t>(H) * PD));
+      GLP_TRY(upload_linear(d, g, p + "inp_gate.weight", PD, H, L.ple_gate, 0, 0, 0, staging, staging_bytes));
+      GLP_TRY(upload_linear(d, g, p + "proj.weight", H, PD, L.ple_proj, 0, 0, 0, staging, staging_bytes));
+      GLP_TRY(make_map16(&L.m_pg, L.ple_gate, PD, H, H, bn_for(PD), true));
+      GLP_TRY(make_map16(&L.p_pg, L.ple_gate, PD, H, H, 128, true));
+      GLP_TRY(make_map16(&L.m_pp, L.ple_proj, H, PD, PD, bn_for(H), true));
+      GLP_TRY(make_map16(&L.p_pp, L.ple_proj, H, PD, PD, 128, true));
+    }
+  }
+  if (c.ple_dim) {
+    const int LD = c.n_layers * c.ple_dim;
+    GLP_TRY(upload_gain(d, g, "per_layer_proj_norm.weight", c.ple_dim, &d.ple_norm));
+    GLP_TRY(d.alloc(&d.ple_w, static_cast<size_t>(LD) * H));
+    GLP_TRY(upload_linear(d, g, "per_layer_model_proj.weight", LD, H, d.ple_w, 0, 0, 0, staging, staging_bytes));
+    GLP_TRY(make_map16(&d.m_plew, d.ple_w, LD, H, H, bn_for(LD), true));
+    GLP_TRY(make_map16(&d.p_plew, d.ple_w, LD, H, H, 128, true));
   }
   GLP_TRY(upload_gain(d, g, "output_norm.weight", H, &d.out_norm));
   // dense head: dense.0 .. dense.N (BASELINE two-stage 768->3072->768), else output.weight
@@ -860,6 +915,10 @@ int setup_device(Device& d, const Config& c, const glp::GgufFile& g, int64_t cap
   GLP_TRY(d.alloc(&d.attn, static_cast<size_t>(cap_tokens) * AW));
   GLP_TRY(d.alloc(&d.y, static_cast<size_t>(cap_tokens) * H));
   GLP_TRY(d.alloc(&d.a, static_cast<size_t>(cap_tokens) * F));
+  if (c.ple_dim) {
+    GLP_TRY(d.alloc(&d.ple, static_cast<size_t>(cap_tokens) * c.n_layers * c.ple_dim));
+    GLP_TRY(d.alloc(&d.ple_g, static_cast<size_t>(cap_tokens) * c.ple_dim));
+  }
   GLP_TRY(d.alloc(&d.pos, static_cast<size_t>(cap_tokens)));
   GLP_TRY(d.alloc(&d.pooled, static_cast<size_t>(cap_seqs) * max_head));  // also a head stage's output
   GLP_TRY(d.alloc(&d.pool_part, (static_cast<size_t>(cap_tokens) / glp::kPoolSeg + cap_seqs + 1) * H));
@@ -891,6 +950,10 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
     }));
     const unsigned rows_grid = static_cast<unsigned>((T + 7) / 8);
     const float scale = static_cast<float>(std::sqrt(static_cast<double>(H)));
+    // per-layer embeddings: the embedding rows x0 (f16, staged in y until layer 0's O
+    // projection) feed the projection to [T, L * D]
+    const int PD = c.ple_dim, LD = c.n_layers * c.ple_dim;
+    const bool ple = PD != 0;
     const double row_in = d.table_type == glp::kGgmlQ8_0 ? H / 32 * 34.0 : 2.0 * H;
     GLP_TRY(prof_launch(d, st, kProfEmbed, 0.0, Td * (4.0 + row_in + 4.0 * H), [&] {
       return with_hidden(H, [&](auto hc) {
@@ -898,11 +961,11 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
         if (d.table_type == glp::kGgmlQ8_0)
           glp::embed_gather_norm_kernel<kH><<<rows_grid, 256, 0, st>>>(static_cast<const uint8_t*>(d.table),
                                                                        d_ids_chunk, T, scale, d.layers[0].attn_norm,
-                                                                       eps, d.h, d.x);
+                                                                       eps, d.h, d.x, ple ? d.y : nullptr);
         else
           glp::embed_gather_norm_bf16_kernel<kH><<<rows_grid, 256, 0, st>>>(
               static_cast<const __nv_bfloat16*>(d.table), d_ids_chunk, T, scale, d.layers[0].attn_norm, eps, d.h,
-              d.x);
+              d.x, ple ? d.y : nullptr);
         GLP_CUDA(cudaGetLastError());
         return GLP_OK;
       });
@@ -910,6 +973,29 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
 
     CUtensorMap m_x, m_attn, m_a, m_qkv_out;
     GLP_TRY(make_map16(&m_x, d.x, T, H, H, 128, true));
+    CUtensorMap m_pg;  // the PLE block's gate activations (the projection's A operand)
+    if (ple) {
+      CUtensorMap m_x0;
+      GLP_TRY(make_map16(&m_x0, d.y, T, H, H, 128, true));
+      GLP_TRY(make_map16(&m_pg, d.ple_g, T, PD, PD, 128, true));
+      GemmParams pp{};
+      pp.M = T;
+      pp.N = LD;
+      pp.K = H;
+      pp.C = d.ple;
+      pp.ldc = LD;
+      pp.status = d.status;
+      GLP_TRY(prof_launch(d, st, kProfPleGemm, gemm_flops(Td, LD, H), gemm_bytes(Td, LD, H, 2.0), [&] {
+        return launch_gemm<__half>(m_x0, d.m_plew, bn_for(LD), glp::kEpiStore16, pp, st, &d.p_plew);
+      }));
+      const int64_t rows = static_cast<int64_t>(T) * c.n_layers;
+      GLP_TRY(prof_launch(d, st, kProfPleRows, 0.0, 4.0 * rows * PD, [&] {
+        glp::ple_norm_kernel<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, st>>>(
+            d.ple, rows, PD, static_cast<float>(std::pow(static_cast<double>(H), -0.5)), d.ple_norm, eps);
+        GLP_CUDA(cudaGetLastError());
+        return GLP_OK;
+      }));
+    }
     GLP_TRY(make_map16(&m_qkv_out, d.qkv, T, QKV, QKV, 32, true));  // the QKV epilogue's bulk stores
     GLP_TRY(make_map16(&m_attn, d.attn, T, AW, AW, 128, true));
     GLP_TRY(make_map16(&m_a, d.a, T, F, F, 128, true));
@@ -976,7 +1062,7 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
                             [&] { return launch_gemm<__half>(m_attn, L.m_o, bn_for(H), glp::kEpiStore16, po, st, &L.p_o); }));
         GLP_TRY(prof_launch(d, st, kProfPostNorm, 0.0, post_bytes, [&] {
           return with_hidden(H, [&](auto hc) {
-            glp::post_norm_residual_kernel<decltype(hc)::value, false>
+            glp::post_norm_residual_kernel<decltype(hc)::value, glp::kPostNext>
                 <<<rows_grid, 256, 0, st>>>(d.y, d.h, L.post_attn, 1.0f, L.ffn_norm, eps, T, d.x, nullptr);
             GLP_CUDA(cudaGetLastError());
             return GLP_OK;
@@ -1003,7 +1089,7 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
       pd.ldc = H;
       pd.status = d.status;
       const bool last = l + 1 == c.n_layers;
-      if (fused && !last) {
+      if (fused && !last && !ple) {
         pd.h = d.h;
         pd.x_next = d.x;
         pd.w_post = L.post_ffw;
@@ -1016,15 +1102,56 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
       }
       GLP_TRY(prof_launch(d, st, kProfGemmDown, gemm_flops(Td, H, F), gemm_bytes(Td, H, F, 2.0),
                           [&] { return launch_gemm<__half>(m_a, L.m_down, bn_for(H), glp::kEpiStore16, pd, st, &L.p_down); }));
+      if (ple) {
+        // ple.rs:118-145 after the FFN block: h2 = h + RMSNorm(y) w (kept raw in x for the
+        // gate), g = geglu(gate(h2), P_l), y = proj(g), then the post-norm, residual add and
+        // layer scalar of the shared tail below
+        GLP_TRY(prof_launch(d, st, kProfPostNorm, 0.0, post_bytes, [&] {
+          return with_hidden(H, [&](auto hc) {
+            glp::post_norm_residual_kernel<decltype(hc)::value, glp::kPostRaw>
+                <<<rows_grid, 256, 0, st>>>(d.y, d.h, L.post_ffw, 1.0f, nullptr, eps, T, d.x, nullptr);
+            GLP_CUDA(cudaGetLastError());
+            return GLP_OK;
+          });
+        }));
+        GemmParams pg2{};
+        pg2.M = T;
+        pg2.N = PD;
+        pg2.K = H;
+        pg2.C = d.ple_g;
+        pg2.ldc = PD;
+        pg2.status = d.status;
+        GLP_TRY(prof_launch(d, st, kProfPleGemm, gemm_flops(Td, PD, H), gemm_bytes(Td, PD, H, 2.0), [&] {
+          return launch_gemm<__half>(m_x, L.m_pg, bn_for(PD), glp::kEpiStore16, pg2, st, &L.p_pg);
+        }));
+        const int64_t n_el = static_cast<int64_t>(T) * PD;
+        GLP_TRY(prof_launch(d, st, kProfPleRows, 0.0, 6.0 * n_el, [&] {
+          glp::ple_geglu_kernel<<<static_cast<unsigned>((n_el / 8 + 255) / 256), 256, 0, st>>>(d.ple_g, d.ple, T, PD,
+                                                                                             l, c.n_layers);
+          GLP_CUDA(cudaGetLastError());
+          return GLP_OK;
+        }));
+        GemmParams pp2{};
+        pp2.M = T;
+        pp2.N = H;
+        pp2.K = PD;
+        pp2.C = d.y;
+        pp2.ldc = H;
+        pp2.status = d.status;
+        GLP_TRY(prof_launch(d, st, kProfPleGemm, gemm_flops(Td, H, PD), gemm_bytes(Td, H, PD, 2.0), [&] {
+          return launch_gemm<__half>(m_pg, L.m_pp, bn_for(H), glp::kEpiStore16, pp2, st, &L.p_pp);
+        }));
+      }
+      const float* w_tail = ple ? L.ple_post : L.post_ffw;
       GLP_TRY(prof_launch(d, st, kProfPostNorm, 0.0, last ? Td * 8.0 * H : post_bytes, [&] {
         return with_hidden(H, [&](auto hc) {
           constexpr int kH = decltype(hc)::value;
           if (!last)
-            glp::post_norm_residual_kernel<kH, false><<<rows_grid, 256, 0, st>>>(
-                d.y, d.h, L.post_ffw, L.layer_scalar, d.layers[l + 1].attn_norm, eps, T, d.x, nullptr);
+            glp::post_norm_residual_kernel<kH, glp::kPostNext><<<rows_grid, 256, 0, st>>>(
+                d.y, d.h, w_tail, L.layer_scalar, d.layers[l + 1].attn_norm, eps, T, d.x, nullptr);
           else
-            glp::post_norm_residual_kernel<kH, true><<<rows_grid, 256, 0, st>>>(
-                d.y, d.h, L.post_ffw, L.layer_scalar, d.out_norm, eps, T, nullptr, d.xf);
+            glp::post_norm_residual_kernel<kH, glp::kPostFinal><<<rows_grid, 256, 0, st>>>(
+                d.y, d.h, w_tail, L.layer_scalar, d.out_norm, eps, T, nullptr, d.xf);
           GLP_CUDA(cudaGetLastError());
           return GLP_OK;
         });

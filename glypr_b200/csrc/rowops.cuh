@@ -96,12 +96,14 @@ __device__ __forceinline__ void store16x8(T* p, const float* v) {
 // ---------------------------------------------------------------------------- embedding
 // h[t] = dequant(E[id_t]) * f32(sqrt(H))   (model.rs:252-255, 507-508)
 // x[t] = f16(RMSNorm(h[t]) * w)             (first layer's attn_norm, norm.rs:22-63)
+// x_raw[t] = f16(h[t] in f32), when given    (the per-layer-embedding projection's input)
 // One warp per token; lane l covers elements l, l+32, ... (coalesced byte reads of the
 // 34-byte blocks).
 template <int H>
 __global__ void embed_gather_norm_kernel(const uint8_t* __restrict__ table, const int* __restrict__ ids,
                                          int n_tokens, float scale, const float* __restrict__ w, float eps,
-                                         __nv_bfloat16* __restrict__ h, __half* __restrict__ x) {
+                                         __nv_bfloat16* __restrict__ h, __half* __restrict__ x,
+                                         __half* __restrict__ x_raw) {
   const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (t >= n_tokens) return;
@@ -125,6 +127,7 @@ __global__ void embed_gather_norm_kernel(const uint8_t* __restrict__ table, cons
     const int e = b * 32 + lane;
     hr[e] = __float2bfloat16_rn(v[b]);
     xr[e] = __float2half_rn(v[b] * inv * __ldg(w + e));
+    if (x_raw) x_raw[static_cast<size_t>(t) * H + e] = __float2half_rn(v[b]);
   }
 }
 
@@ -132,7 +135,8 @@ __global__ void embed_gather_norm_kernel(const uint8_t* __restrict__ table, cons
 template <int H>
 __global__ void embed_gather_norm_bf16_kernel(const __nv_bfloat16* __restrict__ table, const int* __restrict__ ids,
                                               int n_tokens, float scale, const float* __restrict__ w, float eps,
-                                              __nv_bfloat16* __restrict__ h, __half* __restrict__ x) {
+                                              __nv_bfloat16* __restrict__ h, __half* __restrict__ x,
+                                              __half* __restrict__ x_raw) {
   const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (t >= n_tokens) return;
@@ -153,18 +157,23 @@ __global__ void embed_gather_norm_bf16_kernel(const __nv_bfloat16* __restrict__ 
     const int e = b * 32 + lane;
     hr[e] = __float2bfloat16_rn(v[b]);
     xr[e] = __float2half_rn(v[b] * inv * __ldg(w + e));
+    if (x_raw) x_raw[static_cast<size_t>(t) * H + e] = __float2half_rn(v[b]);
   }
 }
 
 // ---------------------------------------------------------------------------- post-norm
 // h <- (h + RMSNorm(y) * w_post) * layer_scalar            (norm.rs:65-94, layer.rs:20-50)
-// then the next pre-norm:  x = RMSNorm(h) * w_next
-//   FINAL = false: h is updated (bf16) and x is f16 (the next GEMM's input)
-//   FINAL = true : the normalised row is written to xf in f32 (output_norm, model.rs:576)
+// then, by MODE:
+//   kPostNext : the next pre-norm x = f16(RMSNorm(h) * w_next), h updated (bf16)
+//   kPostFinal: the final norm RMSNorm(h) * w_next written to xf in f32 (output_norm, model.rs:576)
+//   kPostRaw  : x = f16(h) without a norm, h updated (the per-layer-embedding block's gate
+//               input is the un-normalised residual, ple.rs:130)
 // All arithmetic in f32.  One warp per row; lane owns elements [c*256 + lane*8, +8).  Up to
 // H = 768 capped at 64 registers (4 blocks of 8 rows per SM) for more rows in flight (H = 768:
 // 5.26 -> 5.56 TB/s); wider rows keep 2 blocks per SM (1 above 1536, no spills).
-template <int H, bool FINAL>
+constexpr int kPostNext = 0, kPostFinal = 1, kPostRaw = 2;
+
+template <int H, int MODE>
 __global__ void __launch_bounds__(256, H <= 768 ? 4 : (H <= 1536 ? 2 : 1)) post_norm_residual_kernel(const __half* __restrict__ y, __nv_bfloat16* __restrict__ h,
                                           const float* __restrict__ w_post, float layer_scalar,
                                           const float* __restrict__ w_next, float eps, int n_tokens,
@@ -209,6 +218,15 @@ __global__ void __launch_bounds__(256, H <= 768 ? 4 : (H <= 1536 ? 2 : 1)) post_
       ss2 = fmaf(hv[c][j], hv[c][j], ss2);
     }
   }
+  if constexpr (MODE == kPostRaw) {
+#pragma unroll
+    for (int c = 0; c < kVec; ++c) {
+      const int e0 = c * 256 + lane * 8;
+      store16x8<__nv_bfloat16>(hr + e0, hv[c]);
+      store16x8<__half>(x + static_cast<size_t>(t) * H + e0, hv[c]);
+    }
+    return;
+  }
   ss2 = warp_sum(ss2);
   const float inv_h = 1.0f / sqrtf(ss2 / static_cast<float>(H) + eps);
 #pragma unroll
@@ -218,7 +236,7 @@ __global__ void __launch_bounds__(256, H <= 768 ? 4 : (H <= 1536 ? 2 : 1)) post_
     load_f32x8(w_next + e0, wv);
 #pragma unroll
     for (int j = 0; j < 8; ++j) o[j] = hv[c][j] * inv_h * wv[j];
-    if constexpr (FINAL) {
+    if constexpr (MODE == kPostFinal) {
       store_f32x8(xf + static_cast<size_t>(t) * H + e0, o);
     } else {
       store16x8<__nv_bfloat16>(hr + e0, hv[c]);

@@ -16,9 +16,14 @@ schema the reference loader looks up:
   ``model.rs:472-473``, which is also accepted by the loader when ``head_dims`` is
   ``(embedding_out,)``).
 
-Per-layer-embedding tensors (``ple.rs``) are not written: absent PLE is the identity
-(zero ``proj`` weight and a layer scalar of 1 give ``h' = (h + RMSNorm(0)) * 1 = h``,
-``ple.rs:118-145``).
+Per-layer-embedding tensors (``ple.rs``) are written only when ``ple_dim > 0``: absent PLE is
+the identity (zero ``proj`` weight and a layer scalar of 1 give ``h' = (h + RMSNorm(0)) * 1 =
+h``, ``ple.rs:118-145``).  With ``ple_dim = D`` the file carries the reference's PLE schema
+(``model.rs:257-275, 418-453``): metadata ``embedding_length_per_layer_input`` = D,
+``per_layer_model_proj.weight`` [L*D, H], ``per_layer_proj_norm.weight`` [D] and per layer
+``inp_gate.weight`` [D, H], ``proj.weight`` [H, D], ``post_norm.weight`` [H] and
+``layer_output_scale.weight`` [1].  They follow every other tensor, so the other tensors'
+seeds (their index in the order) are the same with or without PLE.
 
 Quantiser (pinned here; the reference only reads the blocks): per 32-element block,
 ``d = absmax / 127`` in f32, stored as IEEE fp16 (round to nearest even);
@@ -86,6 +91,8 @@ class EncoderConfig:
     # logit by 1/16 (a well-conditioned variant used for end-to-end parity tests; the
     # reference attention scale stays 1.0, standard.rs:62).
     qk_gain_scale: float = 1.0
+    # per-layer-embedding width D (0 = no PLE tensors)
+    ple_dim: int = 0
 
     @property
     def embedding_out(self) -> int:
@@ -218,6 +225,14 @@ def _tensor_order(cfg: EncoderConfig) -> List[Tuple[str, Tuple[int, ...], str]]:
         for j, dim in enumerate(cfg.head_dims):
             order.append((f"dense.{j}.weight", (dim, prev), "mat"))
             prev = dim
+    if cfg.ple_dim:
+        pd = cfg.ple_dim
+        order += [("per_layer_model_proj.weight", (cfg.n_layers * pd, h), "mat"),
+                  ("per_layer_proj_norm.weight", (pd,), "gain")]
+        for i in range(cfg.n_layers):
+            p = f"blk.{i}."
+            order += [(p + "inp_gate.weight", (pd, h), "mat"), (p + "proj.weight", (h, pd), "mat"),
+                      (p + "post_norm.weight", (h,), "gain"), (p + "layer_output_scale.weight", (1,), "gain")]
     return order
 
 
@@ -278,6 +293,8 @@ def metadata(cfg: EncoderConfig, tokenizer: Optional[Tuple[Sequence[str], Sequen
     ]
     if tokenizer is not None:
         kvs.append(_kv("tokenizer.ggml.merges", _ARR, (_STR, list(tokenizer[1]))))
+    if cfg.ple_dim:
+        kvs.append(_kv(a + "embedding_length_per_layer_input", _U32, cfg.ple_dim))
     return kvs
 
 

@@ -99,7 +99,7 @@ int glp_device_status(glp_ctx* ctx, int dev_index, int* status);
 /* ---- per-kernel profiling (the reference's forward_profiled, profile.rs:55-430, done with
  * CUDA events on the launching stream instead of wall clock + device sync) ---- */
 
-#define GLP_PROFILE_KINDS 12
+#define GLP_PROFILE_KINDS 14
 
 typedef struct glp_profile {
   int n_kinds;

@@ -22,6 +22,10 @@
 //   rope.rs:14-106          inv_freq in f64 -> f32, freqs = pos * inv_freq (f32), NeoX halves
 //   mlp.rs:31-70, cpu_simd/geglu.rs:6-18       tanh GELU with the +-10 clamp
 //   linear.rs:150-172       Q8_0 linears through candle QMatMul on f32 activations
+//   ple.rs:48-145, model.rs:257-275, 418-453, 527-542, layer.rs:44-49, norm.rs:65-94
+//                           per-layer embeddings (when per_layer_model_proj.weight exists):
+//                           P = RMSNorm_D(proj(x0) * f32(H^-0.5)) * w, [t, L, D]; after the FFN
+//                           block h = (h + RMSNorm(proj_l(geglu(gate_l(h), P[:, l]))) * w_l) * s_l
 // Third-party arithmetic restated from its published design (candle-core 0.11.0,
 // Cargo.lock:258-261, not vendored): QMatMul on CPU quantises each activation row to Q8_0
 // (ggml quantize_row_q8_0: d = amax/127, q = roundf(x/d)) and sums int8 block dot products
@@ -239,7 +243,9 @@ struct Linear {
 
 struct Layer {
   Linear q, k, v, o, gate, up, down;
-  std::vector<float> attn_norm, q_norm, k_norm, post_attn, ffn_norm, post_ffw;
+  Linear ple_gate, ple_proj;  // PLE block (ple.rs:96-145): inp_gate [D, H], proj [H, D]
+  std::vector<float> attn_norm, q_norm, k_norm, post_attn, ffn_norm, post_ffw, ple_post;
+  float scalar = 1.0f;  // layer_output_scale (1 when absent)
   bool sliding = true;
   int head_dim = 256, n_kv = 1;
   double theta = 1e4;
@@ -256,6 +262,9 @@ struct oracle_model {
   std::vector<Layer> layers;
   std::vector<float> out_norm;
   std::vector<Linear> head;
+  int ple_dim = 0;  // 0: no per-layer embeddings
+  Linear ple_model_proj;
+  std::vector<float> ple_norm;
   std::string err;
 };
 
@@ -525,9 +534,39 @@ bool load_model(oracle_model* m, const char* path) {
         !get_linear(g, p + "ffn_up.weight", m->ffn, H, &L.up) ||
         !get_linear(g, p + "ffn_down.weight", H, m->ffn, &L.down))
       return false;
-    if (g.tensors.count(p + "proj.weight") || g.tensors.count(p + "layer_output_scale.weight")) {
-      g_err = "per-layer-embedding tensors are not supported by this oracle";
+    auto sc = g.tensors.find(p + "layer_output_scale.weight");
+    if (sc != g.tensors.end()) {
+      std::vector<float> v;
+      if (!get_f32_vec(g, sc->first, 1, &v)) return false;
+      L.scalar = v[0];
+    }
+  }
+  // model.rs:257-275 (TextPLE) and 418-440 (TextPLEBlock per layer)
+  if (g.tensors.count("per_layer_model_proj.weight")) {
+    m->ple_dim = (int)meta_num(g, a + "embedding_length_per_layer_input", 512);
+    const int64_t D = m->ple_dim;
+    if (!get_linear(g, "per_layer_model_proj.weight", m->n_layers * D, H, &m->ple_model_proj) ||
+        !get_f32_vec(g, "per_layer_proj_norm.weight", D, &m->ple_norm))
       return false;
+    for (int i = 0; i < m->n_layers; ++i) {
+      Layer& L = m->layers[i];
+      std::string p = "blk." + std::to_string(i) + ".";
+      if (!get_linear(g, p + "inp_gate.weight", D, H, &L.ple_gate) ||
+          !get_linear(g, p + "proj.weight", H, D, &L.ple_proj) ||
+          !get_f32_vec(g, p + "post_norm.weight", H, &L.ple_post))
+        return false;
+      if (!g.tensors.count(p + "layer_output_scale.weight")) {
+        g_err = "missing tensor " + p + "layer_output_scale.weight";
+        return false;
+      }
+    }
+  } else {
+    for (int i = 0; i < m->n_layers; ++i) {
+      std::string p = "blk." + std::to_string(i) + ".";
+      if (g.tensors.count(p + "proj.weight") || g.tensors.count(p + "inp_gate.weight")) {
+        g_err = "missing tensor per_layer_model_proj.weight";
+        return false;
+      }
     }
   }
   if (!get_f32_vec(g, "output_norm.weight", H, &m->out_norm)) return false;
@@ -566,6 +605,16 @@ void forward_seq(const oracle_model* m, const int32_t* ids, int64_t t, int mode,
     dequant_row(emb, ids[i], &h[(size_t)(i * H)]);
     for (int64_t j = 0; j < H; ++j) h[(size_t)(i * H + j)] *= scale;
   }
+  // ple.rs:48-93: P = RMSNorm(proj(x0) * f32(H^-0.5)) * w over each of the L slices of D
+  const int64_t PD = m->ple_dim, NL = m->n_layers;
+  std::vector<float> ple;
+  if (PD) {
+    ple.resize((size_t)(t * NL * PD));
+    linear_forward(m->ple_model_proj, h.data(), t, ple.data(), mode);
+    const float ps = (float)std::pow((double)H, -0.5);
+    for (auto& v : ple) v *= ps;
+    rmsnorm_rows(ple.data(), m->ple_norm.data(), t * NL, PD, eps, ple.data());
+  }
   for (int l = 0; l < m->n_layers; ++l) {
     const Layer& L = m->layers[l];
     const int D = L.head_dim, NH = m->n_heads, KV = L.n_kv;
@@ -595,7 +644,20 @@ void forward_seq(const oracle_model* m, const int32_t* ids, int64_t t, int mode,
     for (size_t i = 0; i < gt.size(); ++i) gt[i] = geglu1(gt[i], up[i]);
     linear_forward(L.down, gt.data(), t, y.data(), mode);
     rmsnorm_rows(y.data(), L.post_ffw.data(), t, H, eps, y.data());
-    for (size_t i = 0; i < h.size(); ++i) h[i] += y[i];
+    if (PD) {
+      for (size_t i = 0; i < h.size(); ++i) h[i] += y[i];
+      // ple.rs:118-145: gate on the un-normalised residual, GeGLU with this layer's slice,
+      // projection, post-norm, residual add, then the layer scalar (norm.rs:65-94)
+      std::vector<float> pg((size_t)(t * PD));
+      linear_forward(L.ple_gate, h.data(), t, pg.data(), mode);
+      for (int64_t i = 0; i < t; ++i)
+        for (int64_t j = 0; j < PD; ++j)
+          pg[(size_t)(i * PD + j)] = geglu1(pg[(size_t)(i * PD + j)], ple[(size_t)((i * NL + l) * PD + j)]);
+      linear_forward(L.ple_proj, pg.data(), t, y.data(), mode);
+      rmsnorm_rows(y.data(), L.ple_post.data(), t, H, eps, y.data());
+    }
+    // without PLE the block is the identity and the layer scalar applies to the FFN sum
+    for (size_t i = 0; i < h.size(); ++i) h[i] = (h[i] + y[i]) * L.scalar;
     if (l == stop_layer) {
       memcpy(out, h.data(), sizeof(float) * h.size());
       return;

@@ -198,3 +198,34 @@ def test_other_hidden_sizes(gguf_dir, hidden, n_heads, n_kv, ffn, head_dims, wei
     np.testing.assert_allclose(mrl, np.stack([api.truncate_mrl(g, 128) for g in got]), atol=2e-6)
     np.testing.assert_allclose(np.linalg.norm(got, axis=1), 1.0, atol=1e-5)
     _check_both(got, orc, ids, lens)
+
+
+@pytest.mark.parametrize("kw", [
+    # EmbeddingGemma 2 widths (hidden 512, FFN 2048, 4 query heads over 2 KV heads) with
+    # 256-wide per-layer inputs, six layers with the global one
+    dict(n_layers=6, hidden=512, n_heads=4, n_kv_heads=2, ffn=2048, head_dims=(2048, 512), ple_dim=256),
+    # BASELINE widths (the fused row-norm O projection) with 512-wide per-layer inputs
+    dict(n_layers=2, ple_dim=512),
+])
+def test_per_layer_embeddings(gguf_dir, kw):
+    """Per-layer embeddings (ple.rs:48-145): the per-layer inputs from the embedding rows, and
+    after each FFN block the gate, GeGLU with the layer's slice, projection, post-norm,
+    residual and layer scalar.  Parity with the oracle, batch == single."""
+    import os
+    cfg = synth.small_config(qk_gain_scale=0.25, **kw)
+    path = synth.ensure_gguf(os.path.join(str(gguf_dir), f"ple_{cfg.hidden}_{cfg.ple_dim}.gguf"), cfg)
+    orc = oracle.OracleModel(path)
+    ids, lens = synth.make_batch(4, 600, orc.vocab, lengths=[600, 513, 64, 1])
+    with GlyprEmbedder.load_gguf(path, [0]) as emb:
+        got = emb.embed_tokens(ids, lens)
+        one = emb.embed_tokens(ids[2:3, : lens[2]], lens[2:3])
+        assert emb.device_status() == 0
+    np.testing.assert_array_equal(one[0], got[2])
+    np.testing.assert_allclose(np.linalg.norm(got, axis=1), 1.0, atol=1e-5)
+    _check_both(got, orc, ids, lens)
+    # the block is not the identity: the same weights without PLE tensors embed differently
+    plain = synth.small_config(qk_gain_scale=0.25, **{k: v for k, v in kw.items() if k != "ple_dim"})
+    ppath = synth.ensure_gguf(os.path.join(str(gguf_dir), f"nople_{plain.hidden}.gguf"), plain)
+    with GlyprEmbedder.load_gguf(ppath, [0]) as emb:
+        base = emb.embed_tokens(ids, lens)
+    assert cosine_rows(got, base).max() < 0.999

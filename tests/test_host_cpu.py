@@ -83,10 +83,32 @@ def test_open_missing_tensor(tmp_path, tiny_cfg):
     assert rc == api.GLP_ERR_FORMAT and "blk.0.ffn_up.weight" in msg
 
 
-def test_open_rejects_ple(tmp_path, tiny_cfg):
+def test_open_ple_block_without_projection(tmp_path, tiny_cfg):
+    """A layer's PLE block without the model-level projection (model.rs:257-275 loads both)."""
     p = synth.write_gguf(str(tmp_path / "ple.gguf"), tiny_cfg, extra_f32=[("blk.0.proj.weight", (768, 256))])
     rc, msg = _open(p)
-    assert rc == api.GLP_ERR_UNSUPPORTED and "PLE" in msg
+    assert rc == api.GLP_ERR_FORMAT and msg == "missing tensor per_layer_model_proj.weight"
+
+
+@pytest.mark.parametrize("drop,want", [
+    ("blk.0.layer_output_scale.weight", "missing tensor blk.0.layer_output_scale.weight"),
+    ("blk.0.inp_gate.weight", "missing tensor blk.0.inp_gate.weight"),
+    ("per_layer_proj_norm.weight", "missing tensor per_layer_proj_norm.weight"),
+])
+def test_open_ple_missing_tensor(tmp_path, drop, want):
+    cfg = synth.small_config(n_layers=1, vocab=256, ple_dim=256)
+    p = synth.write_gguf(str(tmp_path / "ple.gguf"), cfg, drop={drop})
+    rc, msg = _open(p)
+    assert rc == api.GLP_ERR_FORMAT and msg == want
+
+
+def test_open_ple_width(tmp_path):
+    cfg = synth.small_config(n_layers=1, vocab=256, ple_dim=96)
+    rc, msg = _open(synth.write_gguf(str(tmp_path / "p96.gguf"), cfg))
+    assert rc == api.GLP_ERR_UNSUPPORTED and "per_layer_input" in msg
+    cfg = synth.small_config(n_layers=2, vocab=256, ple_dim=256)
+    rc, msg = _open(synth.write_gguf(str(tmp_path / "p256.gguf"), cfg))
+    assert rc not in (api.GLP_ERR_UNSUPPORTED, api.GLP_ERR_FORMAT), msg
 
 
 def test_open_rejects_f32_linear(tmp_path, tiny_cfg):

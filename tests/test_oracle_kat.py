@@ -200,3 +200,43 @@ def test_golden_vectors_reproduce(gguf_dir):
             want = data[mode_name]
             # same restatement, same seed: reproducible to f32 round-off of the thread split
             assert np.abs(got - want).max() <= 1e-5, (case["name"], mode_name)
+
+
+# ------------------------------------------------------------------ ple.rs:48-145, layer.rs:44-49
+def _tensor(cfg, name):
+    """The synthetic writer's tensor `name` of `cfg`: Q8_0 blocks [n, k/32] or an f32 gain."""
+    order = synth._tensor_order(cfg)
+    idx = [n for n, _, _ in order].index(name)
+    shape, kind = order[idx][1], order[idx][2]
+    _, raw, logical = synth.generate_tensor(cfg, synth.MASTER_SEED, idx, shape, kind)
+    if logical is not None:
+        return logical
+    return np.frombuffer(raw, dtype=synth.Q8_0_DTYPE).reshape(shape[0], shape[1] // 32)
+
+
+@pytest.mark.parametrize("mode", [oracle.M1_CANDLE, oracle.M2_EXACT])
+def test_ple_block_restated(gguf_dir, mode):
+    """The oracle's per-layer-embedding path against a composition of the pinned primitives:
+    a one-layer model with PLE tensors equals the same model without them (identical other
+    tensors) followed by P = RMSNorm(proj(x0) * H^-0.5) * w (ple.rs:48-93) and
+    h = (h + RMSNorm(proj(geglu(gate(h), P))) * w) * s (ple.rs:118-145, norm.rs:65-94)."""
+    base = dict(n_layers=1, hidden=512, n_heads=2, n_kv_heads=1, ffn=1024, head_dims=(512,), vocab=512,
+                qk_gain_scale=0.25)
+    cfg_a = synth.small_config(**base)
+    cfg_b = synth.small_config(ple_dim=256, **base)
+    pa = synth.ensure_gguf(os.path.join(str(gguf_dir), "ple_off.gguf"), cfg_a)
+    pb = synth.ensure_gguf(os.path.join(str(gguf_dir), "ple_on.gguf"), cfg_b)
+    ids = np.random.default_rng(5).integers(2, 512, size=37).astype(np.int32)
+    h2 = oracle.OracleModel(pa).hidden_after(ids, 0, mode)
+    got = oracle.OracleModel(pb).hidden_after(ids, 0, mode)
+    H, D = 512, 256
+    x0 = synth.dequantize_q8_0(_tensor(cfg_b, "token_embd.weight")[ids]) * np.float32(np.sqrt(H))
+    p = oracle.q8_0_matmul(_tensor(cfg_b, "per_layer_model_proj.weight"), D, H, x0, mode)
+    p = oracle.rmsnorm(p * np.float32(H ** -0.5), _tensor(cfg_b, "per_layer_proj_norm.weight"))
+    g = oracle.q8_0_matmul(_tensor(cfg_b, "blk.0.inp_gate.weight"), D, H, h2, mode)
+    y = oracle.q8_0_matmul(_tensor(cfg_b, "blk.0.proj.weight"), H, D, oracle.geglu(g, p), mode)
+    y = oracle.rmsnorm(y, _tensor(cfg_b, "blk.0.post_norm.weight"))
+    s = _tensor(cfg_b, "blk.0.layer_output_scale.weight")[0]
+    want = (h2 + y) * s
+    assert s != 1.0 and np.abs(y).max() > 0.1
+    np.testing.assert_allclose(got, want, rtol=1e-5, atol=1e-5)
