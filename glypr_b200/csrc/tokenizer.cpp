@@ -695,23 +695,35 @@ int glp_task_format(const char* task, const char* title, const char* text, size_
   return write_string(s, out, cap, n_out);
 }
 
-int glp_embed_texts(glp_ctx* ctx, const glp_tokenizer* tok, const char* const* texts, const size_t* text_lens,
-                    int n_texts, int form, int max_seq_len, int out_dim, float* out) {
-  if (!ctx || !tok || n_texts <= 0 || !texts || !text_lens || !out || form < GLP_TOKENS_BARE ||
-      form > GLP_TOKENS_SEQUENCE || max_seq_len < 0)
-    return fail(GLP_ERR_INVALID_ARG, "bad glp_embed_texts arguments");
-  size_t cap = 2 * static_cast<size_t>(n_texts);
-  for (int i = 0; i < n_texts; ++i) cap += 3 * text_lens[i];  // a space may take 3 byte tokens
-  std::vector<int32_t> packed(std::max<size_t>(cap, 1));
-  std::vector<int64_t> off(n_texts + 1);
-  int rc = glp_tokenize_batch(tok, texts, text_lens, n_texts, form, 0, 0, packed.data(), cap, off.data());
-  if (rc != GLP_OK) return rc;
-  // the preflight check of the reference path the form stands for
-  const int64_t limit = max_seq_len > 0 ? max_seq_len : GLP_DEFAULT_MAX_SEQ_LEN;
-  int64_t width = 1;
-  for (int i = 0; i < n_texts; ++i) {
-    const int64_t len = off[i + 1] - off[i];
-    width = std::max(width, len);
+}  // extern "C"
+
+namespace {
+
+// One slice [lo, hi) of glp_embed_texts' batch, tokenised into packed ids + offsets.
+struct TextPart {
+  int lo = 0, hi = 0;
+  std::vector<int32_t> packed;
+  std::vector<int64_t> off;
+  int rc = GLP_OK;
+  std::string err;  // glp_last_error() of the thread that tokenised the part
+};
+
+void tokenize_part(const glp_tokenizer* tok, const char* const* texts, const size_t* text_lens, int form,
+                   TextPart* P) {
+  size_t cap = 2 * static_cast<size_t>(P->hi - P->lo);
+  for (int i = P->lo; i < P->hi; ++i) cap += 3 * text_lens[i];  // a space may take 3 byte tokens
+  P->packed.assign(std::max<size_t>(cap, 1), 0);
+  P->off.assign(static_cast<size_t>(P->hi - P->lo) + 1, 0);
+  P->rc = glp_tokenize_batch(tok, texts + P->lo, text_lens + P->lo, P->hi - P->lo, form, 0, 0, P->packed.data(),
+                             cap, P->off.data());
+  if (P->rc != GLP_OK) P->err = glp_last_error();
+}
+
+// The preflight length check of the reference path the form stands for, over one part (item
+// indices are the batch's).
+int preflight_part(const TextPart& P, int n_texts, int form, int64_t limit) {
+  for (int i = P.lo; i < P.hi; ++i) {
+    const int64_t len = P.off[i - P.lo + 1] - P.off[i - P.lo];
     if (len <= limit) continue;
     const std::string n = std::to_string(len), l = std::to_string(limit);
     std::string msg;
@@ -727,12 +739,100 @@ int glp_embed_texts(glp_ctx* ctx, const glp_tokenizer* tok, const char* const* t
             l + " tokens)";
     return fail(GLP_ERR_CONTEXT_LIMIT, msg);
   }
-  std::vector<int32_t> ids(static_cast<size_t>(n_texts) * width, kTokenPad), lengths(n_texts);
-  for (int i = 0; i < n_texts; ++i) {
-    lengths[i] = static_cast<int32_t>(off[i + 1] - off[i]);
-    std::copy(packed.begin() + off[i], packed.begin() + off[i + 1], ids.begin() + static_cast<size_t>(i) * width);
+  return GLP_OK;
+}
+
+int embed_part(glp_ctx* ctx, const TextPart& P, int out_dim, int row_dim, float* out) {
+  const int n = P.hi - P.lo;
+  int64_t width = 1;
+  for (int i = 0; i < n; ++i) width = std::max(width, P.off[i + 1] - P.off[i]);
+  std::vector<int32_t> ids(static_cast<size_t>(n) * width, kTokenPad), lengths(n);
+  for (int i = 0; i < n; ++i) {
+    lengths[i] = static_cast<int32_t>(P.off[i + 1] - P.off[i]);
+    std::copy(P.packed.begin() + P.off[i], P.packed.begin() + P.off[i + 1], ids.begin() + static_cast<size_t>(i) * width);
   }
-  return glp_embed_tokens(ctx, ids.data(), lengths.data(), n_texts, static_cast<int>(width), out_dim, out, nullptr);
+  return glp_embed_tokens(ctx, ids.data(), lengths.data(), n, static_cast<int>(width), out_dim,
+                          out + static_cast<size_t>(P.lo) * row_dim, nullptr);
+}
+
+}  // namespace
+
+extern "C" {
+
+// Texts -> embeddings: tokenise (all host threads), run the reference's preflight length
+// check, embed.  A large batch is cut into up to four parts of about 64 k estimated ids, and
+// the next part is tokenised on a helper thread while the current one is embedded: a
+// sequence's embedding does not depend on the batch it is in, so the output is the same.
+// Errors keep the unsplit order -- every tokenisation error before every preflight error
+// before an embedding error, each the first in batch order: when a part fails, the later
+// parts are tokenised and checked before its error is returned.  Parts are used only where
+// glp_embed_tokens cannot fail on ids or out_dim (valid out_dim, every token id inside the
+// model's vocabulary).
+int glp_embed_texts(glp_ctx* ctx, const glp_tokenizer* tok, const char* const* texts, const size_t* text_lens,
+                    int n_texts, int form, int max_seq_len, int out_dim, float* out) {
+  if (!ctx || !tok || n_texts <= 0 || !texts || !text_lens || !out || form < GLP_TOKENS_BARE ||
+      form > GLP_TOKENS_SEQUENCE || max_seq_len < 0)
+    return fail(GLP_ERR_INVALID_ARG, "bad glp_embed_texts arguments");
+  const int64_t limit = max_seq_len > 0 ? max_seq_len : GLP_DEFAULT_MAX_SEQ_LEN;
+  glp_model_info_t info{};
+  int rc = glp_model_info(ctx, &info);
+  if (rc != GLP_OK) return rc;
+  int n_tok = 0;
+  rc = glp_tokenizer_info(tok, &n_tok, nullptr);
+  if (rc != GLP_OK) return rc;
+  size_t bytes = 0;
+  for (int i = 0; i < n_texts; ++i) bytes += text_lens[i];
+  constexpr size_t kPartBytes = 3 * 65536;  // about 64 k ids at 3 bytes per id
+  int parts = static_cast<int>(std::min<size_t>(4, bytes / kPartBytes));
+  const bool splittable = out_dim >= 0 && out_dim <= info.embedding_dim && n_tok <= info.vocab;
+  if (!splittable || parts < 2 || n_texts < 2 * parts) parts = 1;
+  if (parts > 1) {
+    // glp_tokenize_batch's argument errors, with the batch's item indices
+    for (int i = 0; i < n_texts; ++i) {
+      if (text_lens[i] && !texts[i]) return fail(GLP_ERR_INVALID_ARG, "text " + std::to_string(i) + " is NULL");
+      if (!utf8_valid(texts[i], text_lens[i]))
+        return fail(GLP_ERR_INVALID_ARG, "text " + std::to_string(i) + " is not valid UTF-8");
+    }
+  }
+  const int row_dim = out_dim > 0 ? out_dim : info.embedding_dim;
+  std::vector<TextPart> ps(parts);
+  for (int p = 0; p < parts; ++p) {
+    ps[p].lo = static_cast<int>(static_cast<int64_t>(n_texts) * p / parts);
+    ps[p].hi = static_cast<int>(static_cast<int64_t>(n_texts) * (p + 1) / parts);
+  }
+  auto over_positions = [&](const TextPart& P) {  // glp_embed_tokens' max_position_embeddings check
+    for (size_t i = 0; i + 1 < P.off.size(); ++i)
+      if (P.off[i + 1] - P.off[i] > info.max_position) return true;
+    return false;
+  };
+  tokenize_part(tok, texts, text_lens, form, &ps[0]);
+  for (int p = 0; p < parts; ++p) {
+    std::thread next;
+    if (p + 1 < parts) next = std::thread(tokenize_part, tok, texts, text_lens, form, &ps[p + 1]);
+    if (ps[p].rc != GLP_OK) {  // the batch's first tokenisation error
+      if (next.joinable()) next.join();
+      return fail(ps[p].rc, ps[p].err);
+    }
+    rc = preflight_part(ps[p], n_texts, form, limit);
+    const bool embed_fails = rc == GLP_OK && over_positions(ps[p]);
+    if (rc != GLP_OK || embed_fails) {
+      // an earlier error class may still come from a later part
+      const std::string own = glp_last_error();
+      if (next.joinable()) next.join();
+      for (int q = p + 2; q < parts; ++q) tokenize_part(tok, texts, text_lens, form, &ps[q]);
+      for (int q = p + 1; q < parts; ++q)
+        if (ps[q].rc != GLP_OK) return fail(ps[q].rc, ps[q].err);
+      if (rc != GLP_OK) return fail(rc, own);
+      for (int q = p + 1; q < parts; ++q) {
+        rc = preflight_part(ps[q], n_texts, form, limit);
+        if (rc != GLP_OK) return rc;
+      }
+    }
+    rc = embed_part(ctx, ps[p], out_dim, row_dim, out);
+    if (next.joinable()) next.join();
+    if (rc != GLP_OK) return rc;
+  }
+  return GLP_OK;
 }
 
 }  // extern "C"

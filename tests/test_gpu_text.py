@@ -97,3 +97,64 @@ def test_engine_text_requests(text_model):
             np.testing.assert_array_equal(g, w)
         full = _by_ids(emb, [ref.encode(R.task_format("document", "Doc A", "ka lo"), R.FORM_SEQUENCE)])[0]
         np.testing.assert_allclose(got[-1], api.truncate_mrl(full, 256), atol=1e-6)
+
+
+def _long_texts(n, words):
+    rng = np.random.default_rng(11)
+    base = [c["text"] for c in TRAINED["cases"] if 20 < len(c["text"]) < 400]
+    return [" ".join(base[j] for j in rng.integers(0, len(base), size=words)) for _ in range(n)]
+
+
+def test_embed_texts_in_parts_equal_one_batch(text_model):
+    """A batch of ~0.6 MB of text is tokenised in parts, each overlapping the previous part's
+    embedding; the result equals one token batch of the same ids."""
+    path, _ = text_model
+    texts = _long_texts(64, 60)
+    assert sum(len(t.encode()) for t in texts) > 3 * 3 * 65536  # three parts or more
+    with GlyprEmbedder.load_gguf(path, [0]) as emb, Tokenizer.from_gguf(path) as tok:
+        got = emb.embed_texts(tok, texts, api.GLP_TOKENS_SEQUENCE)
+        rows = tok.encode_batch(texts, api.GLP_TOKENS_SEQUENCE)
+        width = max(len(r) for r in rows)
+        ids = np.zeros((len(rows), width), np.int32)
+        for i, r in enumerate(rows):
+            ids[i, :len(r)] = r
+        want = emb.embed_tokens(ids, np.array([len(r) for r in rows], np.int32))
+        np.testing.assert_array_equal(got, want)
+        got128 = emb.embed_texts(tok, texts[:40], api.GLP_TOKENS_SINGLE, truncate_dim=128)
+        np.testing.assert_allclose(got128, np.stack([api.truncate_mrl(w, 128) for w in
+                                                     emb.embed_texts(tok, texts[:40], api.GLP_TOKENS_SINGLE)]),
+                                   atol=2e-6)
+
+
+def test_embed_texts_in_parts_first_error(text_model):
+    """Errors of a split batch are the unsplit ones: the first over-limit item in batch order,
+    and a later part's preflight error before an earlier part's max-position failure."""
+    path, _ = text_model
+    texts = _long_texts(64, 60)
+    with GlyprEmbedder.load_gguf(path, [0]) as emb, Tokenizer.from_gguf(path) as tok:
+        n = [len(r) for r in tok.encode_batch(texts, api.GLP_TOKENS_SEQUENCE)]
+        lim = sorted(n)[-3] - 1  # exactly three items exceed it
+        first = min(i for i in range(64) if n[i] > lim)
+        with pytest.raises(GlyprError) as e:
+            emb.embed_texts(tok, texts, api.GLP_TOKENS_SEQUENCE, max_seq_len=lim)
+        assert e.value.code == api.GLP_ERR_CONTEXT_LIMIT
+        assert e.value.message == f"Batch item {first} sequence length ({n[first]}) exceeds maximum context limit ({lim})"
+        # item 2 is longer than the model's 8192 positions but within the default limit 8320;
+        # item 50 is beyond the limit: the reference's preflight reports item 50
+        unit = "the station "
+        per = len(tok.encode(unit * 101, api.GLP_TOKENS_BARE)) - len(tok.encode(unit * 100, api.GLP_TOKENS_BARE))
+        k = (8240 - 2) // per
+        mid = unit * k
+        m = len(tok.encode(mid, api.GLP_TOKENS_SEQUENCE))
+        assert emb.info.max_position < m <= 8320, m
+        bad = list(texts)
+        bad[2] = mid
+        bad[50] = unit * (9000 // per)
+        nb = len(tok.encode(bad[50], api.GLP_TOKENS_SEQUENCE))
+        with pytest.raises(GlyprError) as e:
+            emb.embed_texts(tok, bad, api.GLP_TOKENS_SEQUENCE)
+        assert e.value.message == f"Batch item 50 sequence length ({nb}) exceeds maximum context limit (8320)"
+        bad[50] = texts[50]
+        with pytest.raises(GlyprError) as e:
+            emb.embed_texts(tok, bad, api.GLP_TOKENS_SEQUENCE)
+        assert e.value.code == api.GLP_ERR_CONTEXT_LIMIT and "max_position_embeddings" in e.value.message
