@@ -363,6 +363,7 @@ struct Config {
   int emb_out = 768, max_pos = 262144, window = 512;
   double eps = 1e-6, theta_swa = 1e4, theta_full = 1e6;
   std::vector<bool> sliding;
+  std::vector<int> kv;  // KV heads per layer (config.rs:141-160: head_count_kv[i], global layers may differ)
   uint32_t linear_type = glp::kGgmlQ8_0;
   int ple_dim = 0;  // per-layer-embedding width D; 0 = no PLE tensors (model.rs:257-275)
 };
@@ -403,13 +404,16 @@ int parse_config(const glp::GgufFile& g, Config* c) {
   }
   const glp::GgufValue* kv = g.find(a + "attention.head_count_kv");
   c->n_kv = kv && kv->type == 9 && !kv->arr.empty() ? static_cast<int>(kv->arr[0]) : 2;
+  c->kv.assign(c->n_layers, c->n_kv);
   for (int i = 0; i < c->n_layers; ++i) {
     int kvi = c->n_kv;
     if (!c->sliding[i]) kvi = kv && kv->type == 9 && i < static_cast<int>(kv->arr.size()) ? static_cast<int>(kv->arr[i]) : 1;
     const int hd = c->sliding[i] ? static_cast<int>(hd_swa) : static_cast<int>(hd_full);
-    if (kvi != c->n_kv || hd != static_cast<int>(hd_swa))
-      return fail(GLP_ERR_UNSUPPORTED,
-                  "per-layer head_dim / kv-head overrides are not supported (all layers must share head_dim and kv heads)");
+    if (hd != static_cast<int>(hd_swa))
+      return fail(GLP_ERR_UNSUPPORTED, "per-layer head_dim overrides are not supported (all layers must share head_dim)");
+    if (kvi <= 0 || c->n_heads % kvi)
+      return fail(GLP_ERR_FORMAT, "head_count must be a multiple of head_count_kv");
+    c->kv[i] = kvi;
   }
   c->head_dim = static_cast<int>(hd_swa);
   if (c->hidden <= 0 || c->hidden % 256 || c->hidden > glp::kMaxHidden)
@@ -471,8 +475,8 @@ int validate_tensors(const glp::GgufFile& g, const Config& c) {
     GLP_TRY(need(p + "ffn_norm.weight", {H}, false));
     GLP_TRY(need(p + "post_ffw_norm.weight", {H}, false));
     GLP_TRY(need(p + "attn_q.weight", {H, c.n_heads * D}, true));
-    GLP_TRY(need(p + "attn_k.weight", {H, c.n_kv * D}, true));
-    GLP_TRY(need(p + "attn_v.weight", {H, c.n_kv * D}, true));
+    GLP_TRY(need(p + "attn_k.weight", {H, c.kv[l] * D}, true));
+    GLP_TRY(need(p + "attn_v.weight", {H, c.kv[l] * D}, true));
     GLP_TRY(need(p + "attn_output.weight", {c.n_heads * D, H}, true));
     GLP_TRY(need(p + "ffn_gate.weight", {H, F}, true));
     GLP_TRY(need(p + "ffn_up.weight", {H, F}, true));
@@ -509,6 +513,7 @@ struct LayerW {
         *post_ffw = nullptr;
   float layer_scalar = 1.0f;
   bool sliding = true;
+  int kv = 1, qkv_w = 0;  // KV heads and q|k|v width of this layer
   CUtensorMap m_qkv, m_o, m_gu, m_down;
   CUtensorMap p_qkv, p_o, p_gu, p_down;  // the same weights, 128-row boxes for CTA pairs
   // per-layer-embedding block (ple.rs:96-145): gate [D, H], projection [H, D], post-norm
@@ -770,7 +775,9 @@ int setup_device(Device& d, const Config& c, const glp::GgufFile& g, int64_t cap
   GLP_CUDA(cudaEventCreate(&d.ev0));
   GLP_CUDA(cudaEventCreate(&d.ev1));
   const int H = c.hidden, F = c.ffn, D = c.head_dim;
-  const int QKV = (c.n_heads + 2 * c.n_kv) * D, AW = c.n_heads * D;
+  const int AW = c.n_heads * D;
+  int QKV = 0;  // the widest layer's q|k|v width (the activation buffer)
+  for (int l = 0; l < c.n_layers; ++l) QKV = std::max(QKV, (c.n_heads + 2 * c.kv[l]) * D);
 
   // token table: kept as raw Q8_0 (or bf16) rows, gathered per token
   const glp::GgufTensor* te = g.tensor("token_embd.weight");
@@ -825,23 +832,25 @@ int setup_device(Device& d, const Config& c, const glp::GgufFile& g, int64_t cap
       if (s->type != glp::kGgmlF32 || s->numel() != 1) return fail(GLP_ERR_FORMAT, "bad layer_output_scale");
       std::memcpy(&L.layer_scalar, s->data, 4);
     }
-    GLP_TRY(d.alloc(&L.qkv, static_cast<size_t>(QKV) * H));
+    L.kv = c.kv[l];
+    L.qkv_w = (c.n_heads + 2 * L.kv) * D;
+    GLP_TRY(d.alloc(&L.qkv, static_cast<size_t>(L.qkv_w) * H));
     GLP_TRY(d.alloc(&L.o, static_cast<size_t>(H) * AW));
     GLP_TRY(d.alloc(&L.gu, static_cast<size_t>(2 * F) * H));
     GLP_TRY(d.alloc(&L.down, static_cast<size_t>(H) * F));
     GLP_TRY(upload_linear(d, g, p + "attn_q.weight", c.n_heads * D, H, L.qkv, 0, 0, 0, staging, staging_bytes));
-    GLP_TRY(upload_linear(d, g, p + "attn_k.weight", c.n_kv * D, H, L.qkv, c.n_heads * D, 0, 0, staging, staging_bytes));
-    GLP_TRY(upload_linear(d, g, p + "attn_v.weight", c.n_kv * D, H, L.qkv, (c.n_heads + c.n_kv) * D, 0, 0, staging,
+    GLP_TRY(upload_linear(d, g, p + "attn_k.weight", L.kv * D, H, L.qkv, c.n_heads * D, 0, 0, staging, staging_bytes));
+    GLP_TRY(upload_linear(d, g, p + "attn_v.weight", L.kv * D, H, L.qkv, (c.n_heads + L.kv) * D, 0, 0, staging,
                           staging_bytes));
     GLP_TRY(upload_linear(d, g, p + "attn_output.weight", H, AW, L.o, 0, 0, 0, staging, staging_bytes));
     GLP_TRY(upload_linear(d, g, p + "ffn_gate.weight", F, H, L.gu, 0, 128, 256, staging, staging_bytes));
     GLP_TRY(upload_linear(d, g, p + "ffn_up.weight", F, H, L.gu, 128, 128, 256, staging, staging_bytes));
     GLP_TRY(upload_linear(d, g, p + "ffn_down.weight", H, F, L.down, 0, 0, 0, staging, staging_bytes));
-    GLP_TRY(make_map16(&L.m_qkv, L.qkv, QKV, H, H, 256, true));
+    GLP_TRY(make_map16(&L.m_qkv, L.qkv, L.qkv_w, H, H, 256, true));
     GLP_TRY(make_map16(&L.m_o, L.o, H, AW, AW, bn_for(H), true));
     GLP_TRY(make_map16(&L.m_gu, L.gu, 2 * F, H, H, 256, true));
     GLP_TRY(make_map16(&L.m_down, L.down, H, F, F, bn_for(H), true));
-    GLP_TRY(make_map16(&L.p_qkv, L.qkv, QKV, H, H, 128, true));
+    GLP_TRY(make_map16(&L.p_qkv, L.qkv, L.qkv_w, H, H, 128, true));
     GLP_TRY(make_map16(&L.p_o, L.o, H, AW, AW, 128, true));
     GLP_TRY(make_map16(&L.p_gu, L.gu, 2 * F, H, H, 128, true));
     GLP_TRY(make_map16(&L.p_down, L.down, H, F, F, 128, true));
@@ -937,7 +946,7 @@ int setup_device(Device& d, const Config& c, const glp::GgufFile& g, int64_t cap
 int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_cu_chunk, const int* h_cu_chunk,
               int base, int n_seq, int T, int max_len, int out_dim, float* d_out, cudaStream_t st) {
   const int H = c.hidden, F = c.ffn, D = c.head_dim;
-  const int QKV = (c.n_heads + 2 * c.n_kv) * D, AW = c.n_heads * D;
+  const int QKV = d.layers.empty() ? 0 : d.layers[0].qkv_w, AW = c.n_heads * D;  // layer 0's q|k|v width
   const float eps = static_cast<float>(c.eps);
   const double Td = T;
   auto gemm_flops = [&](double m, double n, double k) { return 2.0 * m * n * k; };
@@ -997,6 +1006,8 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
       }));
     }
     GLP_TRY(make_map16(&m_qkv_out, d.qkv, T, QKV, QKV, 32, true));  // the QKV epilogue's bulk stores
+    CUtensorMap m_qkv_out2;  // the same for layers of another KV-head count (re-encoded when that width changes)
+    int qkv_w2 = 0;
     GLP_TRY(make_map16(&m_attn, d.attn, T, AW, AW, 128, true));
     GLP_TRY(make_map16(&m_a, d.a, T, F, F, 128, true));
     double pairs_local = 0, pairs_global = 0;
@@ -1005,7 +1016,7 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
       pairs_local += visible_pairs(len, c.window);
       pairs_global += visible_pairs(len, 0);
     }
-    const double attn_bytes = 2.0 * Td * QKV + 2.0 * Td * AW;
+
     const double post_bytes = Td * (2.0 * H + 4.0 * H + 2.0 * H);  // y + h in/out + x (16-bit)
     const double fused_bytes = Td * (4.0 * H + 2.0 * H);              // h in/out + x, no y
     // the row-norm GEMM needs 768-wide rows (three CTA pairs per cluster) and the CTA-pair weight
@@ -1021,23 +1032,33 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
       p.K = H;
       p.status = d.status;
       // QKV projection + per-head RMSNorm + RoPE -> f16 qkv
-      p.N = QKV;
+      const int W = L.qkv_w;
+      const CUtensorMap* m_out = &m_qkv_out;
+      if (W != QKV) {
+        if (W != qkv_w2) {
+          GLP_TRY(make_map16(&m_qkv_out2, d.qkv, T, W, W, 32, true));
+          qkv_w2 = W;
+        }
+        m_out = &m_qkv_out2;
+      }
+      p.N = W;
       p.C = d.qkv;
-      p.ldc = QKV;
+      p.ldc = W;
       p.q_gain = L.q_norm;
       p.k_gain = L.k_norm;
       p.rope_cs = L.sliding ? d.cs_swa : d.cs_full;
       p.pos = d.pos;
       p.rope_stride = c.max_pos;
       p.n_q_heads = c.n_heads;
-      p.n_kv_heads = c.n_kv;
+      p.n_kv_heads = L.kv;
       p.eps = eps;
-      GLP_TRY(prof_launch(d, st, kProfGemmQkv, gemm_flops(Td, QKV, H), gemm_bytes(Td, QKV, H, 2.0),
-                          [&] { return launch_gemm<__half>(m_x, L.m_qkv, 256, glp::kEpiQkv, p, st, &L.p_qkv, &m_qkv_out); }));
+      GLP_TRY(prof_launch(d, st, kProfGemmQkv, gemm_flops(Td, W, H), gemm_bytes(Td, W, H, 2.0),
+                          [&] { return launch_gemm<__half>(m_x, L.m_qkv, 256, glp::kEpiQkv, p, st, &L.p_qkv, m_out); }));
       // attention
       const double pairs = L.sliding ? pairs_local : pairs_global;
+      const double attn_bytes = 2.0 * Td * W + 2.0 * Td * AW;
       GLP_TRY(prof_launch(d, st, kProfAttention, 4.0 * D * c.n_heads * pairs, attn_bytes, [&] {
-        return launch_attention(d.qkv, T, QKV, d_cu_chunk, base, n_seq, max_len, c.n_heads, c.n_kv,
+        return launch_attention(d.qkv, T, W, d_cu_chunk, base, n_seq, max_len, c.n_heads, L.kv,
                                 L.sliding ? c.window : 0, d.attn, d.status, st);
       }));
       // O projection

@@ -93,6 +93,11 @@ class EncoderConfig:
     qk_gain_scale: float = 1.0
     # per-layer-embedding width D (0 = no PLE tensors)
     ple_dim: int = 0
+    # KV heads of the global layers (0 = n_kv_heads, as on the sliding layers)
+    global_kv_heads: int = 0
+
+    def kv_heads(self, i: int) -> int:
+        return self.n_kv_heads if self.layer_is_sliding(i) or not self.global_kv_heads else self.global_kv_heads
 
     @property
     def embedding_out(self) -> int:
@@ -205,8 +210,8 @@ def _tensor_order(cfg: EncoderConfig) -> List[Tuple[str, Tuple[int, ...], str]]:
         order += [
             (p + "attn_norm.weight", (h,), "gain"),
             (p + "attn_q.weight", (cfg.n_heads * d, h), "mat"),
-            (p + "attn_k.weight", (cfg.n_kv_heads * d, h), "mat"),
-            (p + "attn_v.weight", (cfg.n_kv_heads * d, h), "mat"),
+            (p + "attn_k.weight", (cfg.kv_heads(i) * d, h), "mat"),
+            (p + "attn_v.weight", (cfg.kv_heads(i) * d, h), "mat"),
             (p + "attn_output.weight", (h, cfg.n_heads * d), "mat"),
             (p + "attn_q_norm.weight", (d,), "qkgain"),
             (p + "attn_k_norm.weight", (d,), "qkgain"),
@@ -275,7 +280,7 @@ def metadata(cfg: EncoderConfig, tokenizer: Optional[Tuple[Sequence[str], Sequen
         _kv(a + "embedding_length", _U32, cfg.hidden),
         _kv(a + "feed_forward_length", _U32, cfg.ffn),
         _kv(a + "attention.head_count", _U32, cfg.n_heads),
-        _kv(a + "attention.head_count_kv", _ARR, (_U32, [cfg.n_kv_heads] * cfg.n_layers)),
+        _kv(a + "attention.head_count_kv", _ARR, (_U32, [cfg.kv_heads(i) for i in range(cfg.n_layers)])),
         _kv(a + "attention.key_length_swa", _U32, cfg.head_dim),
         _kv(a + "attention.key_length", _U32, cfg.head_dim),
         _kv(a + "embedding_length_out", _U32, cfg.embedding_out),

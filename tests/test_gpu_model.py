@@ -201,9 +201,10 @@ def test_other_hidden_sizes(gguf_dir, hidden, n_heads, n_kv, ffn, head_dims, wei
 
 
 @pytest.mark.parametrize("kw", [
-    # EmbeddingGemma 2 widths (hidden 512, FFN 2048, 4 query heads over 2 KV heads) with
-    # 256-wide per-layer inputs, six layers with the global one
-    dict(n_layers=6, hidden=512, n_heads=4, n_kv_heads=2, ffn=2048, head_dims=(2048, 512), ple_dim=256),
+    # EmbeddingGemma 2 widths (hidden 512, FFN 2048, 4 query heads over 2 KV heads on the sliding
+    # layers and 1 on the global one) with 256-wide per-layer inputs, six layers
+    dict(n_layers=6, hidden=512, n_heads=4, n_kv_heads=2, global_kv_heads=1, ffn=2048, head_dims=(2048, 512),
+         ple_dim=256),
     # BASELINE widths (the fused row-norm O projection) with 512-wide per-layer inputs
     dict(n_layers=2, ple_dim=512),
 ])

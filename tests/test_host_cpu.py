@@ -135,6 +135,16 @@ def test_open_accepts_hidden_multiples_of_256(tmp_path, hidden):
     assert rc not in (api.GLP_ERR_UNSUPPORTED, api.GLP_ERR_FORMAT), msg
 
 
+def test_open_accepts_global_kv_heads(tmp_path):
+    """Global layers with their own KV-head count (head_count_kv[i], config.rs:141-160) load."""
+    cfg = synth.small_config(n_layers=6, vocab=256, n_heads=4, n_kv_heads=2, global_kv_heads=1)
+    rc, msg = _open(synth.write_gguf(str(tmp_path / "kv.gguf"), cfg))
+    assert rc not in (api.GLP_ERR_UNSUPPORTED, api.GLP_ERR_FORMAT), msg
+    cfg = synth.small_config(n_layers=6, vocab=256, n_heads=4, n_kv_heads=2, global_kv_heads=3)
+    rc, msg = _open(synth.write_gguf(str(tmp_path / "kv3.gguf"), cfg))
+    assert rc == api.GLP_ERR_FORMAT and msg == "head_count must be a multiple of head_count_kv"
+
+
 def test_open_rejects_head_dim_override(tmp_path):
     cfg = synth.small_config(n_layers=6, vocab=256)
     p = synth.write_gguf(str(tmp_path / "hd.gguf"), cfg, drop={"gemma-embedding2.attention.key_length"})
