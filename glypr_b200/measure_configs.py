@@ -19,7 +19,11 @@
             BPE vocabulary of tests/golden/tokenizer_golden.json written into the model file;
 * config 4  BF16 weights, one 8192-token sequence (sliding window 512 on local layers, full on
             global): latency, then per-kernel ms / TFLOP/s / GB/s from the library's own CUDA-event
-            profile (a separate pass, so the latency carries no profiling overhead).
+            profile (a separate pass, so the latency carries no profiling overhead);
+* ple       an EmbeddingGemma-2-shaped Q8_0 model (hidden 512, FFN 2048, 4 query heads over 2 KV
+            heads on sliding layers and 1 on global ones, per-layer embeddings of 512, head 512 ->
+            768; head_dim 256 on every layer): 1,024 sequences of 512 tokens, embeddings/s and the
+            per-kernel profile.
 
 All inputs are the seeded synthetic GGUFs of glypr_b200.synth; times are CUDA events on the
 launching stream.  Prints a markdown report (and writes it with --out).
@@ -197,6 +201,40 @@ def config4(torch, path, report):
     report.append("")
 
 
+EMBEDDINGGEMMA2_SHAPE = synth.EncoderConfig(hidden=512, ffn=2048, n_heads=4, n_kv_heads=2, global_kv_heads=1,
+                                            head_dims=(768,), ple_dim=512)
+
+
+def ple_config(torch, path, report, n=1024):
+    with api.GlyprEmbedder.load_gguf(path, [0]) as emb:
+        ids, lens = synth.make_batch(n, 512, emb.info.vocab, seed=synth.MASTER_SEED + 55)
+        d_ids, d_cu, h_cu = packed_inputs(torch, ids, lens)
+        d_out = torch.empty((n, 768), dtype=torch.float32, device="cuda")
+        stream = torch.cuda.current_stream().cuda_stream
+        run = lambda: emb.embed_packed_device(d_ids.data_ptr(), d_cu.data_ptr(), h_cu, n, 768, d_out.data_ptr(),
+                                              stream)
+        ms = timed(torch, run, warm=3, reps=5)
+        emb.profile_enable(True)
+        run()
+        torch.cuda.synchronize()
+        prof = emb.profile_read()
+        emb.profile_enable(False)
+    total = sum(v["ms"] for k, v in prof.items() if not k.startswith("_"))
+    report.append("## Per-layer embeddings — EmbeddingGemma-2-shaped Q8_0 model, 512-token sequences\n")
+    report.append(f"24 layers, hidden 512, FFN 2048, 4 query heads over 2 KV heads (1 on the global layers), "
+                  f"per-layer inputs of 512, head 512 -> 768, head_dim 256 throughout. {n} sequences: "
+                  f"{ms:.1f} ms per batch, {n / ms * 1e3:.0f} embeddings/s (device-resident ids).\n")
+    report.append("Per kernel (one batch, library CUDA-event profile):\n")
+    report.append("| kernel | launches | ms | share | TFLOP/s | GB/s |\n|---|---:|---:|---:|---:|---:|")
+    for name, v in sorted(((k, v) for k, v in prof.items() if not k.startswith("_")), key=lambda kv: -kv[1]["ms"]):
+        if v["launches"] == 0:
+            continue
+        tf = f"{v['flops'] / v['ms'] / 1e9:.0f}" if v["flops"] > 0 else "—"
+        gb = f"{v['bytes'] / v['ms'] / 1e6:.0f}" if v["bytes"] > 0 else "—"
+        report.append(f"| {name} | {v['launches']} | {v['ms']:.3f} | {v['ms'] / total:.3f} | {tf} | {gb} |")
+    report.append("")
+
+
 def serving(emb, report, clients=64, per_client=64, max_batch=512):
     import threading
     ids, lens = synth.make_batch(clients * per_client, 512, emb.info.vocab, seed=synth.MASTER_SEED + 55)
@@ -343,6 +381,9 @@ def main(argv=None) -> None:
         text_path(torch, args.model_dir, report)
     if 2 in want:
         config2(torch, report)
+    if "ple" in want:
+        pl = synth.ensure_gguf(os.path.join(args.model_dir, "embeddinggemma2_shape_q8_0.gguf"), EMBEDDINGGEMMA2_SHAPE)
+        ple_config(torch, pl, report)
     if 4 in want:
         bf = synth.ensure_gguf(os.path.join(args.model_dir, "baseline_bf16.gguf"),
                                synth.EncoderConfig(weight_type="bf16"))
