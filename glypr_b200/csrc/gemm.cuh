@@ -717,20 +717,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
 }
 
 // ---------------------------------------------------------------------------- row-norm GEMM
-// y = A * B^T with N == 768 (three 256-column blocks), fused with the post-norm + residual +
-// next pre-norm that follows the O and down projections (norm.rs:22-94, layer.rs:20-50):
+// y = A * B^T with N == 256 NP (NP 256-column blocks: 512, 768 or 1024 columns), fused with the
+// post-norm + residual + next pre-norm that follows the O and down projections (norm.rs:22-94, layer.rs:20-50):
 //   s  = rsqrt(mean(y^2) + eps),  hv = (h + y * s * w_post) * lambda,  h <- bf16(hv),
 //   x  = f16(hv * rsqrt(mean(hv^2) + eps) * w_next)
 // so y never goes to HBM and the row pass over h happens in the GEMM's shadow.
-// A cluster of 6 CTAs = 3 CTA pairs: pair j computes columns [256 j, 256 j + 256) of a
+// A cluster of 2 NP CTAs = NP CTA pairs: pair j computes columns [256 j, 256 j + 256) of a
 // 256-row tile exactly as gemm_pair_kernel does (cta_group::2, leader = the even rank), so the
-// three CTAs with the same in-pair rank hold the same 128 rows' 768 columns.  Both row scales
+// NP CTAs with the same in-pair rank hold the same 128 rows' N columns.  Both row scales
 // come from one exchange per tile: with u = y * w_post, sum(hv^2) = lambda^2 (sum h^2 +
 // 2 s sum(h u) + s^2 sum u^2), so every CTA sends the four partial sums (y^2, h^2, h u, u^2) of
-// its columns to the other two (st.async into their slots, counted on their exchange
-// mbarrier) and each adds the three in pair order: all three derive bit-identical scales.
+// its columns to the other NP - 1 (st.async into their slots, counted on their exchange
+// mbarrier) and each adds the NP in pair order: all of them derive bit-identical scales.
 // When the expansion cancels for a row (sum hv^2 below 2^-8 of its positive terms, where its
-// rounding would show), that row's quad of 32 rows in the three CTAs -- deciding on identical
+// rounding would show), that row's quad of 32 rows in the NP CTAs -- deciding on identical
 // totals -- takes a second exchange of the directly summed hv^2, which that row then uses
 // (GemmParams::rownorm_direct selects it for every row).
 // The residual rows are fetched by TMA into each epilogue warp's two 4 KB boxes (64 columns
@@ -738,8 +738,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
 // bulk tensor stores (x, then h, rows past M clipped), and each box is refilled with the next
 // tile's rows as soon as the stores have read it, so the loads overlap the rest of the epilogue.  Epilogue warp (quad q, half c) owns rows 32q..32q+31 and the 128
 // columns 128c.. of its CTA's 256; the row arithmetic runs on packed f32x2 pairs.
-struct GemmRowCfg {
-  static constexpr int STAGES = 4;
+template <int NP>
+struct GemmRowCfgT {
+  static constexpr int STAGES = NP <= 3 ? 4 : 3;  // 8-CTA clusters' larger exchange slots take a stage
   static constexpr uint32_t A_BYTES = 128 * 64 * 2;
   static constexpr uint32_t B_BYTES = 128 * 64 * 2;
   static constexpr uint32_t TMEM_COLS = 512;
@@ -749,15 +750,17 @@ struct GemmRowCfg {
   static constexpr uint32_t RED4_OFFSET = BAR_OFFSET + 512;   // float4 [acc buf][half][row]
   static constexpr uint32_t RED1_OFFSET = RED4_OFFSET + 2 * 2 * 128 * 16;  // float [buf][half][row]
   static constexpr uint32_t XV_OFFSET = RED1_OFFSET + 2 * 2 * 128 * 4;     // float4 [buf][pair][row]
-  static constexpr uint32_t XT_OFFSET = XV_OFFSET + 2 * 3 * 128 * 16;      // float [buf][pair][row]
-  static constexpr uint32_t XS_OFFSET = XT_OFFSET + 2 * 3 * 128 * 4;       // float [buf][pair][half][row]
-  static constexpr uint32_t W_OFFSET = XS_OFFSET + 2 * 3 * 2 * 128 * 4;    // float [post | next][256]
+  static constexpr uint32_t XT_OFFSET = XV_OFFSET + 2 * NP * 128 * 16;     // float [buf][pair][row]
+  static constexpr uint32_t XS_OFFSET = XT_OFFSET + 2 * NP * 128 * 4;      // float [buf][pair][half][row]
+  static constexpr uint32_t W_OFFSET = XS_OFFSET + 2 * NP * 2 * 128 * 4;   // float [post | next][256]
   static constexpr size_t SMEM = W_OFFSET + 2 * 256 * 4;
-  // bytes each CTA receives per exchange from the other two: sums (half-0 warps, 16 B a row)
-  // and arrival tokens (half-1 warps, 4 B a row); a quad's direct exchange: 4 B from both of
-  // the quad's warps
-  static constexpr uint32_t XCH_TX = 2 * (128 * 16 + 128 * 4);
-  static constexpr uint32_t XS_TX = 2 * (2 * 32 * 4);
+  // bytes each CTA receives per exchange from the other NP - 1: sums (half-0 warps, 16 B a
+  // row) and arrival tokens (half-1 warps, 4 B a row); a quad's direct exchange: 4 B from both
+  // of the quad's warps
+  static constexpr uint32_t XCH_TX = (NP - 1) * (128 * 16 + 128 * 4);
+  static constexpr uint32_t XS_TX = (NP - 1) * (2 * 32 * 4);
+  static_assert(NP >= 2 && NP <= 4, "clusters of 4, 6 or 8 CTAs");
+  static_assert(SMEM <= 232448, "shared memory per CTA");
 };
 
 __device__ __forceinline__ void st_async_v4(uint32_t cluster_addr, float4 v, uint32_t cluster_mbar) {
@@ -768,13 +771,13 @@ __device__ __forceinline__ void st_async_v4(uint32_t cluster_addr, float4 v, uin
                : "memory");
 }
 
-// p.m_tiles counts 256-row tiles; p.N == 768; p.C is unused (outputs go to p.h and p.x_next).
-template <typename T>
-__global__ void __cluster_dims__(6, 1, 1) __launch_bounds__(kGemmThreads, 1)
+// p.m_tiles counts 256-row tiles; p.N == 256 NP; p.C is unused (outputs go to p.h and p.x_next).
+template <typename T, int NP>
+__global__ void __cluster_dims__(2 * NP, 1, 1) __launch_bounds__(kGemmThreads, 1)
     gemm_rownorm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmH, const __grid_constant__ CUtensorMap tmX,
                         const GemmParams p) {
-  using Cfg = GemmRowCfg;
+  using Cfg = GemmRowCfgT<NP>;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   if (smem_u32(smem_raw) & 1023) {  // the same in every CTA: all leave before any cluster step
@@ -933,7 +936,7 @@ __global__ void __cluster_dims__(6, 1, 1) __launch_bounds__(kGemmThreads, 1)
     const int quad = warp & 3;
     const int half = ew >> 2;
     const int row_in_tile = quad * 32 + lane;
-    const int col0 = pj * 256 + half * 128;  // this warp's first column of the 768
+    const int col0 = pj * 256 + half * 128;  // this warp's first column of the row
     uint8_t* hb = smem + Cfg::HBUF_OFFSET + ew * Cfg::HBUF_WARP;
     float4* red4 = reinterpret_cast<float4*>(smem + Cfg::RED4_OFFSET);
     float* red1 = reinterpret_cast<float*>(smem + Cfg::RED1_OFFSET);
@@ -1022,7 +1025,7 @@ __global__ void __cluster_dims__(6, 1, 1) __launch_bounds__(kGemmThreads, 1)
         hu = t0 + t1;
         f2_split(U2, t0, t1);
         u2 = t0 + t1;
-        // exchange: quad halves -> this CTA's sums -> the other two CTAs of the row triple
+        // exchange: quad halves -> this CTA's sums -> the other NP - 1 CTAs holding these rows
         red4[(ab * 2 + half) * 128 + row_in_tile] = make_float4(y2, h2, hu, u2);
         if (ok) ok = pair_rendezvous(&xbar[quad], xph, abort_flag);
         if (ok) {
@@ -1030,21 +1033,21 @@ __global__ void __cluster_dims__(6, 1, 1) __launch_bounds__(kGemmThreads, 1)
           const float4 mine = make_float4(r0.x + r1.x, r0.y + r1.y, r0.z + r1.z, r0.w + r1.w);
           const uint32_t bar = smem_u32(&xf0[ab]);
 #pragma unroll
-          for (int k = 1; k <= 2; ++k) {
-            const uint32_t dst = static_cast<uint32_t>(((pj + k) % 3) * 2) + prank;
+          for (int k = 1; k < NP; ++k) {
+            const uint32_t dst = static_cast<uint32_t>(((pj + k) % NP) * 2) + prank;
             if (half == 0)
-              st_async_v4(mapa_shared(smem_u32(xv + (ab * 3 + pj) * 128 + row_in_tile), dst), mine,
+              st_async_v4(mapa_shared(smem_u32(xv + (ab * NP + pj) * 128 + row_in_tile), dst), mine,
                           mapa_shared(bar, dst));
             else
-              st_async_b32(mapa_shared(smem_u32(xt + (ab * 3 + pj) * 128 + row_in_tile), dst), 0u,
+              st_async_b32(mapa_shared(smem_u32(xt + (ab * NP + pj) * 128 + row_in_tile), dst), 0u,
                            mapa_shared(bar, dst));
           }
           ok = __all_sync(0xffffffffu, mbar_wait_cluster(&xf0[ab], aph, abort_flag));
           if (ok) {
             float4 tot = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-            for (int j = 0; j < 3; ++j) {
-              const float4 v = j == pj ? mine : xv[(ab * 3 + j) * 128 + row_in_tile];
+            for (int j = 0; j < NP; ++j) {
+              const float4 v = j == pj ? mine : xv[(ab * NP + j) * 128 + row_in_tile];
               tot.x += v.x;
               tot.y += v.y;
               tot.z += v.z;
@@ -1053,11 +1056,11 @@ __global__ void __cluster_dims__(6, 1, 1) __launch_bounds__(kGemmThreads, 1)
             s = 1.0f / sqrtf(tot.x * inv_n + p.eps);
             const float pos = fmaf(s * s, tot.w, tot.y);
             float ss2 = lam * lam * fmaf(s, fmaf(s, tot.w, 2.0f * tot.z), tot.y);
-            // identical totals (and rows) in the three CTAs, so all of them decide alike; each
+            // identical totals (and rows) in the NP CTAs, so all of them decide alike; each
             // row keeps its own choice, so a row's result never depends on its neighbours
             const bool live = mt * 256 + static_cast<int>(prank) * 128 + row_in_tile < p.M;
             const bool direct = live && (p.rownorm_direct || !(ss2 > pos * lam * lam * 0.00390625f));
-            // (the same vote in both warps of the quad and in the three CTAs)
+            // (the same vote in both warps of the quad and in the NP CTAs)
             if (__any_sync(0xffffffffu, direct)) {
               // exact sum of hv^2 for the quad's rows, second exchange on the quad's barrier
               uint64_t* qbar = &xf1[ab * 4 + quad];
@@ -1086,9 +1089,9 @@ __global__ void __cluster_dims__(6, 1, 1) __launch_bounds__(kGemmThreads, 1)
                 const float m1 = red1[(ab * 2) * 128 + row_in_tile] + red1[(ab * 2 + 1) * 128 + row_in_tile];
                 const uint32_t bar1 = smem_u32(qbar);
 #pragma unroll
-                for (int k = 1; k <= 2; ++k) {
-                  const uint32_t dst = static_cast<uint32_t>(((pj + k) % 3) * 2) + prank;
-                  st_async_b32(mapa_shared(smem_u32(xs + ((ab * 3 + pj) * 2 + half) * 128 + row_in_tile), dst),
+                for (int k = 1; k < NP; ++k) {
+                  const uint32_t dst = static_cast<uint32_t>(((pj + k) % NP) * 2) + prank;
+                  st_async_b32(mapa_shared(smem_u32(xs + ((ab * NP + pj) * 2 + half) * 128 + row_in_tile), dst),
                                __float_as_uint(m1), mapa_shared(bar1, dst));
                 }
                 const uint32_t par = (xf1ph >> (ab * 4 + quad)) & 1u;
@@ -1098,7 +1101,7 @@ __global__ void __cluster_dims__(6, 1, 1) __launch_bounds__(kGemmThreads, 1)
                   direct_armed = false;
                   float sd = 0.f;
 #pragma unroll
-                  for (int j = 0; j < 3; ++j) sd += j == pj ? m1 : xs[((ab * 3 + j) * 2) * 128 + row_in_tile];
+                  for (int j = 0; j < NP; ++j) sd += j == pj ? m1 : xs[((ab * NP + j) * 2) * 128 + row_in_tile];
                   if (direct) ss2 = sd;
                 }
               }

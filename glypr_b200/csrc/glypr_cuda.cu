@@ -170,7 +170,9 @@ int ensure_kernel_attrs() {
   GLP_CUDA(cudaFuncSetAttribute(glp::gemm_pair_kernel<glp::kEpiGeglu, __half>, A, sp));
   GLP_CUDA(cudaFuncSetAttribute(glp::gemm_pair_kernel<glp::kEpiStore16, __nv_bfloat16>, A, sp));
   GLP_CUDA(cudaFuncSetAttribute(glp::gemm_pair_kernel<glp::kEpiF32, __nv_bfloat16>, A, sp));
-  GLP_CUDA(cudaFuncSetAttribute(glp::gemm_rownorm_kernel<__half>, A, static_cast<int>(glp::GemmRowCfg::SMEM)));
+  GLP_CUDA(cudaFuncSetAttribute(glp::gemm_rownorm_kernel<__half, 2>, A, static_cast<int>(glp::GemmRowCfgT<2>::SMEM)));
+  GLP_CUDA(cudaFuncSetAttribute(glp::gemm_rownorm_kernel<__half, 3>, A, static_cast<int>(glp::GemmRowCfgT<3>::SMEM)));
+  GLP_CUDA(cudaFuncSetAttribute(glp::gemm_rownorm_kernel<__half, 4>, A, static_cast<int>(glp::GemmRowCfgT<4>::SMEM)));
   GLP_CUDA(cudaFuncSetAttribute(glp::flash_attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 static_cast<int>(glp::kAttnSmem)));
   GLP_CUDA(cudaFuncSetAttribute(glp::flash_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -240,11 +242,11 @@ bool pair_gemm_for(int epi, int M, int n_tiles) {
   return static_cast<int64_t>((M + 255) / 256) * n_tiles >= sm_count() / 2;
 }
 
-// Post-norms fused into the O / down GEMMs (gemm_rownorm_kernel) for 768-wide rows, for every
-// launch chunk (GLP_FUSED_NORM=0: separate row kernels).  Not chosen by chunk size, although a
-// single-wave chunk runs the row kernels faster (one 512-token sequence 1.70 vs 1.81 ms): the two
-// paths round differently, and a sequence's embedding stays bit-identical whatever batch it
-// is embedded in only if every chunk takes the same path.
+// Post-norms fused into the O / down GEMMs (gemm_rownorm_kernel) for 512-, 768- and 1024-wide
+// rows, for every launch chunk (GLP_FUSED_NORM=0: separate row kernels).  Not chosen by chunk
+// size, although a single-wave chunk runs the row kernels faster (one 512-token sequence 1.70
+// vs 1.81 ms): the two paths round differently, and a sequence's embedding stays bit-identical
+// whatever batch it is embedded in only if every chunk takes the same path.
 int fused_norm_mode() {  // 0 never, 2 always
   static const int mode = [] {
     const char* e = std::getenv("GLP_FUSED_NORM");
@@ -253,8 +255,12 @@ int fused_norm_mode() {  // 0 never, 2 always
   return mode;
 }
 
-// Clusters of 6 that can be resident at once (per device, cached): the persistent row-norm
-// GEMM launches that many.
+// Row widths the clustered row-norm GEMM covers: 2, 3 or 4 CTA pairs of 256 columns.
+bool rownorm_width(int n) { return n == 512 || n == 768 || n == 1024; }
+
+// Clusters of 2 NP CTAs that fit the device at once (cached per device and NP): the persistent
+// row-norm GEMM launches that many.
+template <int NP>
 int rownorm_clusters() {
   static std::mutex mu;
   static std::array<int, 64> cache{};
@@ -263,35 +269,48 @@ int rownorm_clusters() {
   std::lock_guard<std::mutex> lk(mu);
   if (dev >= 0 && dev < 64 && cache[dev] > 0) return cache[dev];
   cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(6 * 24);
+  cfg.gridDim = dim3(2 * NP * 16);
   cfg.blockDim = dim3(glp::kGemmThreads);
-  cfg.dynamicSmemBytes = glp::GemmRowCfg::SMEM;
+  cfg.dynamicSmemBytes = glp::GemmRowCfgT<NP>::SMEM;
   int n = 0;
-  if (cudaOccupancyMaxActiveClusters(&n, glp::gemm_rownorm_kernel<__half>, &cfg) != cudaSuccess || n <= 0) {
+  if (cudaOccupancyMaxActiveClusters(&n, glp::gemm_rownorm_kernel<__half, NP>, &cfg) != cudaSuccess || n <= 0) {
     cudaGetLastError();
-    n = sm_count() / 6;
+    n = sm_count() / (2 * NP);
   }
   if (dev >= 0 && dev < 64) cache[dev] = n;
   return n;
 }
 
-// y = A * B^T (N == 768) fused with the post-norm + residual + next pre-norm: updates p.h in
-// place and writes p.x_next.  `mb_pair` covers B with 128-row boxes, `mh` the residual rows
-// [M, 768] bf16 and `mx` the next pre-normed rows [M, 768] f16, both with 32-row boxes.
+template <int NP>
+void launch_rownorm_np(const CUtensorMap& ma, const CUtensorMap& mb_pair, const CUtensorMap& mh, const CUtensorMap& mx,
+                       const GemmParams& p, cudaStream_t st) {
+  const int clusters = std::min(p.m_tiles, rownorm_clusters<NP>());
+  glp::gemm_rownorm_kernel<__half, NP>
+      <<<2 * NP * clusters, glp::kGemmThreads, glp::GemmRowCfgT<NP>::SMEM, st>>>(ma, mb_pair, mh, mx, p);
+}
+
+// y = A * B^T (N = 512, 768 or 1024: clusters of 2, 3 or 4 CTA pairs) fused with the post-norm
+// + residual + next pre-norm: updates p.h in place and writes p.x_next.  `mb_pair` covers B
+// with 128-row boxes, `mh` the residual rows [M, N] bf16 and `mx` the next pre-normed rows
+// [M, N] f16, both with 32-row boxes.
 int launch_rownorm_gemm(const CUtensorMap& ma, const CUtensorMap& mb_pair, const CUtensorMap& mh, const CUtensorMap& mx,
                         GemmParams p, cudaStream_t st) {
   if (p.M <= 0) return GLP_OK;
-  if (p.N != 768 || p.K % 64 || p.K <= 0) return fail(GLP_ERR_INVALID_ARG, "row-norm GEMM needs N == 768, K % 64 == 0");
+  if (!rownorm_width(p.N) || p.K % 64 || p.K <= 0)
+    return fail(GLP_ERR_INVALID_ARG, "row-norm GEMM needs N in {512, 768, 1024}, K % 64 == 0");
   p.m_tiles = (p.M + 255) / 256;
-  p.n_tiles = 3;
+  p.n_tiles = p.N / 256;
   p.k_blocks = p.K / 64;
   static const bool direct = [] {  // GLP_ROWNORM_DIRECT=1: the exact two-exchange scale everywhere
     const char* e = std::getenv("GLP_ROWNORM_DIRECT");
     return e && std::string(e) == "1";
   }();
   p.rownorm_direct = direct ? 1 : 0;
-  const int clusters = std::min(p.m_tiles, rownorm_clusters());
-  glp::gemm_rownorm_kernel<__half><<<6 * clusters, glp::kGemmThreads, glp::GemmRowCfg::SMEM, st>>>(ma, mb_pair, mh, mx, p);
+  switch (p.N) {
+    case 512: launch_rownorm_np<2>(ma, mb_pair, mh, mx, p, st); break;
+    case 768: launch_rownorm_np<3>(ma, mb_pair, mh, mx, p, st); break;
+    default: launch_rownorm_np<4>(ma, mb_pair, mh, mx, p, st); break;
+  }
   GLP_CUDA(cudaGetLastError());
   return GLP_OK;
 }
@@ -1019,9 +1038,9 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
 
     const double post_bytes = Td * (2.0 * H + 4.0 * H + 2.0 * H);  // y + h in/out + x (16-bit)
     const double fused_bytes = Td * (4.0 * H + 2.0 * H);              // h in/out + x, no y
-    // the row-norm GEMM needs 768-wide rows (three CTA pairs per cluster) and the CTA-pair weight
-    // maps; other widths run the GEMM then post_norm_residual_kernel
-    const bool fused = fused_norm_mode() != 0 && H == 768 && use_pair_gemm(glp::kEpiStore16);
+    // the row-norm GEMM covers 512-, 768- and 1024-wide rows (2-4 CTA pairs per cluster) and
+    // needs the CTA-pair weight maps; other widths run the GEMM then post_norm_residual_kernel
+    const bool fused = fused_norm_mode() != 0 && rownorm_width(H) && use_pair_gemm(glp::kEpiStore16);
     CUtensorMap m_h, m_xo;  // residual rows (loads and stores) and next pre-normed rows, 32-row boxes
     if (fused) GLP_TRY(make_map16(&m_h, d.h, T, H, H, 32, false));
     if (fused) GLP_TRY(make_map16(&m_xo, d.x, T, H, H, 32, true));

@@ -142,3 +142,38 @@ def test_default_fuses_every_chunk(small_cond_gguf, tmp_path):
     _run(MODEL_SCRIPT, [small_cond_gguf, a], None, tmp_path, fused_norm=None)
     _run(MODEL_SCRIPT, [small_cond_gguf, b], None, tmp_path, fused_norm=True)
     np.testing.assert_array_equal(np.load(a), np.load(b))
+
+
+@pytest.mark.parametrize("name,kw", [
+    # clusters of 2 CTA pairs: hidden 512 (with per-layer KV heads and per-layer embeddings)
+    ("h512", dict(n_layers=6, hidden=512, n_heads=4, n_kv_heads=2, global_kv_heads=1, ffn=2048,
+                  head_dims=(512,), ple_dim=256)),
+    ("h512_plain", dict(n_layers=2, hidden=512, n_heads=4, n_kv_heads=2, ffn=2048, head_dims=(512,))),
+    # clusters of 4 CTA pairs (8 CTAs, three operand stages): hidden 1024
+    ("h1024", dict(n_layers=2, hidden=1024, n_heads=4, n_kv_heads=1, ffn=1536, head_dims=(1024,))),
+])
+def test_fused_post_norm_other_widths(gguf_dir, tmp_path, name, kw):
+    """The row-norm GEMM on 512- and 1024-wide rows (2 and 4 CTA pairs per cluster) against the
+    GEMM + row-kernel path, with the same bounds as the 768-wide case above, deterministic, and
+    the directly summed row scale."""
+    from glypr_b200 import synth
+    path = synth.ensure_gguf(os.path.join(str(gguf_dir), f"fused_{name}.gguf"),
+                             synth.small_config(qk_gain_scale=0.25, **kw))
+    a, b = str(tmp_path / "fused.npy"), str(tmp_path / "rows.npy")
+    _run(MODEL_SCRIPT, [path, a], None, tmp_path, fused_norm=True)
+    _run(MODEL_SCRIPT, [path, b], None, tmp_path, fused_norm=False)
+    fa, fb = np.load(a), np.load(b)
+    assert np.isfinite(fa).all()
+    cos = (fa * fb).sum(axis=1) / np.linalg.norm(fa, axis=1) / np.linalg.norm(fb, axis=1)
+    long_seq = np.array(LENGTHS) >= 16
+    assert cos[long_seq].min() >= 0.99999, cos
+    assert cos.min() >= 0.999, cos
+    assert np.abs(fa - fb)[long_seq].max() <= 1e-3
+    assert not np.array_equal(fa, fb)  # the fused kernel ran
+    _run(MODEL_SCRIPT, [path, b], None, tmp_path, fused_norm=True)
+    np.testing.assert_array_equal(np.load(b), fa)
+    _run(MODEL_SCRIPT, [path, b], None, tmp_path, fused_norm=True, direct=True)
+    fd = np.load(b)
+    cos = (fa * fd).sum(axis=1) / np.linalg.norm(fa, axis=1) / np.linalg.norm(fd, axis=1)
+    assert cos[long_seq].min() >= 0.99999, cos
+    assert cos.min() >= 0.999, cos
