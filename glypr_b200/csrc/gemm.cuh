@@ -19,12 +19,15 @@
 //               One 256-column tile == one head (attention/mod.rs:166-188, rope.rs:90-106).
 //   kEpiGeglu   B rows interleaved [gate 128 | up 128] per tile; out = gelu_tanh(g)*u as T
 //               (cpu_simd/geglu.rs:6-18, with its +-10 clamp).
+//   kEpiMulGeglu  out = gelu_tanh(acc) * U[row, col] as f16, U an f16 matrix in HBM (the
+//               per-layer-embedding block's gate times the layer's per-layer inputs,
+//               ple.rs:118-136).
 #pragma once
 #include "common.cuh"
 
 namespace glp {
 
-enum EpiKind : int { kEpiStore16 = 0, kEpiF32 = 1, kEpiQkv = 2, kEpiGeglu = 3 };
+enum EpiKind : int { kEpiStore16 = 0, kEpiF32 = 1, kEpiQkv = 2, kEpiGeglu = 3, kEpiMulGeglu = 4 };
 
 struct GemmParams {
   int M, N, K;
@@ -47,6 +50,9 @@ struct GemmParams {
   const float* w_next;
   float layer_scalar;
   int rownorm_direct;  // 1: always the exact two-exchange row scale (testing)
+  // kEpiMulGeglu: the second GeGLU operand U (row stride ld_mul elements)
+  const __half* mul;
+  int ld_mul;
 };
 
 template <int BN>
@@ -131,7 +137,7 @@ __device__ __forceinline__ bool gemm_epilogue_tile(const GemmParams& p, uint32_t
   const int row = m_blk * 128 + row_in_tile;
   const int wrow0 = row - (threadIdx.x & 31);  // first row of this warp's 32
   const int rows_valid = min(32, p.M - wrow0);
-  if constexpr (EPI == kEpiStore16 || EPI == kEpiF32) {
+  if constexpr (EPI == kEpiStore16 || EPI == kEpiF32 || EPI == kEpiMulGeglu) {
     // this warp's BN/2 columns in slices of 128 bytes per row: 64 16-bit or 32 f32 columns
     constexpr int ELT = EPI == kEpiF32 ? 4 : 2;
     constexpr int SLICE = 128 / ELT;
@@ -152,10 +158,28 @@ __device__ __forceinline__ bool gemm_epilogue_tile(const GemmParams& p, uint32_t
         tmem_ld32(tbase + sl * 64 + 32, rb);
         tmem_ld_wait_tied(ra);
         tmem_ld_wait_tied(rb);
+        if constexpr (EPI == kEpiMulGeglu) {
+          // this lane's row of U under the slice: 64 f16 = 128 contiguous bytes (rows past M
+          // are not read; their outputs are clipped by the flush)
+          uint4 uu[8];
+          const int r = wrow0 + static_cast<int>(threadIdx.x & 31);
+          const uint4* src = reinterpret_cast<const uint4*>(p.mul + static_cast<size_t>(r) * p.ld_mul + col0 + sl * 64);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          w[j] = Half16<T>::pack(u2f(ra[2 * j]), u2f(ra[2 * j + 1]));
-          w[16 + j] = Half16<T>::pack(u2f(rb[2 * j]), u2f(rb[2 * j + 1]));
+          for (int i = 0; i < 8; ++i) uu[i] = r < p.M ? src[i] : make_uint4(0u, 0u, 0u, 0u);
+          const __half* ue = reinterpret_cast<const __half*>(uu);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            w[j] = Half16<T>::pack(geglu_f(u2f(ra[2 * j]), __half2float(ue[2 * j])),
+                                   geglu_f(u2f(ra[2 * j + 1]), __half2float(ue[2 * j + 1])));
+            w[16 + j] = Half16<T>::pack(geglu_f(u2f(rb[2 * j]), __half2float(ue[32 + 2 * j])),
+                                        geglu_f(u2f(rb[2 * j + 1]), __half2float(ue[32 + 2 * j + 1])));
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            w[j] = Half16<T>::pack(u2f(ra[2 * j]), u2f(ra[2 * j + 1]));
+            w[16 + j] = Half16<T>::pack(u2f(rb[2 * j]), u2f(rb[2 * j + 1]));
+          }
         }
       }
       stage_words32(stage, w);

@@ -159,6 +159,8 @@ int ensure_kernel_attrs() {
   GLP_CUDA(cudaFuncSetAttribute(glp::gemm_tc_kernel<256, glp::kEpiGeglu, __half>, A, s256));
   GLP_CUDA(cudaFuncSetAttribute(glp::gemm_tc_kernel<128, glp::kEpiStore16, __half>, A, s128));
   GLP_CUDA(cudaFuncSetAttribute(glp::gemm_tc_kernel<128, glp::kEpiF32, __half>, A, s128));
+  GLP_CUDA(cudaFuncSetAttribute(glp::gemm_tc_kernel<256, glp::kEpiMulGeglu, __half>, A, s256));
+  GLP_CUDA(cudaFuncSetAttribute(glp::gemm_tc_kernel<128, glp::kEpiMulGeglu, __half>, A, s128));
   GLP_CUDA(cudaFuncSetAttribute(glp::gemm_tc_kernel<256, glp::kEpiStore16, __nv_bfloat16>, A, s256));
   GLP_CUDA(cudaFuncSetAttribute(glp::gemm_tc_kernel<256, glp::kEpiF32, __nv_bfloat16>, A, s256));
   GLP_CUDA(cudaFuncSetAttribute(glp::gemm_tc_kernel<128, glp::kEpiStore16, __nv_bfloat16>, A, s128));
@@ -168,6 +170,7 @@ int ensure_kernel_attrs() {
   GLP_CUDA(cudaFuncSetAttribute(glp::gemm_pair_kernel<glp::kEpiF32, __half>, A, sp));
   GLP_CUDA(cudaFuncSetAttribute(glp::gemm_pair_kernel<glp::kEpiQkv, __half>, A, sp));
   GLP_CUDA(cudaFuncSetAttribute(glp::gemm_pair_kernel<glp::kEpiGeglu, __half>, A, sp));
+  GLP_CUDA(cudaFuncSetAttribute(glp::gemm_pair_kernel<glp::kEpiMulGeglu, __half>, A, sp));
   GLP_CUDA(cudaFuncSetAttribute(glp::gemm_pair_kernel<glp::kEpiStore16, __nv_bfloat16>, A, sp));
   GLP_CUDA(cudaFuncSetAttribute(glp::gemm_pair_kernel<glp::kEpiF32, __nv_bfloat16>, A, sp));
   GLP_CUDA(cudaFuncSetAttribute(glp::gemm_rownorm_kernel<__half, 2>, A, static_cast<int>(glp::GemmRowCfgT<2>::SMEM)));
@@ -328,7 +331,7 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, int bn, int epi, G
   if (p.K % 64 || p.N % bn || p.K <= 0) return fail(GLP_ERR_INVALID_ARG, "GEMM needs K % 64 == 0 and N % tile == 0");
   const bool f16 = std::is_same<T, __half>::value;
   if (bn == 256 && mb_pair && pair_gemm_for(epi, p.M, p.n_tiles)) {
-    if ((epi == glp::kEpiQkv || epi == glp::kEpiGeglu) && !f16)
+    if ((epi == glp::kEpiQkv || epi == glp::kEpiGeglu || epi == glp::kEpiMulGeglu) && !f16)
       return fail(GLP_ERR_INVALID_ARG, "fused epilogues run on f16 operands");
     p.m_tiles = (p.M + 255) / 256;  // 256-row pair tiles
     const int pairs = std::min(p.m_tiles * p.n_tiles, sm_count() / 2);
@@ -342,6 +345,9 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, int bn, int epi, G
         glp::gemm_pair_kernel<glp::kEpiQkv, __half><<<grid, glp::kGemmThreads, smem, st>>>(ma, *mb_pair, *mc, p);
         break;
       case glp::kEpiGeglu: glp::gemm_pair_kernel<glp::kEpiGeglu, __half><<<grid, glp::kGemmThreads, smem, st>>>(ma, *mb_pair, ma, p); break;
+      case glp::kEpiMulGeglu:
+        glp::gemm_pair_kernel<glp::kEpiMulGeglu, __half><<<grid, glp::kGemmThreads, smem, st>>>(ma, *mb_pair, ma, p);
+        break;
       default: return fail(GLP_ERR_INVALID_ARG, "bad epilogue");
     }
     GLP_CUDA(cudaGetLastError());
@@ -362,6 +368,10 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, int bn, int epi, G
         if (!f16) return fail(GLP_ERR_INVALID_ARG, "fused epilogues run on f16 operands");
         glp::gemm_tc_kernel<256, glp::kEpiGeglu, __half><<<grid, glp::kGemmThreads, smem, st>>>(ma, mb, p);
         break;
+      case glp::kEpiMulGeglu:
+        if (!f16) return fail(GLP_ERR_INVALID_ARG, "fused epilogues run on f16 operands");
+        glp::gemm_tc_kernel<256, glp::kEpiMulGeglu, __half><<<grid, glp::kGemmThreads, smem, st>>>(ma, mb, p);
+        break;
       default: return fail(GLP_ERR_INVALID_ARG, "bad epilogue");
     }
   } else {
@@ -369,6 +379,10 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, int bn, int epi, G
     switch (epi) {
       case glp::kEpiStore16: glp::gemm_tc_kernel<128, glp::kEpiStore16, T><<<grid, glp::kGemmThreads, smem, st>>>(ma, mb, p); break;
       case glp::kEpiF32: glp::gemm_tc_kernel<128, glp::kEpiF32, T><<<grid, glp::kGemmThreads, smem, st>>>(ma, mb, p); break;
+      case glp::kEpiMulGeglu:
+        if (!f16) return fail(GLP_ERR_INVALID_ARG, "fused epilogues run on f16 operands");
+        glp::gemm_tc_kernel<128, glp::kEpiMulGeglu, __half><<<grid, glp::kGemmThreads, smem, st>>>(ma, mb, p);
+        break;
       default: return fail(GLP_ERR_INVALID_ARG, "fused epilogues need 256-wide tiles");
     }
   }
@@ -660,7 +674,7 @@ enum ProfKind : int {
   kProfMisc,
   kProfKernelApi,
   kProfPleGemm,  // per-layer-embedding projections (PLE models only)
-  kProfPleRows,  // per-layer-embedding norm and GeGLU
+  kProfPleRows,  // per-layer-embedding input norm
 };
 const char* const kProfNames[GLP_PROFILE_KINDS] = {
     "embed_gather_norm", "gemm_qkv_norm_rope", "flash_attention", "gemm_o", "post_norm_residual",
@@ -1144,8 +1158,8 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
                           [&] { return launch_gemm<__half>(m_a, L.m_down, bn_for(H), glp::kEpiStore16, pd, st, &L.p_down); }));
       if (ple) {
         // ple.rs:118-145 after the FFN block: h2 = h + RMSNorm(y) w (kept raw in x for the
-        // gate), g = geglu(gate(h2), P_l), y = proj(g), then the post-norm, residual add and
-        // layer scalar of the shared tail below
+        // gate), g = geglu(gate(h2), P_l) in the gate GEMM's epilogue, y = proj(g), then the
+        // post-norm, residual add and layer scalar of the shared tail below
         GLP_TRY(prof_launch(d, st, kProfPostNorm, 0.0, post_bytes, [&] {
           return with_hidden(H, [&](auto hc) {
             glp::post_norm_residual_kernel<decltype(hc)::value, glp::kPostRaw>
@@ -1154,22 +1168,18 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
             return GLP_OK;
           });
         }));
+        // gate GEMM with the GeGLU against this layer's per-layer inputs in its epilogue
         GemmParams pg2{};
         pg2.M = T;
         pg2.N = PD;
         pg2.K = H;
         pg2.C = d.ple_g;
         pg2.ldc = PD;
+        pg2.mul = d.ple + static_cast<size_t>(l) * PD;
+        pg2.ld_mul = LD;
         pg2.status = d.status;
-        GLP_TRY(prof_launch(d, st, kProfPleGemm, gemm_flops(Td, PD, H), gemm_bytes(Td, PD, H, 2.0), [&] {
-          return launch_gemm<__half>(m_x, L.m_pg, bn_for(PD), glp::kEpiStore16, pg2, st, &L.p_pg);
-        }));
-        const int64_t n_el = static_cast<int64_t>(T) * PD;
-        GLP_TRY(prof_launch(d, st, kProfPleRows, 0.0, 6.0 * n_el, [&] {
-          glp::ple_geglu_kernel<<<static_cast<unsigned>((n_el / 8 + 255) / 256), 256, 0, st>>>(d.ple_g, d.ple, T, PD,
-                                                                                             l, c.n_layers);
-          GLP_CUDA(cudaGetLastError());
-          return GLP_OK;
+        GLP_TRY(prof_launch(d, st, kProfPleGemm, gemm_flops(Td, PD, H), gemm_bytes(Td, PD, H, 4.0), [&] {
+          return launch_gemm<__half>(m_x, L.m_pg, bn_for(PD), glp::kEpiMulGeglu, pg2, st, &L.p_pg);
         }));
         GemmParams pp2{};
         pp2.M = T;

@@ -1,8 +1,7 @@
-// Per-layer-embedding (PLE) row kernels: the normalised per-layer inputs and the PLE block's
-// GeGLU (crates/glypr-core/src/ple.rs:48-145).  The projections around them are the Q8_0
-// GEMMs of gemm.cuh.
+// Per-layer-embedding (PLE) row kernel: the normalised per-layer inputs
+// (crates/glypr-core/src/ple.rs:48-93).  The projections around it are the Q8_0 GEMMs of
+// gemm.cuh; the PLE block's GeGLU runs in its gate GEMM's epilogue (kEpiMulGeglu).
 #pragma once
-#include "gemm.cuh"    // geglu_f: the MLP's GeGLU, which the PLE block reuses (cpu_simd::cpu_geglu)
 #include "rowops.cuh"  // warp_sum, 8-element vector loads and stores
 
 namespace glp {
@@ -38,25 +37,6 @@ __global__ void ple_norm_kernel(__half* __restrict__ p, int64_t n_rows, int D, f
     for (int j = 0; j < 8; ++j) o[j] = (__half2float(e[j]) * scale) * inv * wv[j];
     store16x8<__half>(row + e0, o);
   }
-}
-
-// g[t, j] = f16(geglu(g[t, j], P[t, layer, j])) in place: the PLE block's gate output times the
-// layer's slice of the per-layer inputs (ple.rs:118-136).  8 elements per thread (D % 8 == 0,
-// so a group never crosses a row).
-__global__ void ple_geglu_kernel(__half* __restrict__ g, const __half* __restrict__ p, int64_t n_tokens, int D,
-                                 int layer, int n_layers) {
-  const int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 8;
-  if (i >= n_tokens * D) return;
-  const int64_t t = i / D;
-  const int64_t j = i - t * D;
-  const uint4 gu = *reinterpret_cast<const uint4*>(g + i);
-  const uint4 pu = *reinterpret_cast<const uint4*>(p + (t * n_layers + layer) * D + j);
-  const __half* ge = reinterpret_cast<const __half*>(&gu);
-  const __half* pe = reinterpret_cast<const __half*>(&pu);
-  float o[8];
-#pragma unroll
-  for (int k = 0; k < 8; ++k) o[k] = geglu_f(__half2float(ge[k]), __half2float(pe[k]));
-  store16x8<__half>(g + i, o);
 }
 
 }  // namespace glp
