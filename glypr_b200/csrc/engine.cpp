@@ -20,6 +20,7 @@
 #include <cmath>
 #include <condition_variable>
 #include <cstring>
+#include <exception>
 #include <deque>
 #include <mutex>
 #include <string>
@@ -170,7 +171,13 @@ int engine_create(glp_batch_fn fn, void* user, bool model, int dim, int max_batc
   e->dim = dim;
   e->max_batch = max_batch;
   e->capacity = queue_capacity > 0 ? static_cast<size_t>(queue_capacity) : 1024;
-  e->worker = std::thread([e] { e->run(); });
+  try {
+    e->worker = std::thread([e] { e->run(); });
+  } catch (const std::exception&) {
+    delete e;
+    glp::set_last_error("cannot start the engine's worker thread");
+    return GLP_ERR_OOM;
+  }
   *out = e;
   return GLP_OK;
 }

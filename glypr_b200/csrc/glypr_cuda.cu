@@ -17,6 +17,7 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <exception>
 #include <memory>
 #include <mutex>
 #include <string>
@@ -1640,7 +1641,15 @@ int glp_embed_tokens(glp_ctx* ctx, const int32_t* ids, const int32_t* lengths, i
     cudaSetDevice(prev);
   } else {
     std::vector<std::thread> th;
-    for (int i = 0; i < nd; ++i) th.emplace_back(work, i);
+    int spawned = 0;
+    try {
+      for (; spawned < nd; ++spawned) th.emplace_back(work, spawned);
+    } catch (const std::exception&) {  // no more threads: the calling thread runs the other shards
+      int prev = 0;
+      cudaGetDevice(&prev);
+      for (int i = spawned; i < nd; ++i) work(i);
+      cudaSetDevice(prev);
+    }
     for (auto& t : th) t.join();
   }
   for (int i = 0; i < nd; ++i) {

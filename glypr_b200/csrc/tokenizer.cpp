@@ -31,6 +31,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
+#include <exception>
 #include <string>
 #include <string_view>
 #include <thread>
@@ -646,7 +647,11 @@ int glp_tokenize_batch(const glp_tokenizer* tok, const char* const* texts, const
     work();
   } else {
     std::vector<std::thread> pool;
-    for (unsigned k = 0; k < nt; ++k) pool.emplace_back(work);
+    try {
+      for (unsigned k = 0; k < nt; ++k) pool.emplace_back(work);
+    } catch (const std::exception&) {  // fewer threads than asked: the calling thread helps
+    }
+    if (pool.size() < nt) work();
     for (auto& th : pool) th.join();
   }
   // the first failing item in order, as the reference's sequential loop reports it
@@ -808,7 +813,13 @@ int glp_embed_texts(glp_ctx* ctx, const glp_tokenizer* tok, const char* const* t
   tokenize_part(tok, texts, text_lens, form, &ps[0]);
   for (int p = 0; p < parts; ++p) {
     std::thread next;
-    if (p + 1 < parts) next = std::thread(tokenize_part, tok, texts, text_lens, form, &ps[p + 1]);
+    if (p + 1 < parts) {
+      try {
+        next = std::thread(tokenize_part, tok, texts, text_lens, form, &ps[p + 1]);
+      } catch (const std::exception&) {  // no thread to be had: tokenise it here, unoverlapped
+        tokenize_part(tok, texts, text_lens, form, &ps[p + 1]);
+      }
+    }
     if (ps[p].rc != GLP_OK) {  // the batch's first tokenisation error
       if (next.joinable()) next.join();
       return fail(ps[p].rc, ps[p].err);
