@@ -95,6 +95,11 @@ class EncoderConfig:
     ple_dim: int = 0
     # KV heads of the global layers (0 = n_kv_heads, as on the sliding layers)
     global_kv_heads: int = 0
+    # head_dim of the global layers (0 = head_dim; the real EmbeddingGemma 2 has 512 there)
+    global_head_dim: int = 0
+
+    def head_dim_of(self, i: int) -> int:
+        return self.head_dim if self.layer_is_sliding(i) or not self.global_head_dim else self.global_head_dim
 
     def kv_heads(self, i: int) -> int:
         return self.n_kv_heads if self.layer_is_sliding(i) or not self.global_kv_heads else self.global_kv_heads
@@ -203,10 +208,11 @@ def _kv_key(kv: bytes) -> str:
 
 def _tensor_order(cfg: EncoderConfig) -> List[Tuple[str, Tuple[int, ...], str]]:
     """(name, shape [rows, cols] or [n], kind) in the fixed sub-stream order."""
-    h, f, d = cfg.hidden, cfg.ffn, cfg.head_dim
+    h, f = cfg.hidden, cfg.ffn
     order: List[Tuple[str, Tuple[int, ...], str]] = [("token_embd.weight", (cfg.vocab, h), "mat")]
     for i in range(cfg.n_layers):
         p = f"blk.{i}."
+        d = cfg.head_dim_of(i)
         order += [
             (p + "attn_norm.weight", (h,), "gain"),
             (p + "attn_q.weight", (cfg.n_heads * d, h), "mat"),
@@ -282,7 +288,7 @@ def metadata(cfg: EncoderConfig, tokenizer: Optional[Tuple[Sequence[str], Sequen
         _kv(a + "attention.head_count", _U32, cfg.n_heads),
         _kv(a + "attention.head_count_kv", _ARR, (_U32, [cfg.kv_heads(i) for i in range(cfg.n_layers)])),
         _kv(a + "attention.key_length_swa", _U32, cfg.head_dim),
-        _kv(a + "attention.key_length", _U32, cfg.head_dim),
+        _kv(a + "attention.key_length", _U32, cfg.global_head_dim or cfg.head_dim),
         _kv(a + "embedding_length_out", _U32, cfg.embedding_out),
         _kv(a + "context_length", _U32, cfg.context_length),
         _kv(a + "attention.layer_norm_rms_epsilon", _F32, cfg.eps),

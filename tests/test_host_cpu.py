@@ -145,6 +145,15 @@ def test_open_accepts_global_kv_heads(tmp_path):
     assert rc == api.GLP_ERR_FORMAT and msg == "head_count must be a multiple of head_count_kv"
 
 
+def test_open_rejects_global_head_dim_512(tmp_path):
+    """The real EmbeddingGemma 2's head_dim-512 global layers: parsed (the oracle runs them) but
+    not supported by the CUDA attention, which holds 256-wide heads."""
+    cfg = synth.small_config(n_layers=6, vocab=256, hidden=512, n_heads=4, n_kv_heads=2, global_kv_heads=1,
+                             global_head_dim=512, head_dims=(512,))
+    rc, msg = _open(synth.write_gguf(str(tmp_path / "d512.gguf"), cfg))
+    assert rc == api.GLP_ERR_UNSUPPORTED and msg.startswith("per-layer head_dim overrides are not supported")
+
+
 def test_open_rejects_head_dim_override(tmp_path):
     cfg = synth.small_config(n_layers=6, vocab=256)
     p = synth.write_gguf(str(tmp_path / "hd.gguf"), cfg, drop={"gemma-embedding2.attention.key_length"})

@@ -240,3 +240,46 @@ def test_ple_block_restated(gguf_dir, mode):
     want = (h2 + y) * s
     assert s != 1.0 and np.abs(y).max() > 0.1
     np.testing.assert_allclose(got, want, rtol=1e-5, atol=1e-5)
+
+
+# ------------------------------------------------------------------ config.rs:141-160, rope.rs, model.rs:279-300
+def _rope(x, cos, sin):
+    """NeoX rotate_half RoPE (rope.rs:90-106) on rows [t, n, d] with tables [t, d]."""
+    d = x.shape[-1]
+    rot = np.concatenate([-x[..., d // 2:], x[..., :d // 2]], axis=-1)
+    return (x * cos[:, None, :] + rot * sin[:, None, :]).astype(np.float32)
+
+
+@pytest.mark.parametrize("mode", [oracle.M1_CANDLE, oracle.M2_EXACT])
+def test_global_layer_head_dim_512_restated(gguf_dir, mode):
+    """The oracle's global layer of the real EmbeddingGemma 2 (head_dim 512 from key_length, its
+    own KV-head count, RoPE over 512 dims with the global theta) against a composition of the
+    pinned primitives.  The CUDA library rejects such files; this pins the checker for them."""
+    H, NH, KV, D = 512, 4, 1, 512
+    cfg = synth.small_config(n_layers=1, global_every=1, hidden=H, n_heads=NH, n_kv_heads=2, global_kv_heads=KV,
+                             global_head_dim=D, ffn=1024, head_dims=(512,), vocab=512, qk_gain_scale=0.25)
+    path = synth.ensure_gguf(os.path.join(str(gguf_dir), "global_d512.gguf"), cfg)
+    m = oracle.OracleModel(path)
+    assert (m.head_dim, m.n_kv) == (D, KV)
+    ids = np.random.default_rng(9).integers(2, 512, size=41).astype(np.int32)
+    t = ids.size
+    got = m.hidden_after(ids, 0, mode)
+
+    def lin(name, n, k, x):
+        return oracle.q8_0_matmul(_tensor(cfg, name), n, k, x, mode)
+
+    h = synth.dequantize_q8_0(_tensor(cfg, "token_embd.weight")[ids]) * np.float32(np.sqrt(H))
+    x = oracle.rmsnorm(h, _tensor(cfg, "blk.0.attn_norm.weight"))
+    q = oracle.rmsnorm(lin("blk.0.attn_q.weight", NH * D, H, x).reshape(t, NH, D), _tensor(cfg, "blk.0.attn_q_norm.weight"))
+    k = oracle.rmsnorm(lin("blk.0.attn_k.weight", KV * D, H, x).reshape(t, KV, D), _tensor(cfg, "blk.0.attn_k_norm.weight"))
+    v = oracle.rmsnorm(lin("blk.0.attn_v.weight", KV * D, H, x).reshape(t, KV, D), None)
+    cos, sin = oracle.rope_tables(D, cfg.rope_theta_full, t)
+    q, k = _rope(q, cos, sin), _rope(k, cos, sin)
+    a = oracle.attention(q.reshape(t, -1), k.reshape(t, -1), v.reshape(t, -1), NH, KV, D, 512, False)
+    y = oracle.rmsnorm(lin("blk.0.attn_output.weight", H, NH * D, a), _tensor(cfg, "blk.0.post_attention_norm.weight"))
+    h = h + y
+    x = oracle.rmsnorm(h, _tensor(cfg, "blk.0.ffn_norm.weight"))
+    g = oracle.geglu(lin("blk.0.ffn_gate.weight", 1024, H, x), lin("blk.0.ffn_up.weight", 1024, H, x))
+    y = oracle.rmsnorm(lin("blk.0.ffn_down.weight", H, 1024, g), _tensor(cfg, "blk.0.post_ffw_norm.weight"))
+    want = h + y
+    np.testing.assert_allclose(got, want, rtol=2e-5, atol=2e-5)
