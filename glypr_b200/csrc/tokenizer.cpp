@@ -800,6 +800,10 @@ int glp_embed_texts(glp_ctx* ctx, const glp_tokenizer* tok, const char* const* t
     }
   }
   const int row_dim = out_dim > 0 ? out_dim : info.embedding_dim;
+  // parts embed into a private buffer, copied out only when the whole batch succeeded (no
+  // partial outputs on failure)
+  std::vector<float> staged(parts > 1 ? static_cast<size_t>(n_texts) * row_dim : 0);
+  float* dst = parts > 1 ? staged.data() : out;
   std::vector<TextPart> ps(parts);
   for (int p = 0; p < parts; ++p) {
     ps[p].lo = static_cast<int>(static_cast<int64_t>(n_texts) * p / parts);
@@ -839,10 +843,11 @@ int glp_embed_texts(glp_ctx* ctx, const glp_tokenizer* tok, const char* const* t
         if (rc != GLP_OK) return rc;
       }
     }
-    rc = embed_part(ctx, ps[p], out_dim, row_dim, out);
+    rc = embed_part(ctx, ps[p], out_dim, row_dim, dst);
     if (next.joinable()) next.join();
     if (rc != GLP_OK) return rc;
   }
+  if (parts > 1) std::memcpy(out, staged.data(), staged.size() * sizeof(float));
   return GLP_OK;
 }
 

@@ -154,6 +154,18 @@ def test_embed_texts_in_parts_first_error(text_model):
         with pytest.raises(GlyprError) as e:
             emb.embed_texts(tok, bad, api.GLP_TOKENS_SEQUENCE)
         assert e.value.message == f"Batch item 50 sequence length ({nb}) exceeds maximum context limit (8320)"
+        # no partial output: parts 0 and 1 embed before part 2's item 50 fails its preflight,
+        # and the caller's buffer stays untouched
+        import ctypes
+        bad2 = list(texts)
+        bad2[50] = unit * (9000 // per)
+        enc = [t.encode() for t in bad2]
+        out = np.full((64, 768), 7.0, np.float32)
+        rc = api.load_library().glp_embed_texts(
+            emb._h, tok._h, ctypes.cast((ctypes.c_char_p * 64)(*enc), ctypes.c_void_p),
+            ctypes.cast((ctypes.c_size_t * 64)(*[len(b) for b in enc]), ctypes.c_void_p), 64,
+            api.GLP_TOKENS_SEQUENCE, 0, 768, out.ctypes.data_as(ctypes.c_void_p))
+        assert rc == api.GLP_ERR_CONTEXT_LIMIT and (out == 7.0).all()
         bad[50] = texts[50]
         with pytest.raises(GlyprError) as e:
             emb.embed_texts(tok, bad, api.GLP_TOKENS_SEQUENCE)
