@@ -1,6 +1,9 @@
 """Regenerate the committed golden vectors (run from the repo root):
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py [CASE ...]
+
+(with case names, only those are regenerated and replaced in manifest.json; the others stay
+byte-identical)
 
 Each case writes a seeded synthetic GGUF (glypr_b200.synth), embeds a fixed batch of token
 ids with the CPU oracle in both matmul modes (M1 candle-faithful, M2 exact dequant) and
@@ -29,13 +32,28 @@ CASES = [
     ("tiny_cond_mrl", dict(n_layers=2, vocab=512, qk_gain_scale=0.25), [64, 20], 64, 256),
     ("one_layer_baseline_init", dict(n_layers=1, vocab=512), [128, 5], 128, 768),
     ("global_layer_window", dict(n_layers=6, vocab=512, qk_gain_scale=0.25), [600], 600, 768),
+    # the EmbeddingGemma 2 structure: hidden 512, 4 query heads over 2 KV heads (1 on the global
+    # layer), per-layer embeddings; the second also with the 512-wide global heads
+    ("embeddinggemma2_shape", dict(n_layers=6, hidden=512, n_heads=4, n_kv_heads=2, global_kv_heads=1, ffn=1024,
+                                   head_dims=(768,), ple_dim=256, vocab=512, qk_gain_scale=0.25), [200, 17], 200, 768),
+    ("embeddinggemma2_global_d512", dict(n_layers=6, hidden=512, n_heads=4, n_kv_heads=2, global_kv_heads=1,
+                                         global_head_dim=512, ffn=1024, head_dims=(768,), ple_dim=256, vocab=512,
+                                         qk_gain_scale=0.25), [200, 17], 200, 768),
 ]
 
 
-def main() -> None:
+def main(only=()) -> None:
     manifest = {"seed": synth.MASTER_SEED, "generator": "tests/golden/make_golden.py", "cases": []}
+    mpath = os.path.join(HERE, "manifest.json")
+    old = {}
+    if only and os.path.exists(mpath):
+        old = {c["name"]: c for c in json.load(open(mpath))["cases"]}
     with tempfile.TemporaryDirectory() as tmp:
         for name, over, lengths, max_len, out_dim in CASES:
+            if only and name not in only:
+                if name in old:
+                    manifest["cases"].append(old[name])
+                continue
             cfg = synth.EncoderConfig(**over)
             path = synth.write_gguf(os.path.join(tmp, name + ".gguf"), cfg, synth.MASTER_SEED)
             m = oracle.OracleModel(path)
@@ -48,9 +66,9 @@ def main() -> None:
             manifest["cases"].append({"name": name, "config": cfg_dict, "seed": synth.MASTER_SEED,
                                       "file": fname, "out_dim": out_dim, "lengths": lengths})
             print(name, "cos(m1, m2) =", (m1 * m2).sum(1))
-    with open(os.path.join(HERE, "manifest.json"), "w") as fh:
+    with open(mpath, "w") as fh:
         json.dump(manifest, fh, indent=1)
 
 
 if __name__ == "__main__":
-    main()
+    main(tuple(sys.argv[1:]))
