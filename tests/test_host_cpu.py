@@ -174,3 +174,30 @@ def test_make_batch_padding():
     assert ids.shape == (5, 40) and lens.min() >= 3 and lens.max() <= 40
     for i, L in enumerate(lens):
         assert (ids[i, L:] == 0).all() and (ids[i, :L] >= 2).all() and (ids[i, :L] < 1000).all()
+
+
+@pytest.mark.parametrize("global_kv,ok", [(1, True), (2, False)])
+def test_open_kv_heads_defaults(tmp_path, global_kv, ok):
+    """Without head_count_kv the sliding layers take 2 KV heads and the global ones 1
+    (config.rs:141-160): a file whose tensors agree opens, one whose global layer has 2 fails on
+    that layer's shapes."""
+    cfg = synth.small_config(n_layers=6, vocab=256, n_heads=4, n_kv_heads=2, global_kv_heads=global_kv)
+    p = synth.write_gguf(str(tmp_path / "kv.gguf"), cfg, drop={"gemma-embedding2.attention.head_count_kv"})
+    rc, msg = _open(p)
+    if ok:
+        assert rc not in (api.GLP_ERR_UNSUPPORTED, api.GLP_ERR_FORMAT), msg
+    else:
+        assert rc == api.GLP_ERR_FORMAT and msg == "bad shape for blk.5.attn_k.weight"
+
+
+@pytest.mark.parametrize("ple_dim,ok", [(512, True), (256, False)])
+def test_open_ple_width_default(tmp_path, ple_dim, ok):
+    """Without embedding_length_per_layer_input the per-layer width is 512 (config.rs:100-102)."""
+    cfg = synth.small_config(n_layers=2, vocab=256, ple_dim=ple_dim)
+    p = synth.write_gguf(str(tmp_path / "ple.gguf"), cfg,
+                         drop={"gemma-embedding2.embedding_length_per_layer_input"})
+    rc, msg = _open(p)
+    if ok:
+        assert rc not in (api.GLP_ERR_UNSUPPORTED, api.GLP_ERR_FORMAT), msg
+    else:
+        assert rc == api.GLP_ERR_FORMAT and msg == "bad shape for per_layer_model_proj.weight"
