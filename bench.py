@@ -11,7 +11,13 @@ one JSON line.
   e2e          the public host API glp_embed_tokens (host ids in, host embeddings out: H2D of
                the ids and D2H of the embeddings inside the timed region), max over ranks
   roofline     the dominant kernel's algorithmic FLOP (or byte) rate from CUDA events on the
-               launching stream during the timed region, against MEASURED_PEAKS.json
+               launching stream, in a separate profiled region after the timed one (the timed
+               region runs the product's default CUDA-graph replay, unprofiled), against
+               MEASURED_PEAKS.json
+  q8_0_gemm    BASELINE config 2: glp_q8_0_gemm (the LinearOp::forward seam on raw Q8_0 rows)
+               for W [N,K] in {768x768, 256x768, 1152x768, 768x1152} x M in {512, 4096,
+               32768, 131072}, bf16 out, % of roofline = max(FLOP / tensor peak, bytes / HBM
+               peak) / time, with its own clock record (N=1 only)
   cpu_baseline the C++ restatement of glypr's CPU path (oracle/, candle-faithful mode) on a
                bounded sample of the same workload, all host threads (rank 0, N=1 only)
 
@@ -53,10 +59,13 @@ def parse_args(argv=None):
     ap.add_argument("--seq-len", type=int, default=512)
     ap.add_argument("--max-batch-tokens", type=int, default=0, help="launch-chunk size (0 = library default)")
     ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--profile-steps", type=int, default=2,
+                    help="steps of the separate per-kernel profiled region (not the timed one)")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
     ap.add_argument("--model-dir", default=os.environ.get("GLYPR_BENCH_DIR",
                                                           os.path.join(tempfile.gettempdir(), "glypr_b200_bench")))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-q8-gemm", action="store_true", help="skip the config-2 GEMM section")
     return ap.parse_args(argv)
 
 
@@ -211,6 +220,17 @@ def roofline(prof: dict, peaks: dict) -> tuple:
 
 
 # ------------------------------------------------------------------------------ CPU baseline
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as fh:
+            for line in fh:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
 def cpu_baseline(model_path: str, seq_len: int, budget_s: float) -> dict:
     import oracle
     threads = os.cpu_count() or 1
@@ -225,12 +245,79 @@ def cpu_baseline(model_path: str, seq_len: int, budget_s: float) -> dict:
         if time.perf_counter() - t0 >= budget_s:
             break
     dt = time.perf_counter() - t0
-    return {"value": round(done / dt, 4), "unit": UNIT, "cores": threads, "kind": "port",
+    return {"value": round(done / dt, 4), "unit": UNIT, "cores": threads, "kind": "port", "cpu": cpu_model(),
             "sample": f"{done} x {seq_len}-token sequence(s), same synthetic GGUF, oracle M1 (candle-faithful "
                       f"Q8_0) C++ restatement of glypr's CPU path, {dt:.1f} s wall"}
 
 
 # ------------------------------------------------------------------------------ arms
+# ------------------------------------------------------------------------------ config 2
+Q8_SHAPES = ((768, 768), (256, 768), (1152, 768), (768, 1152))
+Q8_MS = (512, 4096, 32768, 131072)
+
+
+def q8_0_gemm_section(torch, device, peaks, local_rank) -> dict:
+    """Config 2 through the C ABI on the caller's stream: per (shape, M) the mean device time of
+    back-to-back calls that rotate over enough input sets to exceed L2 (126 MB), so no call
+    reads another's inputs from L2; roofline against the burst peaks (a kernel timed alone)."""
+    from glypr_b200 import api
+    stream = torch.cuda.current_stream(device)
+    st = stream.cuda_stream
+    p_t, p_b = peaks["bf16_tflops"], peaks["hbm_gbs"]
+    rng = np.random.default_rng(synth.MASTER_SEED + 22)
+    rows = []
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    host_us = None
+    for n, k in Q8_SHAPES:
+        w = (rng.standard_normal((n, k), dtype=np.float32) * np.float32(0.02)).astype(np.float32)
+        w_raw = synth.quantize_q8_0(w).view(np.uint8).reshape(-1)
+        for m in Q8_MS:
+            set_bytes = w_raw.size + 2 * m * k + 2 * m * n
+            n_sets = max(1, min(64, -(-160 * 2 ** 20 // set_bytes)))
+            sets = []
+            for _ in range(n_sets):
+                d_w = torch.from_numpy(w_raw.copy()).to(device)
+                x = torch.randn((m, k), device=device).to(torch.bfloat16)
+                y = torch.empty((m, n), device=device, dtype=torch.bfloat16)
+                sets.append((d_w, x, y))
+            calls = max(10, n_sets)
+
+            def run(i):
+                d_w, x, y = sets[i % n_sets]
+                api.q8_0_gemm(d_w.data_ptr(), n, k, x.data_ptr(), m, y.data_ptr(), False, st)
+            for i in range(3):
+                run(i)
+            torch.cuda.synchronize(device)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for i in range(calls):
+                run(i)
+            e1.record(stream)
+            torch.cuda.synchronize(device)
+            ms = e0.elapsed_time(e1) / calls
+            if m == Q8_MS[0] and host_us is None:  # host cost of one call (maps + launch), GPU idle
+                t0 = time.perf_counter()
+                for i in range(calls):
+                    run(i)
+                host_us = (time.perf_counter() - t0) / calls * 1e6
+                torch.cuda.synchronize(device)
+            flop = 2.0 * m * n * k
+            byts = n * k / 32 * 34 + 2.0 * m * k + 2.0 * m * n
+            roof_ms = max(flop / (p_t * 1e9), byts / (p_b * 1e6))
+            rows.append({"n": n, "k": k, "m": m, "ms": round(ms, 5), "tflops": round(flop / ms / 1e9, 1),
+                         "gbs": round(byts / ms / 1e6, 1), "roofline_pct": round(100 * roof_ms / ms, 1)})
+            del sets
+    clk = clocks.stop()
+    status = api.kernel_status(local_rank)
+    big = [r["roofline_pct"] for r in rows if r["m"] >= 32768]
+    return {"entry_point": "glp_q8_0_gemm (raw Q8_0 rows, bf16 x, bf16 y)", "peaks": "burst: bf16_tflops and hbm_gbs of "
+            f"{peaks['source']} MEASURED_PEAKS.json", "l2": "inputs rotated over sets larger than L2",
+            "rows": rows, "min_roofline_pct_m_ge_32768": min(big), "host_us_per_call_m512": round(host_us, 2),
+            "kernel_status": status, "clocks": clk}
+
+
 def run_reference(args) -> None:
     rank, world, _ = dist_env()
     if rank != 0:
@@ -259,6 +346,7 @@ def run_reference(args) -> None:
         "config": {"workload": f"config5 sample: 1 x {args.seq_len}-token sequence per step", "model": MODEL_DESC,
                    "seq_len": args.seq_len, "parallelism": "host threads"},
         "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads, "kind": "port",
+                         "cpu": cpu_model(),
                          "sample": f"1 x {args.seq_len}-token sequence per step, C++ restatement of glypr's CPU "
                                    "path (oracle/, candle-faithful Q8_0 mode), Rust reference not buildable here"},
         "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -305,7 +393,9 @@ def run_ours(args) -> None:
     if emb.device_status() != 0:
         raise SystemExit("device status word set during warm-up")
 
-    emb.profile_enable(True)
+    # timed region: the product's default path (launch chunks replayed as CUDA graphs); the
+    # library only counts launches here (no per-launch events)
+    emb.profile_enable(False)
     clocks = ClockSampler(local_rank)
     barrier(world, device)
     torch.cuda.synchronize(device)
@@ -320,12 +410,20 @@ def run_ours(args) -> None:
     barrier(world, device)
     clk = clocks.stop()
     ms = e0.elapsed_time(e1)
-    prof = emb.profile_read()
-    emb.profile_enable(False)
-    launches = prof["_total_launches"]
+    launches = emb.profile_read()["_total_launches"]
     assert emb.device_status() == 0, "device status word set in the timed region"
     ms_max = max_over_ranks(ms, world, device)
     value = world * seqs * args.steps / (ms_max * 1e-3)
+
+    # a separate, profiled region for the per-kernel table and the roofline: CUDA events
+    # around every launch on the launching stream (direct launches, no graph replay)
+    emb.profile_enable(True)
+    for _ in range(args.profile_steps):
+        step()
+    torch.cuda.synchronize(device)
+    prof = emb.profile_read()
+    emb.profile_enable(False)
+    assert emb.device_status() == 0, "device status word set in the profiled region"
 
     # e2e through the public host API (host ids -> host embeddings)
     emb.embed_tokens(ids, lens)  # warm the host staging buffers
@@ -346,8 +444,9 @@ def run_ours(args) -> None:
         "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f16",
         "data": "synthetic (seeded random-init GGUF weights, uniform token ids)",
-        "config": {"workload": f"config5: {L}-token Q8_0 sequences, {seqs} per GPU per step "
-                               f"({8 * seqs} = the box batch at 8 GPUs)",
+        "config": {"workload": f"config5 at weak scaling: {L}-token Q8_0 sequences, {seqs} per GPU per step "
+                               f"(8 x {seqs} = config 5's {8 * seqs}-sequence box batch at 8 GPUs; "
+                               "per-GPU throughput is in steady state at this size)",
                    "model": MODEL_DESC, "seqs_per_gpu": seqs, "global_batch": world * seqs, "seq_len": L,
                    "parallelism": f"dp{world} (contiguous sequence shards, replicated weights, no collective)",
                    "l2": "inputs larger than L2 (per launch chunk the activations are ~3 GB)",
@@ -355,6 +454,8 @@ def run_ours(args) -> None:
                               "attention, f32 norms/softmax/residual"},
         "tokens_per_s": round(value * L, 1),
         "roofline": rl,
+        "roofline_region": f"{args.profile_steps} separate profiled step(s) after the timed region "
+                           "(per-launch CUDA events on the launching stream)",
         "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": int(seqs * L * 4 + (seqs + 1) * 4),
                 "d2h_bytes_per_step": int(seqs * emb.embedding_dim * 4), "steps": args.e2e_steps,
                 "matches_device_path": same},
@@ -362,9 +463,11 @@ def run_ours(args) -> None:
         "clocks": clk,
         "kernels": table,
     }
+    emb.close()
+    if rank == 0 and world == 1 and not args.no_q8_gemm:
+        result["q8_0_gemm"] = q8_0_gemm_section(torch, device, peaks, local_rank)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(path, L, args.cpu_seconds)
-    emb.close()
     if rank == 0:
         print(json.dumps(result), flush=True)
     if world > 1:

@@ -43,7 +43,9 @@ EXPORTED_SYMBOLS = (
     "glp_engine_create", "glp_engine_create_with_executor", "glp_engine_embed", "glp_engine_stats",
     "glp_engine_destroy", "glp_tokenizer_from_gguf", "glp_tokenizer_from_vocab", "glp_tokenizer_free",
     "glp_tokenizer_info", "glp_tokenize", "glp_tokenize_batch", "glp_format_query", "glp_format_document",
-    "glp_task_format", "glp_embed_texts", "glp_engine_embed_text",
+    "glp_task_format", "glp_embed_texts", "glp_engine_embed_text", "glp_embed_tokens_sharded",
+    "glp_kernel_status", "glp_status_text", "glp_selftest_wait_timeout", "glp_gate_up_geglu",
+    "glp_qkv_norm_rope",
 )
 
 # sequence forms of a text (include/glypr_cuda.h GLP_TOKENS_*)
@@ -68,13 +70,13 @@ class GlyprError(RuntimeError):
 
 class GlpOptions(ctypes.Structure):
     _fields_ = [("max_batch_tokens", ctypes.c_int64), ("max_batch_seqs", ctypes.c_int),
-                ("reserved", ctypes.c_int * 6)]
+                ("device_memory_limit_mib", ctypes.c_int), ("reserved", ctypes.c_int * 5)]
 
 
 class GlpModelInfo(ctypes.Structure):
     _fields_ = [(n, ctypes.c_int) for n in (
         "n_layers", "hidden", "ffn", "n_heads", "n_kv_heads", "head_dim", "vocab", "embedding_dim",
-        "max_position", "sliding_window", "weight_type", "n_devices")]
+        "max_position", "sliding_window", "weight_type", "n_devices")] + [("device_bytes", ctypes.c_int64)]
 
 
 class GlpTiming(ctypes.Structure):
@@ -149,6 +151,13 @@ def load_library(path: Optional[str] = None) -> ctypes.CDLL:
         L.glp_task_format.argtypes = [CP, CP, CP, SZ, P, SZ, ctypes.POINTER(SZ)]
         L.glp_embed_texts.argtypes = [P, P, P, P, I, I, I, I, P]
         L.glp_engine_embed_text.argtypes = [P, P, CP, SZ, CP, CP, I, P]
+        L.glp_embed_tokens_sharded.argtypes = [P, P, I, I, P, P, I, I, I, P]
+        L.glp_kernel_status.argtypes = [I, ctypes.POINTER(I)]
+        L.glp_status_text.argtypes = [I]
+        L.glp_status_text.restype = ctypes.c_char_p
+        L.glp_selftest_wait_timeout.argtypes = [I, I]
+        L.glp_gate_up_geglu.argtypes = [P, P, I, I, P, I, P, P]
+        L.glp_qkv_norm_rope.argtypes = [P, I, I, I, P, I, P, P, P, ctypes.c_double, I, ctypes.c_float, P, P]
         _lib = L
         return L
 
@@ -212,11 +221,13 @@ class GlyprEmbedder:
     # reference: GlyprEmbedder::load_gguf(path, device) / load_gguf_q8 (lib.rs:176-229)
     @classmethod
     def load_gguf(cls, path: str, devices: Optional[Sequence[int]] = None,
-                  max_batch_tokens: int = 0, max_batch_seqs: int = 0) -> "GlyprEmbedder":
+                  max_batch_tokens: int = 0, max_batch_seqs: int = 0,
+                  device_memory_limit_mib: int = 0) -> "GlyprEmbedder":
         L = load_library()
         devs = list(devices) if devices is not None else []
         arr = (ctypes.c_int * max(1, len(devs)))(*devs) if devs else None
-        opt = GlpOptions(max_batch_tokens=max_batch_tokens, max_batch_seqs=max_batch_seqs)
+        opt = GlpOptions(max_batch_tokens=max_batch_tokens, max_batch_seqs=max_batch_seqs,
+                         device_memory_limit_mib=device_memory_limit_mib)
         out = ctypes.c_void_p()
         check(L.glp_open(path.encode(), arr, len(devs), ctypes.byref(opt), ctypes.byref(out)))
         return cls(out.value, path, devs or [-1])
@@ -369,9 +380,70 @@ def q8_0_gemm_noalloc(d_w: int, n: int, k: int, d_x: int, m: int, d_y: int, y_is
                                                ctypes.c_void_p(d_y), int(y_is_f32), ctypes.c_void_p(stream)))
 
 
+def kernel_status(device: int = 0) -> int:
+    """glp_kernel_status: read and clear the kernel-level entry points' status word (raises
+    GlyprError with GLP_ERR_DEVICE when a bounded wait expired)."""
+    st = ctypes.c_int(0)
+    check(load_library().glp_kernel_status(device, ctypes.byref(st)))
+    return st.value
+
+
+def status_text(status: int) -> str:
+    return load_library().glp_status_text(int(status)).decode()
+
+
+def selftest_wait_timeout(device: int = 0, limit_us: int = 1000) -> None:
+    """glp_selftest_wait_timeout: a kernel whose bounded wait runs out on purpose."""
+    check(load_library().glp_selftest_wait_timeout(device, limit_us))
+
+
+def embed_tokens_sharded(executors, embedding_dim: int, ids: np.ndarray, lengths: np.ndarray,
+                         out_dim: Optional[int] = None, out: Optional[np.ndarray] = None) -> np.ndarray:
+    """glp_embed_tokens_sharded over Python executors ``fn(ids, lengths, out_dim) -> [n, out_dim]``
+    (an executor fails its shard by raising)."""
+    ids = np.ascontiguousarray(ids, dtype=np.int32)
+    lengths = np.ascontiguousarray(lengths, dtype=np.int32)
+    n, s = ids.shape
+    od = int(out_dim or embedding_dim)
+    if out is None:
+        out = np.empty((n, od), dtype=np.float32)
+
+    def wrap(fn):
+        def trampoline(user, p_ids, p_lengths, m, max_len, o_dim, p_out):
+            try:
+                a = np.ctypeslib.as_array(p_ids, shape=(m * max(max_len, 1),)).reshape(m, max(max_len, 1))
+                lens = np.ctypeslib.as_array(p_lengths, shape=(m,))
+                res = np.asarray(fn(a[:, :max_len].copy(), lens.copy(), o_dim), dtype=np.float32)
+                np.ctypeslib.as_array(p_out, shape=(m * o_dim,))[:] = res.reshape(-1)
+                return GLP_OK
+            except Exception:
+                return GLP_ERR_INVALID_ARG
+        return BATCH_FN(trampoline)
+
+    keep = [wrap(f) for f in executors]
+    fns = (BATCH_FN * len(keep))(*keep)
+    check(load_library().glp_embed_tokens_sharded(ctypes.cast(fns, ctypes.c_void_p), None, len(keep),
+                                                  embedding_dim, _ptr(ids), _ptr(lengths), n, s, od, _ptr(out)))
+    return out
+
+
 def bf16_gemm(d_w: int, n: int, k: int, d_x: int, m: int, d_y: int, y_is_f32: bool, stream: int = 0) -> None:
     check(load_library().glp_bf16_gemm(ctypes.c_void_p(d_w), n, k, ctypes.c_void_p(d_x), m, ctypes.c_void_p(d_y),
                                        int(y_is_f32), ctypes.c_void_p(stream)))
+
+
+def gate_up_geglu(d_wg: int, d_wu: int, f: int, k: int, d_x: int, m: int, d_out: int, stream: int = 0) -> None:
+    check(load_library().glp_gate_up_geglu(ctypes.c_void_p(d_wg), ctypes.c_void_p(d_wu), f, k, ctypes.c_void_p(d_x),
+                                           m, ctypes.c_void_p(d_out), ctypes.c_void_p(stream)))
+
+
+def qkv_norm_rope(d_w: int, n_q_heads: int, n_kv_heads: int, k: int, d_x: int, m: int, d_q_gain: int,
+                  d_k_gain: int, d_pos: int, theta: float, max_pos: int, eps: float, d_out: int,
+                  stream: int = 0) -> None:
+    check(load_library().glp_qkv_norm_rope(ctypes.c_void_p(d_w), n_q_heads, n_kv_heads, k, ctypes.c_void_p(d_x), m,
+                                           ctypes.c_void_p(d_q_gain), ctypes.c_void_p(d_k_gain),
+                                           ctypes.c_void_p(d_pos), float(theta), max_pos, float(eps),
+                                           ctypes.c_void_p(d_out), ctypes.c_void_p(stream)))
 
 
 def flash_attention(d_qkv: int, d_cu: int, n_seq: int, max_len: int, n_q_heads: int, n_kv_heads: int,

@@ -25,6 +25,7 @@ enum : int {
   kErrTimeoutEpilogue = 3,
   kErrTimeoutDrain = 4,
   kErrBadArgs = 5,
+  kErrTimeoutSelfTest = 6,  // glp_selftest_wait_timeout: the expected expiry of a wait nobody ends
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -71,9 +72,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait for the phase with the given parity to complete.  Returns false on timeout
-// or when another role of the CTA has already aborted (*abort != 0).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+// Bounded wait for the phase with the given parity to complete.  Returns false after
+// limit_ns of %globaltimer or when another role of the CTA has already aborted (*abort != 0).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                          uint64_t limit_ns = GLP_WAIT_TIMEOUT_NS) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   while (true) {
@@ -81,7 +83,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     for (int i = 0; i < 32; ++i)
       if (mbar_try_wait(bar, parity)) return true;
     if (*abort) return false;
-    if (globaltimer() - t0 > GLP_WAIT_TIMEOUT_NS) return false;
+    if (globaltimer() - t0 > limit_ns) return false;
   }
 }
 

@@ -212,7 +212,8 @@ __device__ __forceinline__ bool gemm_epilogue_tile(const GemmParams& p, uint32_t
     const bool is_k = !is_q && n_blk < p.n_q_heads + p.n_kv_heads;
     const float* gain = is_q ? p.q_gain : (is_k ? p.k_gain : nullptr);
     const bool rope = is_q || is_k;
-    const int pos = live ? p.pos[row] : 0;
+    // positions outside the table read its last row instead of past its end
+    const int pos = live ? min(max(p.pos[row], 0), p.rope_stride - 1) : 0;
     // frequency-major {cos, sin} table: lanes (consecutive rows) read consecutive positions,
     // one 8-byte load per frequency
     const float2* tab = p.rope_cs + pos;

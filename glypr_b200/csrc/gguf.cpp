@@ -197,16 +197,31 @@ bool GgufFile::open(const char* path, std::string* err) {
   return true;
 }
 
+// Integer GGUF value types (u8, i8, u16, i16, u32, i32, u64, i64): the ones the reference's
+// get_u32 converts (config.rs:253-265, `v as u32`, wrapping negatives); any other type yields
+// no value, so the caller's default applies.
+static bool gguf_int_type(int t) { return (t >= 0 && t <= 5) || t == 10 || t == 11; }
+
+static uint32_t gguf_as_u32(double v) { return static_cast<uint32_t>(static_cast<int64_t>(v)); }
+
 bool GgufFile::get_u32(const std::string& key, uint32_t* out) const {
   const GgufValue* v = find(key);
-  if (!v || v->type == 8 || v->type == 9) return false;
-  *out = static_cast<uint32_t>(v->num);
+  if (!v || !gguf_int_type(v->type)) return false;
+  *out = gguf_as_u32(v->num);
   return true;
 }
 
+bool GgufFile::get_array_u32(const std::string& key, size_t i, uint32_t* out) const {
+  const GgufValue* v = find(key);
+  if (!v || v->type != 9 || i >= v->arr.size() || !gguf_int_type(v->arr_type)) return false;
+  *out = gguf_as_u32(v->arr[i]);
+  return true;
+}
+
+// f32 and f64 only (config.rs:274-280)
 bool GgufFile::get_f64(const std::string& key, double* out) const {
   const GgufValue* v = find(key);
-  if (!v || v->type == 8 || v->type == 9) return false;
+  if (!v || (v->type != 6 && v->type != 12)) return false;
   *out = v->num;
   return true;
 }

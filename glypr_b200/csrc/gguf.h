@@ -57,8 +57,12 @@ class GgufFile {
     auto it = tensors_.find(name);
     return it == tensors_.end() ? nullptr : &it->second;
   }
+  // scalar lookups with the reference's type rules (config.rs:253-280): false = no value
   bool get_u32(const std::string& key, uint32_t* out) const;
   bool get_f64(const std::string& key, double* out) const;
+  // element i of an integer array (false when the key is absent, not an array, i is past its
+  // end or its elements are not integers)
+  bool get_array_u32(const std::string& key, size_t i, uint32_t* out) const;
 
  private:
   void* map_ = nullptr;

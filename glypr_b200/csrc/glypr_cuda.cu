@@ -25,7 +25,6 @@
 #include <type_traits>
 #include <vector>
 
-#include "attention.cuh"
 #include "attention_tc.cuh"
 #include "gemm.cuh"
 #include "gguf.h"
@@ -98,46 +97,30 @@ int make_map16(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int
 
 int sm_count();
 
-// Attention engine: tcgen05 (default) or the warp-level mma.sync kernel (GLP_ATTENTION=mma).
-bool use_tc_attention() {
-  static const bool tc = [] {
-    const char* e = std::getenv("GLP_ATTENTION");
-    return !(e && std::string(e) == "mma");
-  }();
-  return tc;
-}
-
 // Launch attention over packed qkv rows [0, T) for n_seq sequences at cu (minus cu_base).
 int launch_attention(const __half* qkv, int64_t T, int qkv_width, const int* cu, int cu_base, int n_seq, int max_len,
                      int n_q_heads, int n_kv_heads, int window, __half* out, int* status, cudaStream_t st) {
   if (T <= 0 || n_seq <= 0 || max_len <= 0) return GLP_OK;
-  if (use_tc_attention()) {
-    CUtensorMap mq, mkv, mo;
-    GLP_TRY(make_map16(&mq, qkv, T, qkv_width, qkv_width, glp::kFaBQ, true));
-    GLP_TRY(make_map16(&mkv, qkv, T, qkv_width, qkv_width, glp::kFaBKV, true));
-    // output rows [T, Hq * 256]: bulk stores of 64 columns x 32 rows
-    GLP_TRY(make_map16(&mo, out, T, static_cast<int64_t>(n_q_heads) * glp::kFaD,
-                       static_cast<int64_t>(n_q_heads) * glp::kFaD, glp::kFaOutBoxRows, true));
-    glp::FaParams fp{};
-    fp.cu_seqlens = cu;
-    fp.cu_base = cu_base;
-    fp.n_seq = n_seq;
-    fp.q_blocks = (max_len + glp::kFaBQ - 1) / glp::kFaBQ;
-    fp.n_q_heads = n_q_heads;
-    fp.n_kv_heads = n_kv_heads;
-    fp.window = window;
-    fp.out = out;
-    fp.ld_out = n_q_heads * glp::kFaD;
-    fp.status = status;
-    const int64_t items = static_cast<int64_t>(n_seq) * fp.q_blocks * n_q_heads;
-    const int grid = static_cast<int>(std::min<int64_t>(items, sm_count()));  // persistent CTAs
-    glp::flash_attn_tc_kernel<<<grid, glp::kFaThreads, glp::kFaSmem, st>>>(mq, mkv, mo, fp);
-  } else {
-    const dim3 grid(static_cast<unsigned>((max_len + glp::kAttnBQ - 1) / glp::kAttnBQ), static_cast<unsigned>(n_q_heads),
-                    static_cast<unsigned>(n_seq));
-    glp::flash_attn_fwd_kernel<<<grid, glp::kAttnThreads, glp::kAttnSmem, st>>>(
-        qkv, qkv_width, cu, cu_base, n_q_heads, n_kv_heads, window, out, n_q_heads * glp::kAttnD);
-  }
+  CUtensorMap mq, mkv, mo;
+  GLP_TRY(make_map16(&mq, qkv, T, qkv_width, qkv_width, glp::kFaBQ, true));
+  GLP_TRY(make_map16(&mkv, qkv, T, qkv_width, qkv_width, glp::kFaBKV, true));
+  // output rows [T, Hq * 256]: bulk stores of 64 columns x 32 rows
+  GLP_TRY(make_map16(&mo, out, T, static_cast<int64_t>(n_q_heads) * glp::kFaD,
+                     static_cast<int64_t>(n_q_heads) * glp::kFaD, glp::kFaOutBoxRows, true));
+  glp::FaParams fp{};
+  fp.cu_seqlens = cu;
+  fp.cu_base = cu_base;
+  fp.n_seq = n_seq;
+  fp.q_blocks = (max_len + glp::kFaBQ - 1) / glp::kFaBQ;
+  fp.n_q_heads = n_q_heads;
+  fp.n_kv_heads = n_kv_heads;
+  fp.window = window;
+  fp.out = out;
+  fp.ld_out = n_q_heads * glp::kFaD;
+  fp.status = status;
+  const int64_t items = static_cast<int64_t>(n_seq) * fp.q_blocks * n_q_heads;
+  const int grid = static_cast<int>(std::min<int64_t>(items, sm_count()));  // persistent CTAs
+  glp::flash_attn_tc_kernel<<<grid, glp::kFaThreads, glp::kFaSmem, st>>>(mq, mkv, mo, fp);
   GLP_CUDA(cudaGetLastError());
   return GLP_OK;
 }
@@ -177,8 +160,6 @@ int ensure_kernel_attrs() {
   GLP_CUDA(cudaFuncSetAttribute(glp::gemm_rownorm_kernel<__half, 2>, A, static_cast<int>(glp::GemmRowCfgT<2>::SMEM)));
   GLP_CUDA(cudaFuncSetAttribute(glp::gemm_rownorm_kernel<__half, 3>, A, static_cast<int>(glp::GemmRowCfgT<3>::SMEM)));
   GLP_CUDA(cudaFuncSetAttribute(glp::gemm_rownorm_kernel<__half, 4>, A, static_cast<int>(glp::GemmRowCfgT<4>::SMEM)));
-  GLP_CUDA(cudaFuncSetAttribute(glp::flash_attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                static_cast<int>(glp::kAttnSmem)));
   GLP_CUDA(cudaFuncSetAttribute(glp::flash_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 static_cast<int>(glp::kFaSmem)));
   g_attr_done[dev] = true;
@@ -436,12 +417,14 @@ int parse_config(const glp::GgufFile& g, Config* c) {
       c->sliding[i] = (i + 1) % 6 != 0;
     }
   }
-  const glp::GgufValue* kv = g.find(a + "attention.head_count_kv");
-  c->n_kv = kv && kv->type == 9 && !kv->arr.empty() ? static_cast<int>(kv->arr[0]) : 2;
+  // config.rs:141-160: element 0 of head_count_kv (default 2) for the sliding layers, element
+  // i (default 1) for global layer i; an element that is not an integer takes the default
+  const std::string kv_key = a + "attention.head_count_kv";
+  c->n_kv = g.get_array_u32(kv_key, 0, &u) ? static_cast<int>(u) : 2;
   c->kv.assign(c->n_layers, c->n_kv);
   for (int i = 0; i < c->n_layers; ++i) {
     int kvi = c->n_kv;
-    if (!c->sliding[i]) kvi = kv && kv->type == 9 && i < static_cast<int>(kv->arr.size()) ? static_cast<int>(kv->arr[i]) : 1;
+    if (!c->sliding[i]) kvi = g.get_array_u32(kv_key, static_cast<size_t>(i), &u) ? static_cast<int>(u) : 1;
     const int hd = c->sliding[i] ? static_cast<int>(hd_swa) : static_cast<int>(hd_full);
     if (hd != static_cast<int>(hd_swa))
       return fail(GLP_ERR_UNSUPPORTED, "per-layer head_dim overrides are not supported (all layers must share head_dim)");
@@ -499,6 +482,7 @@ int validate_tensors(const glp::GgufFile& g, const Config& c) {
       GLP_TRY(need(p + "post_norm.weight", {H}, false));
       const glp::GgufTensor* s = g.tensor(p + "layer_output_scale.weight");
       if (!s) return fail(GLP_ERR_FORMAT, "missing tensor " + p + "layer_output_scale.weight");
+      if (s->type != glp::kGgmlF32 || s->numel() != 1) return fail(GLP_ERR_FORMAT, "bad layer_output_scale");
     } else if (g.tensor(p + "proj.weight") || g.tensor(p + "inp_gate.weight")) {
       return fail(GLP_ERR_FORMAT, "missing tensor per_layer_model_proj.weight");
     }
@@ -567,6 +551,9 @@ struct Device {
   cudaStream_t stream = nullptr;
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
   std::vector<void*> allocs;
+  // device memory this device's context holds (bytes requested from cudaMalloc, including the
+  // host-API staging buffers) and the caller's limit on it (0 = none)
+  int64_t bytes = 0, limit_bytes = 0;
   void* table = nullptr;
   uint32_t table_type = glp::kGgmlQ8_0;
   std::vector<LayerW> layers;
@@ -622,10 +609,34 @@ struct Device {
   std::vector<ChunkGraph> graphs;
   uint64_t graph_clock = 0;
 
+  // Reserve n bytes against the limit (GLP_ERR_OOM beyond it); release() gives them back.
+  int reserve(size_t n) {
+    if (limit_bytes > 0 && bytes + static_cast<int64_t>(n) > limit_bytes)
+      return fail(GLP_ERR_OOM, "device memory limit of " + std::to_string(limit_bytes >> 20) +
+                                   " MiB reached on device " + std::to_string(dev));
+    bytes += static_cast<int64_t>(n);
+    return GLP_OK;
+  }
+  int raw_malloc(void** v, size_t n) {
+    GLP_TRY(reserve(n));
+    const cudaError_t e = cudaMalloc(v, n);
+    if (e != cudaSuccess) {
+      bytes -= static_cast<int64_t>(n);
+      *v = nullptr;
+      return fail(e == cudaErrorMemoryAllocation ? GLP_ERR_OOM : GLP_ERR_CUDA,
+                  std::string("cudaMalloc: ") + cudaGetErrorString(e));
+    }
+    return GLP_OK;
+  }
+  void raw_free(void* v, size_t n) {
+    if (!v) return;
+    cudaFree(v);
+    bytes -= static_cast<int64_t>(n);
+  }
   template <class T>
   int alloc(T** p, size_t count) {
     void* v = nullptr;
-    GLP_CUDA(cudaMalloc(&v, std::max<size_t>(count, 1) * sizeof(T)));
+    GLP_TRY(raw_malloc(&v, std::max<size_t>(count, 1) * sizeof(T)));
     allocs.push_back(v);
     *p = static_cast<T*>(v);
     return GLP_OK;
@@ -638,6 +649,7 @@ struct Device {
     if (d_ids) cudaFree(d_ids);
     if (d_cu) cudaFree(d_cu);
     if (d_out) cudaFree(d_out);
+    bytes = 0;
     if (h_ids) cudaFreeHost(h_ids);
     if (h_cu) cudaFreeHost(h_cu);
     if (h_out) cudaFreeHost(h_out);
@@ -722,6 +734,7 @@ double visible_pairs(int64_t len, int w) {
 
 struct glp_ctx {
   Config cfg;
+  int64_t plan_bytes = 0;  // device memory each device's setup requests (device_plan_bytes)
   std::vector<std::unique_ptr<Device>> devs;
 };
 
@@ -802,6 +815,64 @@ int upload_rope(Device& d, double theta, int d_head, int max_pos, float2** cs) {
   return GLP_OK;
 }
 
+// Device staging for one linear's raw bytes while the weights upload: the largest linear.
+size_t load_staging_bytes(const glp::GgufFile& g, const Config& c) {
+  size_t n = 0;
+  for (const auto* nm : {"attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up", "ffn_down"}) {
+    const glp::GgufTensor* t = g.tensor(std::string("blk.0.") + nm + ".weight");
+    if (t) n = std::max(n, t->nbytes);
+  }
+  for (int j = 0;; ++j) {
+    const glp::GgufTensor* t = g.tensor("dense." + std::to_string(j) + ".weight");
+    if (!t) break;
+    n = std::max(n, t->nbytes);
+  }
+  if (const glp::GgufTensor* t = g.tensor("output.weight")) n = std::max(n, t->nbytes);
+  if (const glp::GgufTensor* t = g.tensor("per_layer_model_proj.weight")) n = std::max(n, t->nbytes);
+  for (const auto* nm : {"inp_gate", "proj"})
+    if (const glp::GgufTensor* t = g.tensor(std::string("blk.0.") + nm + ".weight")) n = std::max(n, t->nbytes);
+  return std::max(n, static_cast<size_t>(4) * c.ffn * std::max(c.hidden, c.ffn));
+}
+
+// Device memory setup_device requests per device (weights, RoPE tables, one launch chunk's
+// activations), without the load staging.  Computed from the file and the configuration
+// alone, so glp_open can hold it against the caller's limit before touching a device.
+int64_t device_plan_bytes(const glp::GgufFile& g, const Config& c, int64_t cap_tokens, int cap_seqs) {
+  const int64_t H = c.hidden, F = c.ffn, D = c.head_dim, AW = static_cast<int64_t>(c.n_heads) * D;
+  const int64_t T = cap_tokens, S = cap_seqs, PD = c.ple_dim;
+  auto b = [](int64_t count, int64_t elem) { return std::max<int64_t>(count, 1) * elem; };
+  int64_t n = b(static_cast<int64_t>(g.tensor("token_embd.weight")->nbytes), 1);
+  int64_t qkv_max = 0;
+  for (int l = 0; l < c.n_layers; ++l) {
+    const int64_t W = (c.n_heads + 2 * c.kv[l]) * D;
+    qkv_max = std::max(qkv_max, W);
+    n += 4 * b(H, 4) + 2 * b(D, 4);                                      // norm gains
+    n += b(W * H, 2) + b(H * AW, 2) + b(2 * F * H, 2) + b(H * F, 2);     // f16 linears
+    if (PD) n += b(H, 4) + b(PD * H, 2) + b(H * PD, 2);                  // PLE block
+  }
+  if (PD) n += b(PD, 4) + b(c.n_layers * PD * H, 2);
+  n += b(H, 4);  // output_norm
+  int64_t prev = H, max_head = H;
+  for (int j = 0;; ++j) {
+    const glp::GgufTensor* t = g.tensor("dense." + std::to_string(j) + ".weight");
+    if (!t) break;
+    n += b(t->ne[1] * prev, 2);
+    prev = t->ne[1];
+    max_head = std::max(max_head, prev);
+  }
+  if (!g.tensor("dense.0.weight")) {
+    const glp::GgufTensor* t = g.tensor("output.weight");
+    n += b(t->ne[1] * H, 2);
+    max_head = std::max(max_head, t->ne[1]);
+  }
+  n += 2 * b(static_cast<int64_t>(c.max_pos) * (D / 2), 8);  // RoPE tables
+  n += b(T * H, 2) + b(T * H, 4) + b(T * H, 2) + b(T * qkv_max, 2) + b(T * AW, 2) + b(T * H, 2) + b(T * F, 2);
+  if (PD) n += b(T * c.n_layers * PD, 2) + b(T * PD, 2);
+  n += b(T, 4) + b(S * max_head, 2) + b((T / glp::kPoolSeg + S + 1) * H, 4) + b(S * max_head, 2) +
+       b(S * max_head, 4) + b(1, 4);
+  return n;
+}
+
 int setup_device(Device& d, const Config& c, const glp::GgufFile& g, int64_t cap_tokens, int cap_seqs) {
   GLP_CUDA(cudaSetDevice(d.dev));
   GLP_TRY(ensure_kernel_attrs());
@@ -826,30 +897,16 @@ int setup_device(Device& d, const Config& c, const glp::GgufFile& g, int64_t cap
   GLP_CUDA(cudaMemcpy(table, te->data, te->nbytes, cudaMemcpyHostToDevice));
   d.table = table;
 
-  // staging for raw linear bytes: the largest linear
-  size_t staging_bytes = 0;
-  for (const auto* nm : {"attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up", "ffn_down"}) {
-    const glp::GgufTensor* t = g.tensor(std::string("blk.0.") + nm + ".weight");
-    if (t) staging_bytes = std::max(staging_bytes, t->nbytes);
-  }
-  for (int j = 0;; ++j) {
-    const glp::GgufTensor* t = g.tensor("dense." + std::to_string(j) + ".weight");
-    if (!t) break;
-    staging_bytes = std::max(staging_bytes, t->nbytes);
-  }
-  if (const glp::GgufTensor* t = g.tensor("output.weight")) staging_bytes = std::max(staging_bytes, t->nbytes);
-  if (const glp::GgufTensor* t = g.tensor("per_layer_model_proj.weight"))
-    staging_bytes = std::max(staging_bytes, t->nbytes);
-  for (const auto* nm : {"inp_gate", "proj"})
-    if (const glp::GgufTensor* t = g.tensor(std::string("blk.0.") + nm + ".weight"))
-      staging_bytes = std::max(staging_bytes, t->nbytes);
-  staging_bytes = std::max(staging_bytes, static_cast<size_t>(4) * F * std::max(H, F));
+  // staging for raw linear bytes: the largest linear (freed when the upload is done)
+  const size_t staging_bytes = load_staging_bytes(g, c);
   void* staging = nullptr;
-  GLP_CUDA(cudaMalloc(&staging, staging_bytes));
+  GLP_TRY(d.raw_malloc(&staging, staging_bytes));
   struct Free {
+    Device& d;
     void* p;
-    ~Free() { cudaFree(p); }
-  } free_staging{staging};
+    size_t n;
+    ~Free() { d.raw_free(p, n); }
+  } free_staging{d, staging, staging_bytes};
 
   d.layers.resize(c.n_layers);
   for (int l = 0; l < c.n_layers; ++l) {
@@ -1351,33 +1408,55 @@ int run_packed(const Config& c, Device& d, const int* d_ids, const int* d_cu, co
 
 int grow_staging(Device& d, int64_t tokens, int64_t seqs, int64_t outs) {
   if (tokens > d.stage_tokens) {
-    if (d.d_ids) cudaFree(d.d_ids);
+    d.raw_free(d.d_ids, std::max<int64_t>(d.stage_tokens, 1) * sizeof(int));
     if (d.h_ids) cudaFreeHost(d.h_ids);
     d.d_ids = nullptr;
     d.h_ids = nullptr;
-    GLP_CUDA(cudaMalloc(&d.d_ids, std::max<int64_t>(tokens, 1) * sizeof(int)));
+    d.stage_tokens = 0;
+    void* v = nullptr;
+    GLP_TRY(d.raw_malloc(&v, std::max<int64_t>(tokens, 1) * sizeof(int)));
+    d.d_ids = static_cast<int*>(v);
     GLP_CUDA(cudaHostAlloc(&d.h_ids, std::max<int64_t>(tokens, 1) * sizeof(int), cudaHostAllocDefault));
     d.stage_tokens = tokens;
   }
   if (seqs > d.stage_seqs) {
-    if (d.d_cu) cudaFree(d.d_cu);
+    d.raw_free(d.d_cu, (d.stage_seqs + 1) * sizeof(int));
     if (d.h_cu) cudaFreeHost(d.h_cu);
     d.d_cu = nullptr;
     d.h_cu = nullptr;
-    GLP_CUDA(cudaMalloc(&d.d_cu, (seqs + 1) * sizeof(int)));
+    d.stage_seqs = 0;
+    void* v = nullptr;
+    GLP_TRY(d.raw_malloc(&v, (seqs + 1) * sizeof(int)));
+    d.d_cu = static_cast<int*>(v);
     GLP_CUDA(cudaHostAlloc(&d.h_cu, (seqs + 1) * sizeof(int), cudaHostAllocDefault));
     d.stage_seqs = seqs;
   }
   if (outs > d.stage_out) {
-    if (d.d_out) cudaFree(d.d_out);
+    d.raw_free(d.d_out, std::max<int64_t>(d.stage_out, 1) * sizeof(float));
     if (d.h_out) cudaFreeHost(d.h_out);
     d.d_out = nullptr;
     d.h_out = nullptr;
-    GLP_CUDA(cudaMalloc(&d.d_out, std::max<int64_t>(outs, 1) * sizeof(float)));
+    d.stage_out = 0;
+    void* v = nullptr;
+    GLP_TRY(d.raw_malloc(&v, std::max<int64_t>(outs, 1) * sizeof(float)));
+    d.d_out = static_cast<float*>(v);
     GLP_CUDA(cudaHostAlloc(&d.h_out, std::max<int64_t>(outs, 1) * sizeof(float), cudaHostAllocDefault));
     d.stage_out = outs;
   }
   return GLP_OK;
+}
+
+const char* status_text(int code) {
+  switch (code) {
+    case glp::kErrNone: return "no device error";
+    case glp::kErrTimeoutProducer: return "a TMA producer's wait for a free pipeline stage timed out";
+    case glp::kErrTimeoutMma: return "the MMA issuer's wait for operands or a free accumulator timed out";
+    case glp::kErrTimeoutEpilogue: return "an epilogue wait (accumulator, row exchange or load) timed out";
+    case glp::kErrTimeoutDrain: return "the wait for the last MMAs to retire timed out";
+    case glp::kErrBadArgs: return "a kernel found its shared memory misaligned and did no work";
+    case glp::kErrTimeoutSelfTest: return "the self-test's wait on a barrier nobody arrives at ran out, as intended";
+    default: return "unknown device status code";
+  }
 }
 
 int check_status(Device& d) {
@@ -1385,14 +1464,17 @@ int check_status(Device& d) {
   GLP_CUDA(cudaMemcpy(&st, d.status, sizeof(int), cudaMemcpyDeviceToHost));
   if (st != 0) {
     cudaMemset(d.status, 0, sizeof(int));
-    return fail(GLP_ERR_DEVICE, "device pipeline wait timed out (status " + std::to_string(st) + ")");
+    return fail(GLP_ERR_DEVICE, "device pipeline wait timed out (status " + std::to_string(st) + ": " +
+                                    status_text(st) + ")");
   }
   return GLP_OK;
 }
 
-// Host-API shard on one device: pack, H2D, forward, D2H (all on the device's stream).
+// Host-API shard on one device: pack, H2D, forward, D2H (all on the device's stream).  The
+// embeddings stay in the device's pinned staging buffer (d.h_out); the caller copies them out
+// once every shard has succeeded, so a failed call leaves the caller's buffer untouched.
 int run_shard(const Config& c, Device& d, const int32_t* ids, const int32_t* lengths, int s0, int s1, int max_len,
-              int out_dim, float* out, float* ms) {
+              int out_dim, float* ms) {
   GLP_CUDA(cudaSetDevice(d.dev));
   const int n = s1 - s0;
   int64_t tokens = 0;
@@ -1417,8 +1499,44 @@ int run_shard(const Config& c, Device& d, const int32_t* ids, const int32_t* len
   GLP_CUDA(cudaStreamSynchronize(st));
   GLP_TRY(check_status(d));
   if (ms) cudaEventElapsedTime(ms, d.ev0, d.ev1);
-  std::memcpy(out + static_cast<size_t>(s0) * out_dim, d.h_out, static_cast<size_t>(n) * out_dim * sizeof(float));
   return GLP_OK;
+}
+
+// Contiguous shards [bounds[i], bounds[i+1]) of n_seq sequences for nd workers, balanced by
+// token count (total = sum of lengths).
+std::vector<int> shard_bounds(const int32_t* lengths, int n_seq, int nd, int64_t total) {
+  std::vector<int> bounds(nd + 1, n_seq);
+  bounds[0] = 0;
+  int64_t acc = 0;
+  int k = 1;
+  for (int i = 0; i < n_seq && k < nd; ++i) {
+    acc += lengths[i];
+    while (k < nd && acc * nd >= total * k) bounds[k++] = i + 1;
+  }
+  for (; k < nd; ++k) bounds[k] = n_seq;
+  return bounds;
+}
+
+// work(i) for every worker i in [0, nd): one host thread each (the calling thread alone when
+// nd == 1, or for the workers no thread could be created for); the caller's current device is
+// restored afterwards.
+template <class Work>
+void run_shards(int nd, Work&& work, bool cuda_workers = true) {
+  int prev = 0;
+  if (cuda_workers) cudaGetDevice(&prev);
+  if (nd == 1) {
+    work(0);
+  } else {
+    std::vector<std::thread> th;
+    int spawned = 0;
+    try {
+      for (; spawned < nd; ++spawned) th.emplace_back(work, spawned);
+    } catch (const std::exception&) {  // no more threads: the calling thread runs the other shards
+      for (int i = spawned; i < nd; ++i) work(i);
+    }
+    for (auto& t : th) t.join();
+  }
+  if (cuda_workers) cudaSetDevice(prev);
 }
 
 // ------------------------------------------------------------------------------ kernel-level scratch
@@ -1427,8 +1545,47 @@ struct Scratch {
   std::array<__nv_bfloat16*, 64> w{};
   std::array<size_t, 64> cap{};
   std::array<int*, 64> status{};
+  std::array<__half*, 64> gu{};  // glp_gate_up_geglu's interleaved weight
+  std::array<size_t, 64> gu_cap{};
+  struct Rope {
+    int dev;
+    double theta;
+    int max_pos;
+    float2* cs;
+  };
+  std::vector<Rope> rope;  // glp_qkv_norm_rope's tables, kept per (device, theta, max_pos)
 };
 Scratch g_scratch;
+
+// RoPE table of head_dim 256 for (theta, max_pos) on the current device, built once (the
+// values of rope.rs:14-76, the layout of upload_rope) and kept until the process exits.
+int kernel_rope_table(int dev, double theta, int max_pos, const float2** out) {
+  std::lock_guard<std::mutex> lk(g_scratch.mu);
+  for (const auto& r : g_scratch.rope)
+    if (r.dev == dev && r.theta == theta && r.max_pos == max_pos) {
+      *out = r.cs;
+      return GLP_OK;
+    }
+  constexpr int kHalf = 128;
+  std::vector<float> inv(kHalf);
+  for (int i = 0; i < kHalf; ++i) inv[i] = static_cast<float>(1.0 / std::pow(theta, (2.0 * i) / 256.0));
+  std::vector<float2> c(static_cast<size_t>(max_pos) * kHalf);
+  for (int i = 0; i < kHalf; ++i)
+    for (int p = 0; p < max_pos; ++p) {
+      const float f = static_cast<float>(p) * inv[i];
+      c[static_cast<size_t>(i) * max_pos + p] = make_float2(std::cos(f), std::sin(f));
+    }
+  float2* cs = nullptr;
+  GLP_CUDA(cudaMalloc(&cs, c.size() * sizeof(float2)));
+  const cudaError_t e = cudaMemcpy(cs, c.data(), c.size() * sizeof(float2), cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    cudaFree(cs);
+    return fail(GLP_ERR_CUDA, std::string("RoPE table upload: ") + cudaGetErrorString(e));
+  }
+  g_scratch.rope.push_back({dev, theta, max_pos, cs});
+  *out = cs;
+  return GLP_OK;
+}
 
 int device_status_word(int dev, int** out) {
   std::lock_guard<std::mutex> lk(g_scratch.mu);
@@ -1466,6 +1623,22 @@ int run_bf16_gemm(const __nv_bfloat16* w, int N, int K, const void* x, int M, vo
 }
 
 }  // namespace
+
+// ------------------------------------------------------------------------------ bounded-wait self-test
+// One thread waits, with the kernels' bounded wait, on an mbarrier that nobody arrives at: the
+// wait must run out after limit_ns and record kErrTimeoutSelfTest in the status word, and the
+// kernel returns normally (no trap, no fault), so the context stays usable.
+__global__ void wait_selftest_kernel(uint64_t limit_ns, int* status) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    glp::mbar_init(&bar, 1);
+    abort_flag = 0;
+    glp::fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && !glp::mbar_wait(&bar, 0, &abort_flag, limit_ns)) glp::record_error(status, glp::kErrTimeoutSelfTest);
+}
 
 // ------------------------------------------------------------------------------ no-allocation GEMM
 // glp_q8_0_gemm_noalloc keeps its dequantised weight in this file-scope device array instead
@@ -1528,6 +1701,15 @@ int glp_open(const char* gguf_path, const int* device_ids, int n_devices, const 
   int64_t cap_tokens = opt && opt->max_batch_tokens > 0 ? opt->max_batch_tokens : 262144;
   cap_tokens = std::max<int64_t>(cap_tokens, ctx->cfg.max_pos);
   const int cap_seqs = opt && opt->max_batch_seqs > 0 ? opt->max_batch_seqs : 4096;
+  // the caller's device-memory limit, checked against the plan before any device is touched
+  ctx->plan_bytes = device_plan_bytes(g, ctx->cfg, cap_tokens, cap_seqs);
+  const int64_t limit = opt && opt->device_memory_limit_mib > 0 ? static_cast<int64_t>(opt->device_memory_limit_mib) << 20 : 0;
+  const int64_t peak = ctx->plan_bytes + static_cast<int64_t>(load_staging_bytes(g, ctx->cfg));
+  if (limit > 0 && peak > limit)
+    return fail(GLP_ERR_OOM, "the model needs " + std::to_string((peak + (1 << 20) - 1) >> 20) +
+                                 " MiB of device memory per device (weights, RoPE tables and one launch chunk of " +
+                                 std::to_string(cap_tokens) + " tokens), above the limit of " +
+                                 std::to_string(opt->device_memory_limit_mib) + " MiB");
   std::vector<int> ids;
   if (n_devices == 0 || !device_ids) {
     int cur = 0;
@@ -1545,6 +1727,7 @@ int glp_open(const char* gguf_path, const int* device_ids, int n_devices, const 
   for (int id : ids) {
     auto d = std::make_unique<Device>();
     d->dev = id;
+    d->limit_bytes = limit;
     const int rc = setup_device(*d, ctx->cfg, g, cap_tokens, cap_seqs);
     if (rc != GLP_OK) {
       const std::string keep = t_err;
@@ -1553,6 +1736,14 @@ int glp_open(const char* gguf_path, const int* device_ids, int n_devices, const 
       cudaSetDevice(prev);
       t_err = keep;
       return rc;
+    }
+    if (d->bytes != ctx->plan_bytes) {  // the plan the limit is checked against must be exact
+      const std::string msg = "device memory plan " + std::to_string(ctx->plan_bytes) + " B differs from the " +
+                              std::to_string(d->bytes) + " B allocated";
+      d->release();
+      for (auto& e : ctx->devs) e->release();
+      cudaSetDevice(prev);
+      return fail(GLP_ERR_CUDA, msg);
     }
     ctx->devs.push_back(std::move(d));
   }
@@ -1585,6 +1776,7 @@ int glp_model_info(const glp_ctx* ctx, glp_model_info_t* info) {
   info->sliding_window = c.window;
   info->weight_type = static_cast<int>(c.linear_type);
   info->n_devices = static_cast<int>(ctx->devs.size());
+  info->device_bytes = ctx->devs.empty() ? ctx->plan_bytes : ctx->devs[0]->bytes;
   return GLP_OK;
 }
 
@@ -1614,48 +1806,71 @@ int glp_embed_tokens(glp_ctx* ctx, const int32_t* ids, const int32_t* lengths, i
     for (int i = 0; i < GLP_MAX_DEVICES; ++i) timing->device_ms[i] = 0.f;
   }
   if (n_seq == 0) return GLP_OK;
-  // contiguous shards balanced by token count
-  std::vector<int> bounds(nd + 1, n_seq);
-  bounds[0] = 0;
-  {
-    int64_t acc = 0;
-    int k = 1;
-    for (int i = 0; i < n_seq && k < nd; ++i) {
-      acc += lengths[i];
-      while (k < nd && acc * nd >= total * k) bounds[k++] = i + 1;
-    }
-    for (; k < nd; ++k) bounds[k] = n_seq;
-  }
+  const std::vector<int> bounds = shard_bounds(lengths, n_seq, nd, total);
   std::vector<int> rcs(nd, GLP_OK);
   std::vector<std::string> errs(nd);
   std::vector<float> ms(nd, 0.f);
-  auto work = [&](int i) {
+  run_shards(nd, [&](int i) {
     if (bounds[i] >= bounds[i + 1]) return;
-    rcs[i] = run_shard(c, *ctx->devs[i], ids, lengths, bounds[i], bounds[i + 1], max_len, out_dim, out, &ms[i]);
+    rcs[i] = run_shard(c, *ctx->devs[i], ids, lengths, bounds[i], bounds[i + 1], max_len, out_dim, &ms[i]);
     if (rcs[i] != GLP_OK) errs[i] = t_err;
-  };
-  if (nd == 1) {
-    int prev = 0;
-    cudaGetDevice(&prev);
-    work(0);
-    cudaSetDevice(prev);
-  } else {
-    std::vector<std::thread> th;
-    int spawned = 0;
-    try {
-      for (; spawned < nd; ++spawned) th.emplace_back(work, spawned);
-    } catch (const std::exception&) {  // no more threads: the calling thread runs the other shards
-      int prev = 0;
-      cudaGetDevice(&prev);
-      for (int i = spawned; i < nd; ++i) work(i);
-      cudaSetDevice(prev);
-    }
-    for (auto& t : th) t.join();
-  }
+  });
   for (int i = 0; i < nd; ++i) {
     if (timing && i < GLP_MAX_DEVICES) timing->device_ms[i] = ms[i];
     if (rcs[i] != GLP_OK) return fail(rcs[i], "device " + std::to_string(ctx->devs[i]->dev) + ": " + errs[i]);
   }
+  // every shard succeeded: only now do the embeddings reach the caller's buffer
+  for (int i = 0; i < nd; ++i)
+    if (bounds[i] < bounds[i + 1])
+      std::memcpy(out + static_cast<size_t>(bounds[i]) * out_dim, ctx->devs[i]->h_out,
+                  static_cast<size_t>(bounds[i + 1] - bounds[i]) * out_dim * sizeof(float));
+  return GLP_OK;
+}
+
+int glp_embed_tokens_sharded(const glp_batch_fn* fns, void* const* users, int n_executors, int embedding_dim,
+                             const int32_t* ids, const int32_t* lengths, int n_seq, int max_len, int out_dim,
+                             float* out) {
+  if (!fns || n_executors <= 0 || n_executors > GLP_MAX_DEVICES) return fail(GLP_ERR_INVALID_ARG, "bad executor list");
+  for (int i = 0; i < n_executors; ++i)
+    if (!fns[i]) return fail(GLP_ERR_INVALID_ARG, "NULL executor");
+  if (n_seq < 0 || max_len < 0) return fail(GLP_ERR_INVALID_ARG, "negative batch shape");
+  if (n_seq > 0 && (!ids || !lengths || !out)) return fail(GLP_ERR_INVALID_ARG, "NULL buffer");
+  if (out_dim <= 0 || out_dim > embedding_dim)
+    return fail(GLP_ERR_INVALID_ARG, "out_dim must be in (0, " + std::to_string(embedding_dim) + "]");
+  int64_t total = 0;
+  for (int i = 0; i < n_seq; ++i) {
+    if (lengths[i] < 0 || lengths[i] > max_len) return fail(GLP_ERR_INVALID_ARG, "length out of [0, max_len]");
+    total += lengths[i];
+  }
+  if (n_seq == 0) return GLP_OK;
+  const int nd = n_executors;
+  const std::vector<int> bounds = shard_bounds(lengths, n_seq, nd, total);
+  std::vector<int> rcs(nd, GLP_OK);
+  std::vector<std::string> errs(nd);
+  std::vector<std::vector<float>> part(nd);
+  run_shards(
+      nd,
+      [&](int i) {
+        const int s0 = bounds[i], s1 = bounds[i + 1];
+        if (s0 >= s1) return;
+        try {
+          part[i].assign(static_cast<size_t>(s1 - s0) * out_dim, 0.f);
+        } catch (const std::exception&) {
+          rcs[i] = GLP_ERR_OOM;
+          errs[i] = "out of host memory";
+          return;
+        }
+        t_err.clear();
+        rcs[i] = fns[i](users ? users[i] : nullptr, ids + static_cast<int64_t>(s0) * max_len, lengths + s0, s1 - s0,
+                        max_len, out_dim, part[i].data());
+        if (rcs[i] != GLP_OK) errs[i] = t_err.empty() ? "executor failed with status " + std::to_string(rcs[i]) : t_err;
+      },
+      false);
+  for (int i = 0; i < nd; ++i)
+    if (rcs[i] != GLP_OK) return fail(rcs[i], "executor " + std::to_string(i) + ": " + errs[i]);
+  for (int i = 0; i < nd; ++i)
+    if (bounds[i] < bounds[i + 1]) std::memcpy(out + static_cast<size_t>(bounds[i]) * out_dim, part[i].data(),
+                                               part[i].size() * sizeof(float));
   return GLP_OK;
 }
 
@@ -1789,7 +2004,7 @@ int glp_bf16_gemm(const void* d_w_bf16, int N, int K, const void* d_x_bf16, int 
 
 int glp_flash_attention(const void* d_qkv, const int32_t* d_cu_seqlens, int n_seq, int max_len, int n_q_heads,
                         int n_kv_heads, int head_dim, int window, void* d_out, void* stream) {
-  if (head_dim != glp::kAttnD) return fail(GLP_ERR_UNSUPPORTED, "head_dim must be 256");
+  if (head_dim != glp::kFaD) return fail(GLP_ERR_UNSUPPORTED, "head_dim must be 256");
   if (n_seq < 0 || max_len < 0 || n_q_heads <= 0 || n_kv_heads <= 0 || n_q_heads % n_kv_heads)
     return fail(GLP_ERR_INVALID_ARG, "bad attention shape");
   if (n_seq == 0 || max_len == 0) return GLP_OK;
@@ -1833,9 +2048,12 @@ int glp_q8_0_gemm_noalloc(const void* d_q8_w, int N, int K, const void* d_x_bf16
       static_cast<const uint8_t*>(d_q8_w), N, K, w, 0, 0, 0);
   GLP_CUDA(cudaGetLastError());
   const int bn = bn_for(N);
-  CUtensorMap ma, mb;
+  // tensor maps are host-side descriptors: building them allocates no device memory; with the
+  // 128-row map the GEMM runs the same kernel (CTA pairs or single CTAs) as glp_q8_0_gemm
+  CUtensorMap ma, mb, mbp;
   GLP_TRY(make_map16(&ma, d_x_bf16, M, K, K, 128, false));
   GLP_TRY(make_map16(&mb, w, N, K, K, bn, false));
+  GLP_TRY(make_map16(&mbp, w, N, K, K, 128, false));
   GemmParams p{};
   p.M = M;
   p.N = N;
@@ -1843,7 +2061,163 @@ int glp_q8_0_gemm_noalloc(const void* d_q8_w, int N, int K, const void* d_x_bf16
   p.C = d_y;
   p.ldc = N;
   p.status = status;
-  return launch_gemm<__nv_bfloat16>(ma, mb, bn, y_is_f32 ? glp::kEpiF32 : glp::kEpiStore16, p, st);
+  return launch_gemm<__nv_bfloat16>(ma, mb, bn, y_is_f32 ? glp::kEpiF32 : glp::kEpiStore16, p, st, &mbp);
+}
+
+const char* glp_status_text(int status) { return status_text(status); }
+
+int glp_kernel_status(int device, int* status) {
+  if (!status) return fail(GLP_ERR_INVALID_ARG, "status is NULL");
+  *status = 0;
+  int n = 0;
+  GLP_CUDA(cudaGetDeviceCount(&n));
+  if (device < 0 || device >= n || device >= 64) return fail(GLP_ERR_INVALID_ARG, "device index out of range");
+  int prev = 0;
+  cudaGetDevice(&prev);
+  GLP_CUDA(cudaSetDevice(device));
+  int code = 0;
+  const cudaError_t se = cudaDeviceSynchronize();
+  int* word = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_scratch.mu);
+    word = g_scratch.status[device];
+  }
+  cudaError_t e = se;
+  if (e == cudaSuccess && word) {
+    int v = 0;
+    e = cudaMemcpy(&v, word, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && v != 0) e = cudaMemset(word, 0, sizeof(int));
+    if (v != 0) code = v;
+  }
+  bool noalloc_used = false;
+  {
+    std::lock_guard<std::mutex> lk(g_noalloc_ptrs.mu);
+    noalloc_used = g_noalloc_ptrs.status[device] != nullptr;
+  }
+  if (e == cudaSuccess && noalloc_used) {  // symbol copies: nothing is allocated
+    int v = 0;
+    e = cudaMemcpyFromSymbol(&v, g_noalloc_status, sizeof(int));
+    if (e == cudaSuccess && v != 0) {
+      const int zero = 0;
+      e = cudaMemcpyToSymbol(g_noalloc_status, &zero, sizeof(int));
+      if (code == 0) code = v;
+    }
+  }
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) return fail(GLP_ERR_CUDA, std::string("reading the kernel status: ") + cudaGetErrorString(e));
+  *status = code;
+  if (code != 0)
+    return fail(GLP_ERR_DEVICE, "device status " + std::to_string(code) + ": " + status_text(code));
+  return GLP_OK;
+}
+
+int glp_selftest_wait_timeout(int device, int limit_us) {
+  if (limit_us <= 0 || limit_us > 2000000) return fail(GLP_ERR_INVALID_ARG, "limit_us must be in (0, 2000000]");
+  int n = 0;
+  GLP_CUDA(cudaGetDeviceCount(&n));
+  if (device < 0 || device >= n || device >= 64) return fail(GLP_ERR_INVALID_ARG, "device index out of range");
+  int prev = 0;
+  cudaGetDevice(&prev);
+  GLP_CUDA(cudaSetDevice(device));
+  int* status = nullptr;
+  int rc = device_status_word(device, &status);
+  if (rc == GLP_OK) {
+    wait_selftest_kernel<<<1, 32>>>(static_cast<uint64_t>(limit_us) * 1000ull, status);
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) rc = fail(GLP_ERR_CUDA, std::string("self-test kernel: ") + cudaGetErrorString(e));
+  }
+  cudaSetDevice(prev);
+  return rc;
+}
+
+int glp_gate_up_geglu(const void* d_w_gate, const void* d_w_up, int F, int K, const void* d_x, int M, void* d_out,
+                      void* stream) {
+  if (F <= 0 || K <= 0 || M < 0 || F % 128 || K % 64)
+    return fail(GLP_ERR_INVALID_ARG, "gate/up GEMM needs F % 128 == 0, K % 64 == 0, M >= 0");
+  if (!d_w_gate || !d_w_up || !d_x || !d_out) return fail(GLP_ERR_INVALID_ARG, "null pointer");
+  GLP_TRY(ensure_kernel_attrs());
+  int dev = 0;
+  GLP_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(GLP_ERR_INVALID_ARG, "device index out of range");
+  int* status = nullptr;
+  GLP_TRY(device_status_word(dev, &status));
+  if (M == 0) return GLP_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  __half* gu = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_scratch.mu);
+    const size_t need = static_cast<size_t>(2) * F * K;
+    if (g_scratch.gu_cap[dev] < need) {
+      if (g_scratch.gu[dev]) {
+        cudaDeviceSynchronize();
+        cudaFree(g_scratch.gu[dev]);
+        g_scratch.gu[dev] = nullptr;
+        g_scratch.gu_cap[dev] = 0;
+      }
+      GLP_CUDA(cudaMalloc(&g_scratch.gu[dev], need * sizeof(__half)));
+      g_scratch.gu_cap[dev] = need;
+    }
+    gu = g_scratch.gu[dev];
+  }
+  // the model path's layout: tile t of 256 rows = [gate rows 128t.. | up rows 128t..]
+  const size_t blk = static_cast<size_t>(128) * K * sizeof(__half);
+  GLP_CUDA(cudaMemcpy2DAsync(gu, 2 * blk, d_w_gate, blk, blk, F / 128, cudaMemcpyDeviceToDevice, st));
+  GLP_CUDA(cudaMemcpy2DAsync(reinterpret_cast<uint8_t*>(gu) + blk, 2 * blk, d_w_up, blk, blk, F / 128,
+                             cudaMemcpyDeviceToDevice, st));
+  CUtensorMap ma, mb, mbp;
+  GLP_TRY(make_map16(&ma, d_x, M, K, K, 128, true));
+  GLP_TRY(make_map16(&mb, gu, 2 * F, K, K, 256, true));
+  GLP_TRY(make_map16(&mbp, gu, 2 * F, K, K, 128, true));
+  GemmParams p{};
+  p.M = M;
+  p.N = 2 * F;
+  p.K = K;
+  p.C = d_out;
+  p.ldc = F;
+  p.status = status;
+  return launch_gemm<__half>(ma, mb, 256, glp::kEpiGeglu, p, st, &mbp);
+}
+
+int glp_qkv_norm_rope(const void* d_w_qkv, int n_q_heads, int n_kv_heads, int K, const void* d_x, int M,
+                      const float* d_q_gain, const float* d_k_gain, const int32_t* d_pos, double theta, int max_pos,
+                      float eps, void* d_out, void* stream) {
+  if (n_q_heads <= 0 || n_kv_heads <= 0 || K <= 0 || K % 64 || M < 0 || max_pos <= 0 || !(theta > 0.0))
+    return fail(GLP_ERR_INVALID_ARG, "QKV GEMM needs heads > 0, K % 64 == 0, M >= 0, max_pos > 0, theta > 0");
+  if (!d_w_qkv || !d_x || !d_q_gain || !d_k_gain || !d_pos || !d_out) return fail(GLP_ERR_INVALID_ARG, "null pointer");
+  if ((reinterpret_cast<uintptr_t>(d_q_gain) | reinterpret_cast<uintptr_t>(d_k_gain)) & 15)
+    return fail(GLP_ERR_INVALID_ARG, "gains must be 16-byte aligned");
+  GLP_TRY(ensure_kernel_attrs());
+  int dev = 0;
+  GLP_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(GLP_ERR_INVALID_ARG, "device index out of range");
+  int* status = nullptr;
+  GLP_TRY(device_status_word(dev, &status));
+  if (M == 0) return GLP_OK;
+  const float2* cs = nullptr;
+  GLP_TRY(kernel_rope_table(dev, theta, max_pos, &cs));
+  const int W = (n_q_heads + 2 * n_kv_heads) * glp::kFaD;
+  CUtensorMap ma, mb, mbp, mc;
+  GLP_TRY(make_map16(&ma, d_x, M, K, K, 128, true));
+  GLP_TRY(make_map16(&mb, d_w_qkv, W, K, K, 256, true));
+  GLP_TRY(make_map16(&mbp, d_w_qkv, W, K, K, 128, true));
+  GLP_TRY(make_map16(&mc, d_out, M, W, W, 32, true));
+  GemmParams p{};
+  p.M = M;
+  p.N = W;
+  p.K = K;
+  p.C = d_out;
+  p.ldc = W;
+  p.q_gain = d_q_gain;
+  p.k_gain = d_k_gain;
+  p.rope_cs = cs;
+  p.pos = d_pos;
+  p.rope_stride = max_pos;
+  p.n_q_heads = n_q_heads;
+  p.n_kv_heads = n_kv_heads;
+  p.eps = eps;
+  p.status = status;
+  return launch_gemm<__half>(ma, mb, 256, glp::kEpiQkv, p, static_cast<cudaStream_t>(stream), &mbp, &mc);
 }
 
 }  // extern "C"

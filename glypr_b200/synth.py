@@ -192,6 +192,8 @@ def _kv(key: str, vtype: int, value) -> bytes:
             out += np.asarray(items, dtype="<u4").tobytes()
         elif etype == _BOOL:
             out += np.asarray(items, dtype=np.uint8).tobytes()
+        elif etype == _F32:
+            out += np.asarray(items, dtype="<f4").tobytes()
         elif etype == _STR:
             out += b"".join(_gstr(s) for s in items)
         else:
@@ -199,6 +201,15 @@ def _kv(key: str, vtype: int, value) -> bytes:
     else:
         raise ValueError(vtype)
     return out
+
+
+def gguf_kv(key: str, vtype: str, value) -> bytes:
+    """One encoded GGUF key/value for write_gguf's ``extra_kv``: vtype "u32", "f32", "f64",
+    "str", "bool", or "arr_u32" / "arr_f32" / "arr_bool" with a list value."""
+    if vtype.startswith("arr_"):
+        et = {"u32": _U32, "f32": _F32, "bool": _BOOL}[vtype[4:]]
+        return _kv(key, _ARR, (et, value))
+    return _kv(key, {"u32": _U32, "f32": _F32, "f64": _F64, "str": _STR, "bool": _BOOL}[vtype], value)
 
 
 def _kv_key(kv: bytes) -> str:
@@ -323,16 +334,20 @@ def _nbytes(shape, ggml_type) -> int:
 def write_gguf(path: str, cfg: EncoderConfig = BASELINE, seed: int = MASTER_SEED,
                drop: Iterable[str] = (), extra_f32: Sequence[Tuple[str, Tuple[int, ...]]] = (),
                f32_mats: Iterable[str] = (),
-               tokenizer: Optional[Tuple[Sequence[str], Sequence[str]]] = None) -> str:
+               tokenizer: Optional[Tuple[Sequence[str], Sequence[str]]] = None,
+               extra_kv: Sequence[bytes] = (), f32_scalars: Iterable[str] = ()) -> str:
     """Write the synthetic encoder to ``path`` (returns ``path``).
 
     ``drop`` omits metadata keys or tensors by name, ``extra_f32`` appends zero F32 tensors
     and ``f32_mats`` stores the named matrices as F32 instead of Q8_0/BF16 -- used by the
-    host-side fault-injection tests to build malformed files; ``tokenizer`` = (tokens,
-    merges) writes a BPE vocabulary into the tokenizer keys."""
+    host-side fault-injection tests to build malformed files; ``extra_kv`` appends encoded
+    key/values (``gguf_kv``; with ``drop`` of the same key it replaces one) and
+    ``f32_scalars`` stores the named one-element tensors with two elements (a malformed layer
+    scalar); ``tokenizer`` = (tokens, merges) writes a BPE vocabulary into the tokenizer keys."""
     drop = set(drop)
     f32_mats = set(f32_mats)
-    order = [o for o in _tensor_order(cfg) if o[0] not in drop]
+    f32_scalars = set(f32_scalars)
+    order = [(n, (2,) if n in f32_scalars else sh, k) for n, sh, k in _tensor_order(cfg) if n not in drop]
     order_idx = {n: i for i, (n, _, _) in enumerate(_tensor_order(cfg))}
     mat_type = GGML_Q8_0 if cfg.weight_type == "q8_0" else GGML_BF16
     infos = []
@@ -347,7 +362,7 @@ def write_gguf(path: str, cfg: EncoderConfig = BASELINE, seed: int = MASTER_SEED
         order.append((name, shape, "zero"))
         offset += _nbytes(shape, GGML_F32)
         offset = (offset + ALIGNMENT - 1) // ALIGNMENT * ALIGNMENT
-    kvs = [kv for kv in metadata(cfg, tokenizer) if _kv_key(kv) not in drop]
+    kvs = [kv for kv in metadata(cfg, tokenizer) if _kv_key(kv) not in drop] + list(extra_kv)
     header = struct.pack("<IIQQ", GGUF_MAGIC, GGUF_VERSION, len(infos), len(kvs)) + b"".join(kvs)
     tinfo = b""
     for name, shape, t, off in infos:

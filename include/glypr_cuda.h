@@ -42,7 +42,12 @@ typedef struct glp_ctx glp_ctx;
 typedef struct glp_options {
   int64_t max_batch_tokens; /* tokens per device launch chunk; 0 = 262144 */
   int max_batch_seqs;       /* sequences per chunk; 0 = 4096 */
-  int reserved[6];
+  int device_memory_limit_mib; /* device memory the context may take on each device; 0 = no limit.
+                                * glp_open fails with GLP_ERR_OOM before touching any device when
+                                * the model's plan (weights, RoPE tables, one launch chunk, load
+                                * staging) exceeds it; later growth of the host-API staging
+                                * buffers past it fails the same way */
+  int reserved[5];
 } glp_options;
 
 typedef struct glp_model_info_t {
@@ -52,6 +57,7 @@ typedef struct glp_model_info_t {
   int sliding_window; /* 512, fixed as in config.rs:191 */
   int weight_type;    /* ggml type id of the linears: 8 = Q8_0, 30 = BF16 */
   int n_devices;
+  int64_t device_bytes; /* device memory the context holds on its first device (bytes requested) */
 } glp_model_info_t;
 
 typedef struct glp_timing {
@@ -85,6 +91,20 @@ int glp_model_info(const glp_ctx* ctx, glp_model_info_t* info);
 int glp_embed_tokens(glp_ctx* ctx, const int32_t* ids, const int32_t* lengths, int n_seq, int max_len,
                      int out_dim, float* out, glp_timing* timing);
 
+/* The sharding of glp_embed_tokens over caller-supplied executors instead of the context's
+ * devices (other backends; the host tests drive the coordinator through it without a GPU):
+ * contiguous shards balanced by token count, one host thread per executor, executor i gets
+ * shard i as a right-padded batch (glp_batch_fn, declared below).  The embeddings reach `out`
+ * only when every executor has succeeded; otherwise `out` is untouched and the first failing
+ * executor's status is returned ("executor i: <its message>").  No counterpart function in the
+ * reference, whose embed_batch runs one device (lib.rs:731-952); its server fails every request
+ * of a failed batch and returns no partial result (glypr-server/src/engine.rs:308-325). */
+typedef int (*glp_batch_fn)(void* user, const int32_t* ids, const int32_t* lengths, int n_seq, int max_len,
+                            int out_dim, float* out);
+int glp_embed_tokens_sharded(const glp_batch_fn* fns, void* const* users, int n_executors, int embedding_dim,
+                             const int32_t* ids, const int32_t* lengths, int n_seq, int max_len, int out_dim,
+                             float* out);
+
 /* Device-resident variant on one device: d_ids = packed valid tokens of all sequences,
  * d_cu_seqlens [n_seq + 1] device offsets into d_ids, h_cu_seqlens the same offsets on the
  * host (used to cut launch chunks); d_out [n_seq * out_dim] f32.  Stream-ordered; the ids
@@ -95,6 +115,11 @@ int glp_embed_packed_device(glp_ctx* ctx, int dev_index, const int32_t* d_ids, c
 /* Status word of the device kernels' bounded waits on device dev_index (0 = none); a
  * non-zero value is also reported by the next glp_embed_* call as GLP_ERR_DEVICE. */
 int glp_device_status(glp_ctx* ctx, int dev_index, int* status);
+
+/* What a device status code means (static string; codes as glp_device_status and
+ * glp_kernel_status report them; unknown codes have a text too).  No reference counterpart
+ * (candle reports device errors as strings). */
+const char* glp_status_text(int status);
 
 /* ---- per-kernel profiling (the reference's forward_profiled, profile.rs:55-430, done with
  * CUDA events on the launching stream instead of wall clock + device sync) ---- */
@@ -123,10 +148,9 @@ int glp_profile_read(glp_ctx* ctx, int dev_index, glp_profile* out);
 
 typedef struct glp_engine glp_engine;
 
-/* A batch executor: embed n_seq right-padded sequences (ids [n_seq * max_len], lengths
- * [n_seq]) into out [n_seq * out_dim] f32; returns GLP_OK or an error status. */
-typedef int (*glp_batch_fn)(void* user, const int32_t* ids, const int32_t* lengths, int n_seq, int max_len,
-                            int out_dim, float* out);
+/* A batch executor (glp_batch_fn, declared above): embed n_seq right-padded sequences (ids
+ * [n_seq * max_len], lengths [n_seq]) into out [n_seq * out_dim] f32; returns GLP_OK or an
+ * error status. */
 
 /* Start an engine over a model context: one worker thread forms batches of up to max_batch
  * requests as the reference's worker does (block for the first, drain what is pending, yield
@@ -252,13 +276,53 @@ int glp_q8_0_gemm(const void* d_q8_w, int N, int K, const void* d_x_bf16, int M,
  * device looks up the array's device address; make that first call before any stream
  * capture.  All calls on a device share the array: calls that overlap on the GPU (other
  * streams, other host threads) race on it.  Each call overwrites every scratch element it
- * reads, so nothing needs to be cleared between calls. */
+ * reads, so nothing needs to be cleared between calls.  A bounded wait that expired inside its
+ * kernel is reported by glp_kernel_status (which reads the call's status word with symbol
+ * copies, allocating nothing). */
 int glp_q8_0_gemm_noalloc(const void* d_q8_w, int N, int K, const void* d_x_bf16, int M, void* d_y, int y_is_f32,
                           void* stream);
+
+/* Status of the kernel-level entry points above and below (glp_q8_0_gemm, glp_bf16_gemm,
+ * glp_flash_attention, glp_q8_0_gemm_noalloc and the fused-epilogue GEMMs) on CUDA device
+ * `device`: they are stream-ordered and return before their kernels run, so a kernel whose
+ * bounded wait expired (its output then undefined) is reported here.  Synchronises the device,
+ * then reads and clears the status words of these entry points: *status = the code recorded
+ * since the last read (0 = none), and a recorded code returns GLP_ERR_DEVICE with
+ * glp_status_text(code) in glp_last_error().  Allocates nothing (the no-allocation entry
+ * point's word is read with symbol copies).  The model path (glp_embed_*) has its own word per
+ * context: glp_device_status. */
+int glp_kernel_status(int device, int* status);
+
+/* Failure-detection self-test on CUDA device `device`: one kernel waits, with the bounded wait
+ * every pipeline kernel uses, on a barrier nobody arrives at; after limit_us microseconds
+ * (at most 2,000,000) the wait gives up, records status 6 in the kernel-level word and the
+ * kernel returns normally.  Returns GLP_OK once the kernel has finished; glp_kernel_status then
+ * reports GLP_ERR_DEVICE with status 6, and the device stays usable.  No reference counterpart. */
+int glp_selftest_wait_timeout(int device, int limit_us);
 
 /* Same GEMM on an already dequantised bf16 weight [N, K] (the model path's layout). */
 int glp_bf16_gemm(const void* d_w_bf16, int N, int K, const void* d_x_bf16, int M, void* d_y, int y_is_f32,
                   void* stream);
+
+/* The MLP's gate/up projection with the GeGLU in its epilogue (MLP::forward, mlp.rs:31-70;
+ * cpu_simd/geglu.rs:6-18 with its +-10 clamp): out[M, F] = gelu_tanh(x Wg^T) * (x Wu^T), x f16
+ * [M, K], Wg and Wu f16 [F, K], out f16; F % 128 == 0, K % 64 == 0.  Each call interleaves the
+ * two weights per 128 rows into library scratch (cached per device; the model path does that
+ * once at load), then runs the fused GEMM. */
+int glp_gate_up_geglu(const void* d_w_gate, const void* d_w_up, int F, int K, const void* d_x, int M, void* d_out,
+                      void* stream);
+
+/* The attention block's QKV projection with the per-head norms and RoPE in its epilogue
+ * (SelfAttention::forward, attention/mod.rs:166-213; rope.rs:14-106): y = x Wqkv^T over
+ * (Hq + 2 Hkv) heads of 256, then per head RMSNorm (eps; gain q_gain on query heads, k_gain on
+ * key heads, none on value heads) and NeoX RoPE at positions pos[M] with base theta on the
+ * query and key heads.  x f16 [M, K], Wqkv f16 [(Hq + 2 Hkv) * 256, K] (q, then k, then v rows),
+ * gains f32 [256] (16-byte aligned), out f16 [M, (Hq + 2 Hkv) * 256]; positions must lie in
+ * [0, max_pos).  The cos/sin table for (theta, max_pos) is built once per device (rope.rs
+ * values) and kept until the process exits. */
+int glp_qkv_norm_rope(const void* d_w_qkv, int n_q_heads, int n_kv_heads, int K, const void* d_x, int M,
+                      const float* d_q_gain, const float* d_k_gain, const int32_t* d_pos, double theta, int max_pos,
+                      float eps, void* d_out, void* stream);
 
 /* Flash attention over packed qkv (f16 [T, (Hq + 2 Hkv) * 256], per-head normed + RoPE'd)
  * for n_seq sequences at d_cu_seqlens; window > 0 applies |i - j| <= window.  Writes

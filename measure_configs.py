@@ -1,6 +1,6 @@
 """Measure BASELINE configs 1-4 on one GPU (config 5 is bench.py's line).
 
-    python glypr_b200/measure_configs.py [--model-dir DIR] [--out FILE.md]
+    python measure_configs.py [--model-dir DIR] [--out FILE.md]
 
 * config 1  one 512-token Q8_0 sequence: latency (median of 10 after 3 warm-ups), device-resident
             ids (glp_embed_packed_device) and host ids -> host embeddings (glp_embed_tokens);
@@ -38,11 +38,12 @@ import time
 
 import numpy as np
 
-ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+ROOT = os.path.dirname(os.path.abspath(__file__))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
 from glypr_b200 import api, synth  # noqa: E402
+from bench import ClockSampler  # noqa: E402
 
 GFLOP_PER_SEQ_512 = 123.21  # linear + attention + head per 512-token sequence (config 1)
 
@@ -361,13 +362,15 @@ def main(argv=None) -> None:
     os.makedirs(args.model_dir, exist_ok=True)
     want = set(int(c) if c.isdigit() else c for c in args.configs.split(","))
     report = [f"# BASELINE configs 1–4 on one {torch.cuda.get_device_name(0)}\n",
-              f"Command: `python glypr_b200/measure_configs.py --configs {args.configs}` "
+              f"Command: `python measure_configs.py --configs {args.configs}` "
               f"({time.strftime('%Y-%m-%d')}); median of 10 runs after 3 warm-ups unless stated.\n"]
     api.load_library()
     # a stream of our own: the library runs repeated launch-chunk shapes as CUDA graphs, which
     # the legacy default stream cannot hold
     side = torch.cuda.Stream()
     torch.cuda.set_stream(side)
+    clocks = ClockSampler(0)
+    clocks.start()
     if want & {1, 3, "serving"}:
         q8 = synth.ensure_gguf(os.path.join(args.model_dir, "baseline_q8_0.gguf"), synth.BASELINE)
         with api.GlyprEmbedder.load_gguf(q8, [0]) as emb:
@@ -388,6 +391,10 @@ def main(argv=None) -> None:
         bf = synth.ensure_gguf(os.path.join(args.model_dir, "baseline_bf16.gguf"),
                                synth.EncoderConfig(weight_type="bf16"))
         config4(torch, bf, report)
+    clk = clocks.stop()
+    report.append(f"Clocks over the whole run (nvidia-smi every 200 ms, samples under load): median SM "
+                  f"{clk.get('sm_mhz')} MHz of {clk.get('sm_max_mhz')} MHz, max power {clk.get('power_w_max')} W, "
+                  f"throttle reasons {clk.get('reasons')}.\n")
     text = "\n".join(report)
     print(text, flush=True)
     if args.out:

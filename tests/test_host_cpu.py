@@ -201,3 +201,77 @@ def test_open_ple_width_default(tmp_path, ple_dim, ok):
         assert rc not in (api.GLP_ERR_UNSUPPORTED, api.GLP_ERR_FORMAT), msg
     else:
         assert rc == api.GLP_ERR_FORMAT and msg == "bad shape for per_layer_model_proj.weight"
+
+
+def test_kv_heads_non_integer_elements_take_the_defaults(tmp_path):
+    """head_count_kv elements that are not integers yield no value in the reference's get_u32
+    (config.rs:253-265), so the defaults apply: 2 for the sliding layers, 1 for global ones.
+    An f32 array therefore behaves like a missing key."""
+    cfg = synth.small_config(n_layers=6, vocab=256, n_heads=4, n_kv_heads=2, global_kv_heads=1)
+    key = "gemma-embedding2.attention.head_count_kv"
+    p = synth.write_gguf(str(tmp_path / "kvf.gguf"), cfg, drop={key},
+                         extra_kv=[synth.gguf_kv(key, "arr_f32", [2.0] * 5 + [1.0])])
+    rc, msg = _open(p)
+    assert rc not in (api.GLP_ERR_UNSUPPORTED, api.GLP_ERR_FORMAT), msg
+    # f32 elements [3, ..] would give 3 KV heads if they were read; the defaults (2, 1) fit the tensors
+    p = synth.write_gguf(str(tmp_path / "kvf3.gguf"), cfg, drop={key},
+                         extra_kv=[synth.gguf_kv(key, "arr_f32", [3.0] * 6)])
+    rc, msg = _open(p)
+    assert rc not in (api.GLP_ERR_UNSUPPORTED, api.GLP_ERR_FORMAT), msg
+
+
+def test_scalar_keys_follow_the_reference_types(tmp_path):
+    """An f32 context_length is not an integer for the reference's get_u32 (config.rs:253-265):
+    the default 262144 (config.rs:95-96) applies instead of a truncated 300, so the model
+    still opens (without a GPU: up to the first CUDA call)."""
+    cfg = synth.small_config(n_layers=1, vocab=256)
+    key = "gemma-embedding2.context_length"
+    p = synth.write_gguf(str(tmp_path / "ctx.gguf"), cfg, drop={key}, extra_kv=[synth.gguf_kv(key, "f32", 300.5)])
+    rc, msg = _open(p)
+    assert rc not in (api.GLP_ERR_UNSUPPORTED, api.GLP_ERR_FORMAT), msg
+
+
+def test_layer_output_scale_checked_before_allocation(tmp_path):
+    """A malformed per-layer scalar is a format error found while validating the file, before
+    any device work (so it fails the same way with or without a GPU)."""
+    cfg = synth.small_config(n_layers=2, vocab=256, ple_dim=256)
+    p = synth.write_gguf(str(tmp_path / "los.gguf"), cfg, f32_scalars={"blk.1.layer_output_scale.weight"})
+    rc, msg = _open(p)
+    assert rc == api.GLP_ERR_FORMAT and msg == "bad layer_output_scale"
+
+
+def _open_opts(path, limit_mib):
+    L = api.load_library()
+    out = ctypes.c_void_p()
+    opt = api.GlpOptions(device_memory_limit_mib=limit_mib)
+    rc = L.glp_open(path.encode(), None, 0, ctypes.byref(opt), ctypes.byref(out))
+    msg = L.glp_last_error().decode()
+    if rc == api.GLP_OK:
+        L.glp_close(out)
+    assert not out.value or rc == api.GLP_OK
+    return rc, msg
+
+
+def test_device_memory_limit_fails_before_any_device_work(tmp_path):
+    """glp_options.device_memory_limit_mib: a plan above the limit fails with GLP_ERR_OOM
+    before the library touches a device (so this runs without one) and no context comes back;
+    a limit above the plan passes the check (without a GPU the open then stops at the first
+    CUDA call)."""
+    cfg = synth.small_config(n_layers=1, vocab=256)
+    p = synth.write_gguf(str(tmp_path / "cap.gguf"), cfg)
+    rc, msg = _open_opts(p, 16)
+    assert rc == api.GLP_ERR_OOM, msg
+    assert "above the limit of 16 MiB" in msg
+    need = int(msg.split("the model needs ")[1].split(" MiB")[0])
+    assert need > 16
+    rc, msg = _open_opts(p, need)
+    assert rc != api.GLP_ERR_OOM, msg
+
+
+def test_status_texts():
+    """Every device status code the kernels record has its own text (glp_status_text)."""
+    texts = {c: api.status_text(c) for c in range(0, 7)}
+    assert texts[0] == "no device error"
+    assert len(set(texts.values())) == 7
+    assert "self-test" in texts[6]
+    assert api.status_text(99) == "unknown device status code"

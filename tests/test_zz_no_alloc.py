@@ -49,6 +49,8 @@ def test_noalloc_matches_allocating_gemm_two_calls_in_a_row():
         free_before = torch.cuda.mem_get_info()[0]
         api.q8_0_gemm_noalloc(d_w.data_ptr(), n, k, x.data_ptr(), m, y_new.data_ptr(), f32)
         torch.cuda.synchronize()
+        # no bounded wait of the kernel ran out (the status read allocates nothing either)
+        assert api.kernel_status(0) == 0
         free_after = torch.cuda.mem_get_info()[0]
         assert free_after == free_before, "the no-allocation entry point changed free device memory"
         got = y_new.float().cpu().numpy().astype(np.float64)
