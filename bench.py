@@ -306,7 +306,8 @@ def q8_0_gemm_section(torch, device, peaks, local_rank) -> dict:
             flop = 2.0 * m * n * k
             byts = n * k / 32 * 34 + 2.0 * m * k + 2.0 * m * n
             roof_ms = max(flop / (p_t * 1e9), byts / (p_b * 1e6))
-            rows.append({"n": n, "k": k, "m": m, "ms": round(ms, 5), "tflops": round(flop / ms / 1e9, 1),
+            rows.append({"n": n, "k": k, "m": m, "route": "fused raw-Q8_0 stream" if m <= 8192 else "dequant + bf16 GEMM",
+                         "ms": round(ms, 5), "tflops": round(flop / ms / 1e9, 1),
                          "gbs": round(byts / ms / 1e6, 1), "roofline_pct": round(100 * roof_ms / ms, 1)})
             del sets
     clk = clocks.stop()

@@ -53,6 +53,8 @@ struct GemmParams {
   // kEpiMulGeglu: the second GeGLU operand U (row stride ld_mul elements)
   const __half* mul;
   int ld_mul;
+  // gemm_q8_pair_kernel: bytes per raw Q8_0 row (34 K / 32) and the rows per TMA group row
+  int raw_pitch, raw_group;
 };
 
 template <int BN>

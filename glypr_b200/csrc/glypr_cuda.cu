@@ -30,6 +30,7 @@
 #include "gguf.h"
 #include "glypr_cuda.h"
 #include "ple.cuh"
+#include "q8gemm.cuh"
 #include "rowops.cuh"
 
 using glp::GemmParams;
@@ -162,6 +163,11 @@ int ensure_kernel_attrs() {
   GLP_CUDA(cudaFuncSetAttribute(glp::gemm_rownorm_kernel<__half, 4>, A, static_cast<int>(glp::GemmRowCfgT<4>::SMEM)));
   GLP_CUDA(cudaFuncSetAttribute(glp::flash_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 static_cast<int>(glp::kFaSmem)));
+  const int q256 = static_cast<int>(glp::Q8PairCfg<256>::SMEM), q128 = static_cast<int>(glp::Q8PairCfg<128>::SMEM);
+  GLP_CUDA(cudaFuncSetAttribute(glp::gemm_q8_pair_kernel<glp::kEpiStore16, __nv_bfloat16, 256>, A, q256));
+  GLP_CUDA(cudaFuncSetAttribute(glp::gemm_q8_pair_kernel<glp::kEpiStore16, __nv_bfloat16, 128>, A, q128));
+  GLP_CUDA(cudaFuncSetAttribute(glp::gemm_q8_pair_kernel<glp::kEpiF32, __nv_bfloat16, 256>, A, q256));
+  GLP_CUDA(cudaFuncSetAttribute(glp::gemm_q8_pair_kernel<glp::kEpiF32, __nv_bfloat16, 128>, A, q128));
   g_attr_done[dev] = true;
   return GLP_OK;
 }
@@ -367,6 +373,88 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, int bn, int epi, G
         break;
       default: return fail(GLP_ERR_INVALID_ARG, "fused epilogues need 256-wide tiles");
     }
+  }
+  GLP_CUDA(cudaGetLastError());
+  return GLP_OK;
+}
+
+// ------------------------------------------------------------------------------ Q8_0 GEMM on raw rows
+// Rows per TMA group row for raw Q8_0 rows of K elements: the smallest G in {1, 2, 4} with
+// G * (34 K / 32) a multiple of 16 bytes (a TMA row stride); 0 when K % 64 != 0.
+int q8_raw_group(int K) {
+  if (K <= 0 || K % 64) return 0;
+  const int64_t pitch = static_cast<int64_t>(K) / 32 * 34;
+  for (int g = 1; g <= 4; g *= 2)
+    if ((g * pitch) % 16 == 0) return g;
+  return 0;
+}
+
+// The raw rows W [N, 34 K / 32 bytes] as the byte tensor {G P, N / G}, boxes of 80 bytes x
+// box_rows group rows (see gemm_q8_pair_kernel).
+int make_map_q8_raw(CUtensorMap* m, const void* base, int N, int K, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(GLP_ERR_CUDA, "cuTensorMapEncodeTiled unavailable (driver too old?)");
+  const int G = q8_raw_group(K);
+  if (!G || N % G) return fail(GLP_ERR_INVALID_ARG, "Q8_0 GEMM needs K % 64 == 0");
+  if (reinterpret_cast<uintptr_t>(base) & 15) return fail(GLP_ERR_INVALID_ARG, "Q8_0 weight must be 16-byte aligned");
+  const uint64_t row = static_cast<uint64_t>(G) * (K / 32) * 34;
+  const cuuint64_t dims[2] = {row, static_cast<cuuint64_t>(N / G)};
+  const cuuint64_t strides[1] = {row};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(glp::kQ8RawBoxBytes), static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t estr[2] = {1u, 1u};
+  const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(GLP_ERR_CUDA, "cuTensorMapEncodeTiled (raw Q8_0) failed: " + std::to_string(r));
+  return GLP_OK;
+}
+
+// Pair-tile width for an M x N Q8_0 GEMM: 256 columns, or 128 when that finishes in fewer
+// waves of the device's pairs (each 128-wide tile costs about 0.55 of a 256-wide one).
+int q8_tile_n(int M, int N) {
+  const int64_t pairs = std::max(1, sm_count() / 2);
+  const int64_t m_tiles = (M + 255) / 256;
+  double best = 1e30;
+  int bn = 128;
+  for (int cand : {256, 128}) {
+    if (N % cand) continue;
+    const int64_t tiles = m_tiles * (N / cand);
+    const double cost = static_cast<double>((tiles + pairs - 1) / pairs) * (cand == 256 ? 1.0 : 0.55);
+    if (cost < best) {
+      best = cost;
+      bn = cand;
+    }
+  }
+  return bn;
+}
+
+// C = A * dequant(W)^T with W as raw Q8_0 rows in device memory: one launch of the pair
+// kernel that streams the raw bytes and dequantises them in shared memory.
+int launch_q8_gemm(const CUtensorMap& ma, const void* w_raw, bool f32_out, GemmParams p, cudaStream_t st) {
+  if (p.M <= 0) return GLP_OK;
+  if (p.N <= 0 || p.N % 128 || p.K <= 0 || p.K % 64) return fail(GLP_ERR_INVALID_ARG, "Q8_0 GEMM needs N % 128 == 0, K % 64 == 0");
+  const int bn = q8_tile_n(p.M, p.N);
+  p.raw_group = q8_raw_group(p.K);
+  p.raw_pitch = p.K / 32 * 34;
+  p.m_tiles = (p.M + 255) / 256;
+  p.n_tiles = p.N / bn;
+  p.k_blocks = p.K / 64;
+  CUtensorMap mw;
+  GLP_TRY(make_map_q8_raw(&mw, w_raw, p.N, p.K, bn / 2 / p.raw_group));
+  const int pairs = std::min(p.m_tiles * p.n_tiles, std::max(1, sm_count() / 2));
+  const dim3 grid(static_cast<unsigned>(2 * pairs));
+  if (bn == 256) {
+    const size_t smem = glp::Q8PairCfg<256>::SMEM;
+    if (f32_out)
+      glp::gemm_q8_pair_kernel<glp::kEpiF32, __nv_bfloat16, 256><<<grid, glp::kQ8Threads, smem, st>>>(ma, mw, p);
+    else
+      glp::gemm_q8_pair_kernel<glp::kEpiStore16, __nv_bfloat16, 256><<<grid, glp::kQ8Threads, smem, st>>>(ma, mw, p);
+  } else {
+    const size_t smem = glp::Q8PairCfg<128>::SMEM;
+    if (f32_out)
+      glp::gemm_q8_pair_kernel<glp::kEpiF32, __nv_bfloat16, 128><<<grid, glp::kQ8Threads, smem, st>>>(ma, mw, p);
+    else
+      glp::gemm_q8_pair_kernel<glp::kEpiStore16, __nv_bfloat16, 128><<<grid, glp::kQ8Threads, smem, st>>>(ma, mw, p);
   }
   GLP_CUDA(cudaGetLastError());
   return GLP_OK;
@@ -1967,12 +2055,44 @@ int glp_q8_0_dequant(const void* d_blocks, int64_t n_blocks, float* d_out, void*
 
 int glp_q8_0_gemm(const void* d_q8_w, int N, int K, const void* d_x_bf16, int M, void* d_y, int y_is_f32,
                   void* stream) {
-  if (N <= 0 || K <= 0 || N % 128 || K % 64) return fail(GLP_ERR_INVALID_ARG, "Q8_0 GEMM needs N % 128 == 0, K % 64 == 0");
-  if (!d_q8_w) return fail(GLP_ERR_INVALID_ARG, "null weight");
+  if (N <= 0 || K <= 0 || N % 128 || K % 64 || M < 0)
+    return fail(GLP_ERR_INVALID_ARG, "Q8_0 GEMM needs N % 128 == 0, K % 64 == 0, M >= 0");
+  if (!d_q8_w || !d_x_bf16 || !d_y) return fail(GLP_ERR_INVALID_ARG, "null pointer");
   int dev = 0;
   GLP_CUDA(cudaGetDevice(&dev));
   if (dev < 0 || dev >= 64) return fail(GLP_ERR_INVALID_ARG, "device index out of range");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // Two routes, chosen by measurement (B200, bf16 out): up to M = 8192 rows one launch of the
+  // kernel that streams the raw rows and dequantises them in shared memory (768 x 768 at
+  // M = 512: 13.7 vs 25 us; at M = 4096: 16.7 vs 24 us); above it the weight is dequantised
+  // into library scratch and the bf16 CTA-pair GEMM runs (M = 131072: 124 vs 170 us; the
+  // fused kernel's tensor pipe waits on the dequantisation warps there).  A weight that is not
+  // 16-byte aligned (a row slice of a fused weight) always takes the second route.
+  // GLP_Q8_GEMM=fused or =two-pass forces one route (for A/B measurements).
+  static const int route = [] {
+    const char* e = std::getenv("GLP_Q8_GEMM");
+    if (e && std::string(e) == "two-pass") return 2;
+    if (e && std::string(e) == "fused") return 1;
+    return 0;
+  }();
+  constexpr int kFusedMaxM = 8192;
+  const bool fused = !(reinterpret_cast<uintptr_t>(d_q8_w) & 15) && (route == 1 || (route == 0 && M <= kFusedMaxM));
+  if (fused) {
+    GLP_TRY(ensure_kernel_attrs());
+    int* status = nullptr;
+    GLP_TRY(device_status_word(dev, &status));
+    if (M == 0) return GLP_OK;
+    CUtensorMap ma;
+    GLP_TRY(make_map16(&ma, d_x_bf16, M, K, K, 128, false));
+    GemmParams p{};
+    p.M = M;
+    p.N = N;
+    p.K = K;
+    p.C = d_y;
+    p.ldc = N;
+    p.status = status;
+    return launch_q8_gemm(ma, d_q8_w, y_is_f32 != 0, p, st);
+  }
   __nv_bfloat16* w = nullptr;
   {
     std::lock_guard<std::mutex> lk(g_scratch.mu);

@@ -261,8 +261,10 @@ int glp_q8_0_dequant(const void* d_blocks, int64_t n_blocks, float* d_out, void*
 /* y[M, N] = x[M, K] (bf16, row-major) * dequant(W[N, K])^T, W as raw Q8_0 rows of K/32
  * blocks; y f32 (y_is_f32 = 1) or bf16.  K % 64 == 0, N % 128 == 0.  The Q8_0 matmul behind
  * LinearOp::forward (linear.rs:150-172; Metal fused_metal_q8_0_matmul,
- * metal_kernels/mod.rs:1271-1394).  Dequantises W into a context-free scratch buffer
- * owned by the library (cached per device), then runs the tcgen05 GEMM. */
+ * metal_kernels/mod.rs:1271-1394).  Up to M = 8192 (and for a 16-byte aligned W) one launch
+ * streams the raw rows by TMA and dequantises them in shared memory in front of the tcgen05
+ * MMA; for larger M, where that measures slower, W is dequantised into a context-free scratch
+ * buffer owned by the library (cached per device) and the bf16 tcgen05 GEMM runs. */
 int glp_q8_0_gemm(const void* d_q8_w, int N, int K, const void* d_x_bf16, int M, void* d_y, int y_is_f32,
                   void* stream);
 

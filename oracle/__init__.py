@@ -44,6 +44,7 @@ def lib() -> ctypes.CDLL:
             L.oracle_last_error.restype = ctypes.c_char_p
             L.oracle_info.argtypes = [P, P]
             L.oracle_set_threads.argtypes = [I]
+            L.oracle_set_simd.argtypes = [I]
             L.oracle_max_threads.restype = I
             L.oracle_embed.argtypes = [P, P, P, I, I, I, I, P]
             L.oracle_hidden.argtypes = [P, P, I, I, I, P]
@@ -66,6 +67,11 @@ def _p(a: Optional[np.ndarray]):
 
 def set_threads(n: int) -> None:
     lib().oracle_set_threads(int(n))
+
+
+def set_simd(on: bool) -> None:
+    """AVX2 block dots and attention (default) or the scalar loops: identical results."""
+    lib().oracle_set_simd(int(bool(on)))
 
 
 def max_threads() -> int:

@@ -44,6 +44,7 @@
 #include <sys/stat.h>
 #include <unistd.h>
 #include <vector>
+#include <immintrin.h>
 #include <omp.h>
 
 namespace {
@@ -338,6 +339,67 @@ void quantize_row_q8_0(const float* x, int64_t k, QBlock* y) {
   }
 }
 
+// SIMD switch for the CPU-baseline speed (oracle_set_simd): the vector paths below compute
+// every value exactly as the scalar loops do (integer block dots are exact; each float
+// accumulation keeps its order), which a test checks bit for bit.
+bool g_simd = true;
+
+#if defined(__AVX2__)
+// Four int8 block dots (32 products each) of one activation block against four weight
+// blocks: exact int32 sums [w0.x, w1.x, w2.x, w3.x].  |w| as unsigned bytes times x with w's
+// sign (maddubs: pairs of products, at most 2 * 128 * 127 < 2^15), then pairs of int16 summed
+// into int32 (madd with ones) and the lanes folded.  Activations never hold -128 (quantised
+// to [-127, 127]), so negating them cannot overflow.
+inline __m128i dot32x4(const int8_t* x, const int8_t* w0, const int8_t* w1, const int8_t* w2, const int8_t* w3) {
+  const __m256i vx = _mm256_loadu_si256(reinterpret_cast<const __m256i*>(x));
+  const __m256i ones = _mm256_set1_epi16(1);
+  auto one = [&](const int8_t* w) {
+    const __m256i vw = _mm256_loadu_si256(reinterpret_cast<const __m256i*>(w));
+    const __m256i p16 = _mm256_maddubs_epi16(_mm256_sign_epi8(vw, vw), _mm256_sign_epi8(vx, vw));
+    return _mm256_madd_epi16(p16, ones);
+  };
+  const __m256i a = one(w0), b = one(w1), c = one(w2), d = one(w3);
+  const __m256i h = _mm256_hadd_epi32(_mm256_hadd_epi32(a, b), _mm256_hadd_epi32(c, d));
+  return _mm_add_epi32(_mm256_castsi256_si128(h), _mm256_extracti128_si256(h, 1));
+}
+#endif
+
+#if defined(__AVX2__)
+// M1 with AVX2 block dots.  The scalar loop's float steps are a multiply, a multiply and an add
+// per block (the compiler fuses none of them there); fp-contract=off keeps this function from
+// fusing the vector multiply and add, so both paths round identically.
+__attribute__((optimize("fp-contract=off"))) void linear_m1_avx2(const Linear& w, const std::vector<QBlock>& xq,
+                                                                 int64_t m, float* y) {
+  const int64_t n = w.n, k = w.k, nb = k / 32;
+  (void)k;
+  // scales converted once: weights [n][nb] transposed to [nb][n], activations [m][nb]
+  std::vector<float> dw((size_t)(nb * n)), dx((size_t)(m * nb));
+#pragma omp parallel for schedule(static)
+  for (int64_t c = 0; c < n; ++c)
+    for (int64_t b = 0; b < nb; ++b) dw[(size_t)(b * n + c)] = blk_d(w.data + (c * nb + b) * 34);
+  for (int64_t i = 0; i < m * nb; ++i) dx[(size_t)i] = f16_to_f32(xq[(size_t)i].d);
+#pragma omp parallel for schedule(dynamic, 4)
+  for (int64_t c0 = 0; c0 < n; c0 += 4) {
+    const uint8_t* wr = w.data + c0 * nb * 34;
+    const int64_t rs = nb * 34;
+    for (int64_t i = 0; i < m; ++i) {
+      const QBlock* xr = &xq[(size_t)(i * nb)];
+      __m128 sum = _mm_setzero_ps();
+      for (int64_t b = 0; b < nb; ++b) {
+        const int8_t* q0 = (const int8_t*)(wr + 34 * b + 2);
+        const __m128 s = _mm_cvtepi32_ps(dot32x4(xr[b].qs, q0, q0 + rs, q0 + 2 * rs, q0 + 3 * rs));
+        // sumf += (float)s * d_w * d_x, per column in block order, as the scalar loop
+        sum = _mm_add_ps(sum, _mm_mul_ps(_mm_mul_ps(s, _mm_loadu_ps(&dw[(size_t)(b * n + c0)])),
+                                         _mm_set1_ps(dx[(size_t)(i * nb + b)])));
+      }
+      float o[4];
+      _mm_storeu_ps(o, sum);
+      for (int j = 0; j < 4; ++j) y[i * n + c0 + j] = o[j];
+    }
+  }
+}
+#endif
+
 // Y[M,N] = X[M,K] * W[N,K]^T.  mode 1 = candle-faithful (Q8_0 activations), 2 = exact f32 dequant.
 void linear_forward(const Linear& w, const float* x, int64_t m, float* y, int mode) {
   const int64_t n = w.n, k = w.k, nb = k / 32;
@@ -345,6 +407,12 @@ void linear_forward(const Linear& w, const float* x, int64_t m, float* y, int mo
     std::vector<QBlock> xq((size_t)(m * nb));
 #pragma omp parallel for schedule(static)
     for (int64_t i = 0; i < m; ++i) quantize_row_q8_0(x + i * k, k, &xq[(size_t)(i * nb)]);
+#if defined(__AVX2__)
+    if (g_simd && n % 4 == 0) {
+      linear_m1_avx2(w, xq, m, y);
+      return;
+    }
+#endif
 #pragma omp parallel for schedule(dynamic, 16)
     for (int64_t c = 0; c < n; ++c) {
       const uint8_t* wr = w.data + c * nb * 34;
@@ -410,6 +478,7 @@ void rope_tables(int d, double theta, int64_t s, float* cos_t, float* sin_t) {
   int half = d / 2;
   std::vector<float> inv(half);
   for (int i = 0; i < half; ++i) inv[i] = (float)(1.0 / std::pow(theta, (double)(2 * i) / (double)d));
+#pragma omp parallel for schedule(static) if (s > 64)
   for (int64_t p = 0; p < s; ++p)
     for (int i = 0; i < d; ++i) {
       float f = (float)p * inv[i % half];
@@ -434,6 +503,83 @@ void apply_rope(float* x, int d, const float* c, const float* s) {
 void attention_seq(const float* q, const float* k, const float* v, int64_t t, int h, int kvh,
                    int d, int window, bool sliding, float* out) {
   const int rep = h / kvh;
+#if defined(__AVX2__)
+  if (g_simd && d % 32 == 0) {
+    // The same arithmetic with the keys transposed per KV head (kt[kv][e][j]): eight keys'
+    // scores advance together, each still one fma chain over e in order; o[e] for eight e at
+    // a time, each still one fma chain over j in order.
+    std::vector<float> kt((size_t)(kvh * d * t));
+#pragma omp parallel for schedule(static)
+    for (int64_t j = 0; j < t; ++j)
+      for (int kv = 0; kv < kvh; ++kv)
+        for (int e = 0; e < d; ++e) kt[((size_t)kv * d + e) * t + j] = k[(j * kvh + kv) * d + e];
+#pragma omp parallel
+    {
+      std::vector<float> sc((size_t)t + 8);
+#pragma omp for collapse(2) schedule(dynamic, 8)
+      for (int hh = 0; hh < h; ++hh)
+        for (int64_t i = 0; i < t; ++i) {
+          const int kv = hh / rep;
+          const float* qi = q + i * h * d + hh * d;
+          const float* kk = kt.data() + (size_t)kv * d * t;
+          int64_t j0 = 0, j1 = t;
+          if (sliding) {
+            j0 = i - window > 0 ? i - window : 0;
+            j1 = i + window + 1 < t ? i + window + 1 : t;
+          }
+          int64_t j = j0;
+          for (; j + 32 <= j1; j += 32) {  // four independent chains hide the fma latency
+            __m256 a0 = _mm256_setzero_ps(), a1 = a0, a2 = a0, a3 = a0;
+            for (int e = 0; e < d; ++e) {
+              const __m256 qe = _mm256_set1_ps(qi[e]);
+              const float* ke = kk + (size_t)e * t + j;
+              a0 = _mm256_fmadd_ps(qe, _mm256_loadu_ps(ke), a0);
+              a1 = _mm256_fmadd_ps(qe, _mm256_loadu_ps(ke + 8), a1);
+              a2 = _mm256_fmadd_ps(qe, _mm256_loadu_ps(ke + 16), a2);
+              a3 = _mm256_fmadd_ps(qe, _mm256_loadu_ps(ke + 24), a3);
+            }
+            _mm256_storeu_ps(&sc[(size_t)j], a0);
+            _mm256_storeu_ps(&sc[(size_t)j + 8], a1);
+            _mm256_storeu_ps(&sc[(size_t)j + 16], a2);
+            _mm256_storeu_ps(&sc[(size_t)j + 24], a3);
+          }
+          for (; j + 8 <= j1; j += 8) {
+            __m256 acc = _mm256_setzero_ps();
+            for (int e = 0; e < d; ++e)
+              acc = _mm256_fmadd_ps(_mm256_set1_ps(qi[e]), _mm256_loadu_ps(kk + (size_t)e * t + j), acc);
+            _mm256_storeu_ps(&sc[(size_t)j], acc);
+          }
+          for (; j < j1; ++j) {
+            float s = 0.f;
+            for (int e = 0; e < d; ++e) s = std::fma(qi[e], kk[(size_t)e * t + j], s);
+            sc[(size_t)j] = s;
+          }
+          float mx = -INFINITY;
+          for (j = j0; j < j1; ++j) mx = std::fmax(mx, sc[(size_t)j]);
+          float sum = 0.f;
+          for (j = j0; j < j1; ++j) { sc[(size_t)j] = std::exp(sc[(size_t)j] - mx); sum += sc[(size_t)j]; }
+          float* o = out + i * h * d + hh * d;
+          for (j = j0; j < j1; ++j) sc[(size_t)j] = sc[(size_t)j] / sum;  // p_j, as the scalar loop forms it
+          for (int e = 0; e < d; e += 32) {  // four independent chains per pass
+            __m256 a0 = _mm256_setzero_ps(), a1 = a0, a2 = a0, a3 = a0;
+            for (j = j0; j < j1; ++j) {
+              const __m256 pj = _mm256_set1_ps(sc[(size_t)j]);
+              const float* vj = v + j * kvh * d + kv * d + e;
+              a0 = _mm256_fmadd_ps(pj, _mm256_loadu_ps(vj), a0);
+              a1 = _mm256_fmadd_ps(pj, _mm256_loadu_ps(vj + 8), a1);
+              a2 = _mm256_fmadd_ps(pj, _mm256_loadu_ps(vj + 16), a2);
+              a3 = _mm256_fmadd_ps(pj, _mm256_loadu_ps(vj + 24), a3);
+            }
+            _mm256_storeu_ps(o + e, a0);
+            _mm256_storeu_ps(o + e + 8, a1);
+            _mm256_storeu_ps(o + e + 16, a2);
+            _mm256_storeu_ps(o + e + 24, a3);
+          }
+        }
+    }
+    return;
+  }
+#endif
 #pragma omp parallel
   {
     std::vector<float> sc((size_t)t);
@@ -641,6 +787,7 @@ void forward_seq(const oracle_model* m, const int32_t* ids, int64_t t, int mode,
     std::vector<float> gt((size_t)(t * m->ffn)), up((size_t)(t * m->ffn));
     linear_forward(L.gate, x.data(), t, gt.data(), mode);
     linear_forward(L.up, x.data(), t, up.data(), mode);
+#pragma omp parallel for schedule(static)
     for (size_t i = 0; i < gt.size(); ++i) gt[i] = geglu1(gt[i], up[i]);
     linear_forward(L.down, gt.data(), t, y.data(), mode);
     rmsnorm_rows(y.data(), L.post_ffw.data(), t, H, eps, y.data());
@@ -725,6 +872,7 @@ int oracle_info(const oracle_model* m, int* out) {
 }
 
 void oracle_set_threads(int n) { if (n > 0) omp_set_num_threads(n); }
+void oracle_set_simd(int on) { g_simd = on != 0; }
 int oracle_max_threads(void) { return omp_get_max_threads(); }
 
 // ids [n_seq, max_len] right-padded; out [n_seq, out_dim] L2-normalised (MRL if out_dim < E).

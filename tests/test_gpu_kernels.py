@@ -89,6 +89,44 @@ def test_q8_0_gemm(n, k, m, f32_out):
     assert np.abs(got - ref_bf).max() <= tol * scale
 
 
+def _gemm_check(blocks, n, k, m, d_w_ptr, f32_out, seed):
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((m, k), dtype=np.float32)
+    xb = torch.from_numpy(x).to(torch.bfloat16).cuda()
+    y = torch.full((m, n), float("nan"), dtype=torch.float32 if f32_out else torch.bfloat16, device="cuda")
+    api.q8_0_gemm(d_w_ptr, n, k, xb.data_ptr(), m, y.data_ptr(), f32_out)
+    assert api.kernel_status(0) == 0
+    got = y.float().cpu().numpy().astype(np.float64)
+    xf = xb.float().cpu().numpy().astype(np.float64)
+    w_bf16 = torch.from_numpy(synth.dequantize_q8_0(blocks)).to(torch.bfloat16).float().numpy().astype(np.float64)
+    ref = xf @ w_bf16.T
+    tol = 2e-5 if f32_out else 8e-3
+    assert np.abs(got - ref).max() <= tol * np.abs(ref).max()
+
+
+@pytest.mark.parametrize("n,k", [(768, 768), (1152, 768), (768, 1152), (256, 64)])
+@pytest.mark.parametrize("m", [8192, 8193])
+def test_q8_0_gemm_both_routes(n, k, m):
+    """M = 8192 runs the kernel that streams raw Q8_0 rows and dequantises in shared memory
+    (every group-row view: K = 768 and 1152 take 1 and 2 rows per TMA row, K = 64 four), M =
+    8193 the dequantise-then-GEMM route; both against bf16(q d) operands with f32 accumulation."""
+    blocks = _q8_blocks(n, k, seed=n + k + m)
+    d_w = _dev(blocks.view(np.uint8).reshape(-1))
+    _gemm_check(blocks, n, k, m, d_w.data_ptr(), True, seed=m)
+    _gemm_check(blocks, n, k, m, d_w.data_ptr(), False, seed=m + 1)
+
+
+def test_q8_0_gemm_unaligned_weight():
+    """A weight that starts off a 16-byte boundary (a row slice of a fused weight, as the
+    reference's try_concat views are) takes the dequantise-then-GEMM route at any M."""
+    n, k = 256, 1152
+    blocks = _q8_blocks(n, k, seed=3)
+    raw = blocks.view(np.uint8).reshape(-1)
+    buf = torch.zeros(raw.size + 16, dtype=torch.uint8, device="cuda")
+    buf[2:2 + raw.size] = _dev(raw)
+    _gemm_check(blocks, n, k, 300, buf.data_ptr() + 2, True, seed=4)
+
+
 def test_q8_0_gemm_reference_recipe():
     """metal_kernels/mod.rs:1924-1979 restated: 128 x 256, sin/cos inputs, 1e-2 (relative to
     the output range) vs the candle-faithful QMatMul (oracle M1)."""

@@ -303,3 +303,20 @@ def test_baseline_init_is_ill_conditioned(deep_gguf, deep_cond_gguf):
     b = cond.embed(ids, lens, oracle.M2_EXACT)
     cos = (a * b).sum(1) / (np.linalg.norm(a, axis=1) * np.linalg.norm(b, axis=1))
     assert (cos >= 0.9999).all(), cos
+
+
+@pytest.mark.parametrize("mode", [oracle.M1_CANDLE, oracle.M2_EXACT])
+def test_simd_paths_bit_identical(small_cond_gguf, mode):
+    """The oracle's AVX2 paths (int8 block dots of M1, attention with transposed keys) give
+    the scalar loops' results bit for bit: the timed CPU baseline computes exactly what the
+    checker computes."""
+    m = oracle.OracleModel(small_cond_gguf)
+    ids, lens = synth.make_batch(3, 700, m.vocab, lengths=[700, 37, 1], seed=11)
+    try:
+        oracle.set_simd(False)
+        slow = m.embed(ids, lens, mode)
+        oracle.set_simd(True)
+        fast = m.embed(ids, lens, mode)
+    finally:
+        oracle.set_simd(True)
+    np.testing.assert_array_equal(fast.view(np.uint32), slow.view(np.uint32))
