@@ -261,6 +261,12 @@ __device__ __forceinline__ void tmem_ld_wait_tied8(uint32_t (&a)[8], uint32_t (&
                :
                : "memory");
 }
+// 32 lanes x 8 consecutive 32-bit columns store.
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]),
+               "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
+}
 // 32 lanes x 4 consecutive 32-bit columns store.
 __device__ __forceinline__ void tmem_st4(uint32_t taddr, const uint32_t* r) {
   asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%2,%3,%4};" ::"r"(taddr), "r"(r[0]), "r"(r[1]),

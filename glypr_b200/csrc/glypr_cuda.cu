@@ -26,6 +26,7 @@
 #include <vector>
 
 #include "attention_tc.cuh"
+#include "attention_d512.cuh"
 #include "gemm.cuh"
 #include "gguf.h"
 #include "glypr_cuda.h"
@@ -100,8 +101,33 @@ int sm_count();
 
 // Launch attention over packed qkv rows [0, T) for n_seq sequences at cu (minus cu_base).
 int launch_attention(const __half* qkv, int64_t T, int qkv_width, const int* cu, int cu_base, int n_seq, int max_len,
-                     int n_q_heads, int n_kv_heads, int window, __half* out, int* status, cudaStream_t st) {
+                     int n_q_heads, int n_kv_heads, int window, __half* out, int* status, cudaStream_t st,
+                     int head_dim = glp::kFaD) {
   if (T <= 0 || n_seq <= 0 || max_len <= 0) return GLP_OK;
+  if (head_dim == glp::kF5D) {  // 512-wide heads: two CTAs per (block, head), one O half each
+    CUtensorMap mq, mkv, mo;
+    GLP_TRY(make_map16(&mq, qkv, T, qkv_width, qkv_width, glp::kF5BQ, true));
+    GLP_TRY(make_map16(&mkv, qkv, T, qkv_width, qkv_width, glp::kF5BKV, true));
+    GLP_TRY(make_map16(&mo, out, T, static_cast<int64_t>(n_q_heads) * glp::kF5D,
+                       static_cast<int64_t>(n_q_heads) * glp::kF5D, glp::kFaOutBoxRows, true));
+    glp::FaParams fp{};
+    fp.cu_seqlens = cu;
+    fp.cu_base = cu_base;
+    fp.n_seq = n_seq;
+    fp.q_blocks = (max_len + glp::kF5BQ - 1) / glp::kF5BQ;
+    fp.n_q_heads = n_q_heads;
+    fp.n_kv_heads = n_kv_heads;
+    fp.window = window;
+    fp.out = out;
+    fp.ld_out = n_q_heads * glp::kF5D;
+    fp.status = status;
+    const int64_t items = static_cast<int64_t>(n_seq) * fp.q_blocks * n_q_heads * 2;
+    const int grid = static_cast<int>(std::min<int64_t>(items, sm_count()));
+    glp::flash_attn_d512_kernel<<<grid, glp::kFaThreads, glp::kF5Smem, st>>>(mq, mkv, mo, fp);
+    GLP_CUDA(cudaGetLastError());
+    return GLP_OK;
+  }
+  if (head_dim != glp::kFaD) return fail(GLP_ERR_UNSUPPORTED, "head_dim must be 256 or 512");
   CUtensorMap mq, mkv, mo;
   GLP_TRY(make_map16(&mq, qkv, T, qkv_width, qkv_width, glp::kFaBQ, true));
   GLP_TRY(make_map16(&mkv, qkv, T, qkv_width, qkv_width, glp::kFaBKV, true));
@@ -163,6 +189,7 @@ int ensure_kernel_attrs() {
   GLP_CUDA(cudaFuncSetAttribute(glp::gemm_rownorm_kernel<__half, 4>, A, static_cast<int>(glp::GemmRowCfgT<4>::SMEM)));
   GLP_CUDA(cudaFuncSetAttribute(glp::flash_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 static_cast<int>(glp::kFaSmem)));
+  GLP_CUDA(cudaFuncSetAttribute(glp::flash_attn_d512_kernel, A, static_cast<int>(glp::kF5Smem)));
   const int q256 = static_cast<int>(glp::Q8PairCfg<256>::SMEM), q128 = static_cast<int>(glp::Q8PairCfg<128>::SMEM);
   GLP_CUDA(cudaFuncSetAttribute(glp::gemm_q8_pair_kernel<glp::kEpiStore16, __nv_bfloat16, 256>, A, q256));
   GLP_CUDA(cudaFuncSetAttribute(glp::gemm_q8_pair_kernel<glp::kEpiStore16, __nv_bfloat16, 128>, A, q128));
@@ -467,6 +494,7 @@ struct Config {
   double eps = 1e-6, theta_swa = 1e4, theta_full = 1e6;
   std::vector<bool> sliding;
   std::vector<int> kv;  // KV heads per layer (config.rs:141-160: head_count_kv[i], global layers may differ)
+  std::vector<int> hd;  // head_dim per layer: key_length_swa on sliding layers, key_length on global ones
   uint32_t linear_type = glp::kGgmlQ8_0;
   int ple_dim = 0;  // per-layer-embedding width D; 0 = no PLE tensors (model.rs:257-275)
 };
@@ -510,12 +538,16 @@ int parse_config(const glp::GgufFile& g, Config* c) {
   const std::string kv_key = a + "attention.head_count_kv";
   c->n_kv = g.get_array_u32(kv_key, 0, &u) ? static_cast<int>(u) : 2;
   c->kv.assign(c->n_layers, c->n_kv);
+  c->hd.assign(c->n_layers, static_cast<int>(hd_swa));
   for (int i = 0; i < c->n_layers; ++i) {
     int kvi = c->n_kv;
     if (!c->sliding[i]) kvi = g.get_array_u32(kv_key, static_cast<size_t>(i), &u) ? static_cast<int>(u) : 1;
     const int hd = c->sliding[i] ? static_cast<int>(hd_swa) : static_cast<int>(hd_full);
-    if (hd != static_cast<int>(hd_swa))
-      return fail(GLP_ERR_UNSUPPORTED, "per-layer head_dim overrides are not supported (all layers must share head_dim)");
+    // sliding layers run 256-wide heads; global layers 256 or 512 (EmbeddingGemma 2's 512,
+    // config.rs:141-160, with the 512-wide RoPE of model.rs:279)
+    if (hd != 256 && !(hd == 512 && !c->sliding[i]))
+      return fail(GLP_ERR_UNSUPPORTED, "head_dim must be 256 (512 is supported on global layers)");
+    c->hd[i] = hd;
     if (kvi <= 0 || c->n_heads % kvi)
       return fail(GLP_ERR_FORMAT, "head_count must be a multiple of head_count_kv");
     c->kv[i] = kvi;
@@ -539,7 +571,7 @@ int parse_config(const glp::GgufFile& g, Config* c) {
 // Check every tensor the forward needs (names as in model.rs:251-473) before any device
 // work, so a malformed file fails without allocating.
 int validate_tensors(const glp::GgufFile& g, const Config& c) {
-  const int64_t H = c.hidden, F = c.ffn, D = c.head_dim;
+  const int64_t H = c.hidden, F = c.ffn;
   auto need = [&](const std::string& name, std::vector<int64_t> ne, bool matrix) -> int {
     const glp::GgufTensor* t = g.tensor(name);
     if (!t) return fail(GLP_ERR_FORMAT, "missing tensor " + name);
@@ -564,6 +596,7 @@ int validate_tensors(const glp::GgufFile& g, const Config& c) {
   }
   for (int l = 0; l < c.n_layers; ++l) {
     const std::string p = "blk." + std::to_string(l) + ".";
+    const int64_t D = c.hd[l];
     if (PD) {
       GLP_TRY(need(p + "inp_gate.weight", {H, PD}, true));
       GLP_TRY(need(p + "proj.weight", {PD, H}, true));
@@ -620,6 +653,7 @@ struct LayerW {
   float layer_scalar = 1.0f;
   bool sliding = true;
   int kv = 1, qkv_w = 0;  // KV heads and q|k|v width of this layer
+  int hd = 256;           // head_dim of this layer (512 on EmbeddingGemma 2's global layers)
   CUtensorMap m_qkv, m_o, m_gu, m_down;
   CUtensorMap p_qkv, p_o, p_gu, p_down;  // the same weights, 128-row boxes for CTA pairs
   // per-layer-embedding block (ple.rs:96-145): gate [D, H], projection [H, D], post-norm
@@ -652,6 +686,7 @@ struct Device {
   float* ple_norm = nullptr;
   CUtensorMap m_plew, p_plew;
   float2 *cs_swa = nullptr, *cs_full = nullptr;  // RoPE tables (sliding / global layers)
+  float2* cs_full512 = nullptr;                   // global layers with 512-wide heads
   int64_t cap_tokens = 0;
   int cap_seqs = 0;
   __nv_bfloat16* h = nullptr;  // residual stream
@@ -926,16 +961,22 @@ size_t load_staging_bytes(const glp::GgufFile& g, const Config& c) {
 // activations), without the load staging.  Computed from the file and the configuration
 // alone, so glp_open can hold it against the caller's limit before touching a device.
 int64_t device_plan_bytes(const glp::GgufFile& g, const Config& c, int64_t cap_tokens, int cap_seqs) {
-  const int64_t H = c.hidden, F = c.ffn, D = c.head_dim, AW = static_cast<int64_t>(c.n_heads) * D;
+  const int64_t H = c.hidden, F = c.ffn;
   const int64_t T = cap_tokens, S = cap_seqs, PD = c.ple_dim;
+  int64_t AW = 0;  // the widest layer's attention width
+  bool d512 = false;
+  for (int l = 0; l < c.n_layers; ++l) {
+    AW = std::max<int64_t>(AW, static_cast<int64_t>(c.n_heads) * c.hd[l]);
+    d512 = d512 || c.hd[l] == 512;
+  }
   auto b = [](int64_t count, int64_t elem) { return std::max<int64_t>(count, 1) * elem; };
   int64_t n = b(static_cast<int64_t>(g.tensor("token_embd.weight")->nbytes), 1);
   int64_t qkv_max = 0;
   for (int l = 0; l < c.n_layers; ++l) {
-    const int64_t W = (c.n_heads + 2 * c.kv[l]) * D;
+    const int64_t D = c.hd[l], W = (c.n_heads + 2 * c.kv[l]) * D;
     qkv_max = std::max(qkv_max, W);
-    n += 4 * b(H, 4) + 2 * b(D, 4);                                      // norm gains
-    n += b(W * H, 2) + b(H * AW, 2) + b(2 * F * H, 2) + b(H * F, 2);     // f16 linears
+    n += 4 * b(H, 4) + 2 * b(D, 4);                                            // norm gains
+    n += b(W * H, 2) + b(H * c.n_heads * D, 2) + b(2 * F * H, 2) + b(H * F, 2);  // f16 linears
     if (PD) n += b(H, 4) + b(PD * H, 2) + b(H * PD, 2);                  // PLE block
   }
   if (PD) n += b(PD, 4) + b(c.n_layers * PD * H, 2);
@@ -953,7 +994,8 @@ int64_t device_plan_bytes(const glp::GgufFile& g, const Config& c, int64_t cap_t
     n += b(t->ne[1] * H, 2);
     max_head = std::max(max_head, t->ne[1]);
   }
-  n += 2 * b(static_cast<int64_t>(c.max_pos) * (D / 2), 8);  // RoPE tables
+  n += 2 * b(static_cast<int64_t>(c.max_pos) * (c.head_dim / 2), 8);  // RoPE tables (256-wide heads)
+  if (d512) n += b(static_cast<int64_t>(c.max_pos) * 256, 8);       // global RoPE over 512 dims
   n += b(T * H, 2) + b(T * H, 4) + b(T * H, 2) + b(T * qkv_max, 2) + b(T * AW, 2) + b(T * H, 2) + b(T * F, 2);
   if (PD) n += b(T * c.n_layers * PD, 2) + b(T * PD, 2);
   n += b(T, 4) + b(S * max_head, 2) + b((T / glp::kPoolSeg + S + 1) * H, 4) + b(S * max_head, 2) +
@@ -968,9 +1010,13 @@ int setup_device(Device& d, const Config& c, const glp::GgufFile& g, int64_t cap
   GLP_CUDA(cudaEventCreate(&d.ev0));
   GLP_CUDA(cudaEventCreate(&d.ev1));
   const int H = c.hidden, F = c.ffn, D = c.head_dim;
-  const int AW = c.n_heads * D;
-  int QKV = 0;  // the widest layer's q|k|v width (the activation buffer)
-  for (int l = 0; l < c.n_layers; ++l) QKV = std::max(QKV, (c.n_heads + 2 * c.kv[l]) * D);
+  int QKV = 0, AW = 0;  // the widest layer's q|k|v and attention widths (the activation buffers)
+  bool d512 = false;
+  for (int l = 0; l < c.n_layers; ++l) {
+    QKV = std::max(QKV, (c.n_heads + 2 * c.kv[l]) * c.hd[l]);
+    AW = std::max(AW, c.n_heads * c.hd[l]);
+    d512 = d512 || c.hd[l] == 512;
+  }
 
   // token table: kept as raw Q8_0 (or bf16) rows, gathered per token
   const glp::GgufTensor* te = g.tensor("token_embd.weight");
@@ -1001,9 +1047,11 @@ int setup_device(Device& d, const Config& c, const glp::GgufFile& g, int64_t cap
     LayerW& L = d.layers[l];
     const std::string p = "blk." + std::to_string(l) + ".";
     L.sliding = c.sliding[l];
+    L.hd = c.hd[l];
+    const int DL = L.hd, AWL = c.n_heads * DL;  // this layer's head and attention widths
     GLP_TRY(upload_gain(d, g, p + "attn_norm.weight", H, &L.attn_norm));
-    GLP_TRY(upload_gain(d, g, p + "attn_q_norm.weight", D, &L.q_norm));
-    GLP_TRY(upload_gain(d, g, p + "attn_k_norm.weight", D, &L.k_norm));
+    GLP_TRY(upload_gain(d, g, p + "attn_q_norm.weight", DL, &L.q_norm));
+    GLP_TRY(upload_gain(d, g, p + "attn_k_norm.weight", DL, &L.k_norm));
     GLP_TRY(upload_gain(d, g, p + "post_attention_norm.weight", H, &L.post_attn));
     GLP_TRY(upload_gain(d, g, p + "ffn_norm.weight", H, &L.ffn_norm));
     GLP_TRY(upload_gain(d, g, p + "post_ffw_norm.weight", H, &L.post_ffw));
@@ -1012,25 +1060,25 @@ int setup_device(Device& d, const Config& c, const glp::GgufFile& g, int64_t cap
       std::memcpy(&L.layer_scalar, s->data, 4);
     }
     L.kv = c.kv[l];
-    L.qkv_w = (c.n_heads + 2 * L.kv) * D;
+    L.qkv_w = (c.n_heads + 2 * L.kv) * DL;
     GLP_TRY(d.alloc(&L.qkv, static_cast<size_t>(L.qkv_w) * H));
-    GLP_TRY(d.alloc(&L.o, static_cast<size_t>(H) * AW));
+    GLP_TRY(d.alloc(&L.o, static_cast<size_t>(H) * AWL));
     GLP_TRY(d.alloc(&L.gu, static_cast<size_t>(2 * F) * H));
     GLP_TRY(d.alloc(&L.down, static_cast<size_t>(H) * F));
-    GLP_TRY(upload_linear(d, g, p + "attn_q.weight", c.n_heads * D, H, L.qkv, 0, 0, 0, staging, staging_bytes));
-    GLP_TRY(upload_linear(d, g, p + "attn_k.weight", L.kv * D, H, L.qkv, c.n_heads * D, 0, 0, staging, staging_bytes));
-    GLP_TRY(upload_linear(d, g, p + "attn_v.weight", L.kv * D, H, L.qkv, (c.n_heads + L.kv) * D, 0, 0, staging,
+    GLP_TRY(upload_linear(d, g, p + "attn_q.weight", c.n_heads * DL, H, L.qkv, 0, 0, 0, staging, staging_bytes));
+    GLP_TRY(upload_linear(d, g, p + "attn_k.weight", L.kv * DL, H, L.qkv, c.n_heads * DL, 0, 0, staging, staging_bytes));
+    GLP_TRY(upload_linear(d, g, p + "attn_v.weight", L.kv * DL, H, L.qkv, (c.n_heads + L.kv) * DL, 0, 0, staging,
                           staging_bytes));
-    GLP_TRY(upload_linear(d, g, p + "attn_output.weight", H, AW, L.o, 0, 0, 0, staging, staging_bytes));
+    GLP_TRY(upload_linear(d, g, p + "attn_output.weight", H, AWL, L.o, 0, 0, 0, staging, staging_bytes));
     GLP_TRY(upload_linear(d, g, p + "ffn_gate.weight", F, H, L.gu, 0, 128, 256, staging, staging_bytes));
     GLP_TRY(upload_linear(d, g, p + "ffn_up.weight", F, H, L.gu, 128, 128, 256, staging, staging_bytes));
     GLP_TRY(upload_linear(d, g, p + "ffn_down.weight", H, F, L.down, 0, 0, 0, staging, staging_bytes));
     GLP_TRY(make_map16(&L.m_qkv, L.qkv, L.qkv_w, H, H, 256, true));
-    GLP_TRY(make_map16(&L.m_o, L.o, H, AW, AW, bn_for(H), true));
+    GLP_TRY(make_map16(&L.m_o, L.o, H, AWL, AWL, bn_for(H), true));
     GLP_TRY(make_map16(&L.m_gu, L.gu, 2 * F, H, H, 256, true));
     GLP_TRY(make_map16(&L.m_down, L.down, H, F, F, bn_for(H), true));
     GLP_TRY(make_map16(&L.p_qkv, L.qkv, L.qkv_w, H, H, 128, true));
-    GLP_TRY(make_map16(&L.p_o, L.o, H, AW, AW, 128, true));
+    GLP_TRY(make_map16(&L.p_o, L.o, H, AWL, AWL, 128, true));
     GLP_TRY(make_map16(&L.p_gu, L.gu, 2 * F, H, H, 128, true));
     GLP_TRY(make_map16(&L.p_down, L.down, H, F, F, 128, true));
     if (c.ple_dim) {
@@ -1090,6 +1138,7 @@ int setup_device(Device& d, const Config& c, const glp::GgufFile& g, int64_t cap
   if (d.head.back().n != c.emb_out) return fail(GLP_ERR_FORMAT, "head output dim != embedding_length_out");
   GLP_TRY(upload_rope(d, c.theta_swa, D, c.max_pos, &d.cs_swa));
   GLP_TRY(upload_rope(d, c.theta_full, D, c.max_pos, &d.cs_full));
+  if (d512) GLP_TRY(upload_rope(d, c.theta_full, 512, c.max_pos, &d.cs_full512));
 
   // activations for one launch chunk
   d.cap_tokens = cap_tokens;
@@ -1124,8 +1173,10 @@ int setup_device(Device& d, const Config& c, const glp::GgufFile& g, int64_t cap
 // sequences) only feeds the profiler's algorithmic work counts.
 int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_cu_chunk, const int* h_cu_chunk,
               int base, int n_seq, int T, int max_len, int out_dim, float* d_out, cudaStream_t st) {
-  const int H = c.hidden, F = c.ffn, D = c.head_dim;
-  const int QKV = d.layers.empty() ? 0 : d.layers[0].qkv_w, AW = c.n_heads * D;  // layer 0's q|k|v width
+  const int H = c.hidden, F = c.ffn;
+  // layer 0's q|k|v and attention widths (layers of other widths re-encode their maps)
+  const int QKV = d.layers.empty() ? 0 : d.layers[0].qkv_w;
+  const int AW = d.layers.empty() ? 0 : c.n_heads * d.layers[0].hd;
   const float eps = static_cast<float>(c.eps);
   const double Td = T;
   auto gemm_flops = [&](double m, double n, double k) { return 2.0 * m * n * k; };
@@ -1188,6 +1239,8 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
     CUtensorMap m_qkv_out2;  // the same for layers of another KV-head count (re-encoded when that width changes)
     int qkv_w2 = 0;
     GLP_TRY(make_map16(&m_attn, d.attn, T, AW, AW, 128, true));
+    CUtensorMap m_attn2;  // the attention output of layers of another width
+    int aw2 = 0;
     GLP_TRY(make_map16(&m_a, d.a, T, F, F, 128, true));
     double pairs_local = 0, pairs_global = 0;
     for (int b = 0; b < n_seq; ++b) {
@@ -1231,20 +1284,43 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
       p.n_q_heads = c.n_heads;
       p.n_kv_heads = L.kv;
       p.eps = eps;
-      GLP_TRY(prof_launch(d, st, kProfGemmQkv, gemm_flops(Td, W, H), gemm_bytes(Td, W, H, 2.0),
-                          [&] { return launch_gemm<__half>(m_x, L.m_qkv, 256, glp::kEpiQkv, p, st, &L.p_qkv, m_out); }));
+      const int DL = L.hd, AWL = c.n_heads * DL;
+      if (DL == 256) {
+        GLP_TRY(prof_launch(d, st, kProfGemmQkv, gemm_flops(Td, W, H), gemm_bytes(Td, W, H, 2.0),
+                            [&] { return launch_gemm<__half>(m_x, L.m_qkv, 256, glp::kEpiQkv, p, st, &L.p_qkv, m_out); }));
+      } else {
+        // 512-wide heads span two 256-column tiles: the GEMM stores, then a row kernel applies
+        // the per-head norms and the 512-wide RoPE (model.rs:279)
+        GLP_TRY(prof_launch(d, st, kProfGemmQkv, gemm_flops(Td, W, H), gemm_bytes(Td, W, H, 2.0),
+                            [&] { return launch_gemm<__half>(m_x, L.m_qkv, 256, glp::kEpiStore16, p, st, &L.p_qkv); }));
+        const int64_t head_rows = static_cast<int64_t>(T) * (c.n_heads + 2 * L.kv);
+        GLP_TRY(prof_launch(d, st, kProfMisc, 0.0, 4.0 * Td * W, [&] {
+          glp::qkv_norm_rope512_kernel<<<static_cast<unsigned>((head_rows + 7) / 8), 256, 0, st>>>(
+              d.qkv, T, c.n_heads, L.kv, L.q_norm, L.k_norm, d.cs_full512, c.max_pos, d.pos, eps);
+          GLP_CUDA(cudaGetLastError());
+          return GLP_OK;
+        }));
+      }
       // attention
       const double pairs = L.sliding ? pairs_local : pairs_global;
-      const double attn_bytes = 2.0 * Td * W + 2.0 * Td * AW;
-      GLP_TRY(prof_launch(d, st, kProfAttention, 4.0 * D * c.n_heads * pairs, attn_bytes, [&] {
+      const double attn_bytes = 2.0 * Td * W + 2.0 * Td * AWL;
+      GLP_TRY(prof_launch(d, st, kProfAttention, 4.0 * DL * c.n_heads * pairs, attn_bytes, [&] {
         return launch_attention(d.qkv, T, W, d_cu_chunk, base, n_seq, max_len, c.n_heads, L.kv,
-                                L.sliding ? c.window : 0, d.attn, d.status, st);
+                                L.sliding ? c.window : 0, d.attn, d.status, st, DL);
       }));
+      const CUtensorMap* m_att = &m_attn;
+      if (AWL != AW) {
+        if (AWL != aw2) {
+          GLP_TRY(make_map16(&m_attn2, d.attn, T, AWL, AWL, 128, true));
+          aw2 = AWL;
+        }
+        m_att = &m_attn2;
+      }
       // O projection
       GemmParams po{};
       po.M = T;
       po.N = H;
-      po.K = AW;
+      po.K = AWL;
       po.C = d.y;
       po.ldc = H;
       po.status = d.status;
@@ -1255,11 +1331,11 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
         po.w_next = L.ffn_norm;
         po.layer_scalar = 1.0f;
         po.eps = eps;
-        GLP_TRY(prof_launch(d, st, kProfGemmO, gemm_flops(Td, H, AW), gemm_bytes(Td, H, AW, 0.0) + fused_bytes,
-                            [&] { return launch_rownorm_gemm(m_attn, L.p_o, m_h, m_xo, po, st); }));
+        GLP_TRY(prof_launch(d, st, kProfGemmO, gemm_flops(Td, H, AWL), gemm_bytes(Td, H, AWL, 0.0) + fused_bytes,
+                            [&] { return launch_rownorm_gemm(*m_att, L.p_o, m_h, m_xo, po, st); }));
       } else {
-        GLP_TRY(prof_launch(d, st, kProfGemmO, gemm_flops(Td, H, AW), gemm_bytes(Td, H, AW, 2.0),
-                            [&] { return launch_gemm<__half>(m_attn, L.m_o, bn_for(H), glp::kEpiStore16, po, st, &L.p_o); }));
+        GLP_TRY(prof_launch(d, st, kProfGemmO, gemm_flops(Td, H, AWL), gemm_bytes(Td, H, AWL, 2.0),
+                            [&] { return launch_gemm<__half>(*m_att, L.m_o, bn_for(H), glp::kEpiStore16, po, st, &L.p_o); }));
         GLP_TRY(prof_launch(d, st, kProfPostNorm, 0.0, post_bytes, [&] {
           return with_hidden(H, [&](auto hc) {
             glp::post_norm_residual_kernel<decltype(hc)::value, glp::kPostNext>
@@ -2124,7 +2200,7 @@ int glp_bf16_gemm(const void* d_w_bf16, int N, int K, const void* d_x_bf16, int 
 
 int glp_flash_attention(const void* d_qkv, const int32_t* d_cu_seqlens, int n_seq, int max_len, int n_q_heads,
                         int n_kv_heads, int head_dim, int window, void* d_out, void* stream) {
-  if (head_dim != glp::kFaD) return fail(GLP_ERR_UNSUPPORTED, "head_dim must be 256");
+  if (head_dim != glp::kFaD && head_dim != glp::kF5D) return fail(GLP_ERR_UNSUPPORTED, "head_dim must be 256 or 512");
   if (n_seq < 0 || max_len < 0 || n_q_heads <= 0 || n_kv_heads <= 0 || n_q_heads % n_kv_heads)
     return fail(GLP_ERR_INVALID_ARG, "bad attention shape");
   if (n_seq == 0 || max_len == 0) return GLP_OK;
@@ -2139,7 +2215,7 @@ int glp_flash_attention(const void* d_qkv, const int32_t* d_cu_seqlens, int n_se
   GLP_CUDA(cudaMemcpy(&total, d_cu_seqlens + n_seq, sizeof(int), cudaMemcpyDeviceToHost));
   return launch_attention(static_cast<const __half*>(d_qkv), total, ld, d_cu_seqlens, 0, n_seq, max_len, n_q_heads,
                           n_kv_heads, window, static_cast<__half*>(d_out), status,
-                          static_cast<cudaStream_t>(stream));
+                          static_cast<cudaStream_t>(stream), head_dim);
 }
 
 // Variant of glp_q8_0_gemm for callers that cannot allocate device memory: the dequantised

@@ -354,3 +354,72 @@ __global__ void l2_mrl_kernel(const float* __restrict__ e, int n_seq, int dim, i
 }
 
 }  // namespace glp
+
+namespace glp {
+
+// ---------------------------------------------------------------------------- 512-wide heads
+// Per-head RMSNorm + NeoX RoPE of the QKV GEMM's output for layers with head_dim 512 (the
+// 256-wide heads have it fused into the GEMM epilogue): qkv [T, (Hq + 2 Hkv) * 512] f16 in
+// place.  One warp per (token, head): lane l holds dims 8l .. 8l + 7 of the lower half and
+// 256 + 8l .. of the upper half, i.e. its 8 RoPE pairs (i, i + 256).  Query heads take
+// q_gain, key heads k_gain (both then rotated with the table cs [256][rope_stride] of
+// {cos, sin}, rope.rs:14-106 values), value heads are normalised without a gain
+// (attention/mod.rs:166-188, model.rs:371-373).
+__global__ void qkv_norm_rope512_kernel(__half* __restrict__ qkv, int64_t T, int n_q_heads, int n_kv_heads,
+                                        const float* __restrict__ q_gain, const float* __restrict__ k_gain,
+                                        const float2* __restrict__ cs, int rope_stride, const int* __restrict__ pos,
+                                        float eps) {
+  const int heads = n_q_heads + 2 * n_kv_heads;
+  const int64_t wid = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (wid >= T * heads) return;
+  const int lane = threadIdx.x & 31;
+  const int64_t t = wid / heads;
+  const int h = static_cast<int>(wid - t * heads);
+  __half* row = qkv + t * static_cast<int64_t>(heads) * 512 + static_cast<int64_t>(h) * 512;
+  uint4 lo4 = reinterpret_cast<const uint4*>(row)[lane];
+  uint4 hi4 = reinterpret_cast<const uint4*>(row + 256)[lane];
+  const __half* lo = reinterpret_cast<const __half*>(&lo4);
+  const __half* hi = reinterpret_cast<const __half*>(&hi4);
+  float x1[8], x2[8];
+  float ss = 0.f;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    x1[e] = __half2float(lo[e]);
+    x2[e] = __half2float(hi[e]);
+    ss = fmaf(x1[e], x1[e], ss);
+    ss = fmaf(x2[e], x2[e], ss);
+  }
+  ss = warp_sum(ss);
+  const float inv = 1.0f / sqrtf(ss / 512.0f + eps);
+  const bool is_q = h < n_q_heads, is_k = !is_q && h < n_q_heads + n_kv_heads;
+  const float* gain = is_q ? q_gain : (is_k ? k_gain : nullptr);
+  const int p = (is_q || is_k) ? min(max(pos[t], 0), rope_stride - 1) : 0;
+  uint32_t olo[4], ohi[4];
+#pragma unroll
+  for (int e = 0; e < 8; e += 2) {
+    float a[2], b[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int i = 8 * lane + e + u;
+      float v1 = x1[e + u] * inv, v2 = x2[e + u] * inv;
+      if (gain) {
+        v1 *= __ldg(gain + i);
+        v2 *= __ldg(gain + 256 + i);
+      }
+      if (is_q || is_k) {  // x cos + rotate_half(x) sin, rotate_half = cat(-x2, x1)
+        const float2 c = __ldg(cs + static_cast<size_t>(i) * rope_stride + p);
+        a[u] = v1 * c.x + (-v2) * c.y;
+        b[u] = v2 * c.x + v1 * c.y;
+      } else {
+        a[u] = v1;
+        b[u] = v2;
+      }
+    }
+    olo[e / 2] = pack_f16(a[0], a[1]);
+    ohi[e / 2] = pack_f16(b[0], b[1]);
+  }
+  reinterpret_cast<uint4*>(row)[lane] = make_uint4(olo[0], olo[1], olo[2], olo[3]);
+  reinterpret_cast<uint4*>(row + 256)[lane] = make_uint4(ohi[0], ohi[1], ohi[2], ohi[3]);
+}
+
+}  // namespace glp

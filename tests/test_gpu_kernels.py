@@ -158,9 +158,8 @@ def test_gemm_rejects_bad_shapes():
     assert e.value.code == api.GLP_ERR_INVALID_ARG
 
 
-def _attn_case(lengths, n_heads, n_kv, window, seed, logit_scale=1.0):
+def _attn_case(lengths, n_heads, n_kv, window, seed, logit_scale=1.0, d=256):
     rng = np.random.default_rng(seed)
-    d = 256
     t = int(sum(lengths))
     width = (n_heads + 2 * n_kv) * d
     qkv = rng.standard_normal((t, width), dtype=np.float32)
@@ -202,3 +201,11 @@ def test_flash_attention_gqa_and_sharp_logits():
     _attn_case([257, 64], 4, 2, 512, seed=5)
     # BASELINE-like logit spread (unit-gain q/k norms, scale 1.0): std ~16
     _attn_case([512], 3, 1, 0, seed=6, logit_scale=16.0)
+
+
+@pytest.mark.parametrize("lengths", [[1], [7, 64, 100], [300, 512, 33], [700]])
+@pytest.mark.parametrize("window", [0, 512])
+def test_flash_attention_head_dim_512(lengths, window):
+    """512-wide heads (EmbeddingGemma 2's global layers): 4 query heads over 1 and 2 KV heads."""
+    _attn_case(lengths, 4, 1, window, seed=sum(lengths) + 3 * window, d=512)
+    _attn_case(lengths, 4, 2, window, seed=sum(lengths) + 3 * window + 1, d=512)

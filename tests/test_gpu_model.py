@@ -234,7 +234,7 @@ def test_per_layer_embeddings(gguf_dir, kw):
 
 def test_committed_golden_vectors(gguf_dir):
     """The GPU path against the committed oracle fixtures (tests/golden/manifest.json) with the
-    gates above, for the conditioned cases; the head_dim-512 case is rejected at load."""
+    gates above, for the conditioned cases (the head_dim-512 global layers included)."""
     import json
     import os
     golden = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
@@ -243,11 +243,6 @@ def test_committed_golden_vectors(gguf_dir):
     for case in man["cases"]:
         cfg = synth.EncoderConfig(**case["config"])
         path = synth.ensure_gguf(os.path.join(str(gguf_dir), "golden_" + case["name"] + ".gguf"), cfg, case["seed"])
-        if cfg.global_head_dim:
-            with pytest.raises(GlyprError) as e:
-                GlyprEmbedder.load_gguf(path, [0])
-            assert e.value.code == api.GLP_ERR_UNSUPPORTED
-            continue
         if cfg.qk_gain_scale == 1.0:
             continue  # BASELINE init: chaotic under rounding (module doc), checked by properties
         data = np.load(os.path.join(golden, case["file"]))
@@ -260,4 +255,30 @@ def test_committed_golden_vectors(gguf_dir):
         gap = 1.0 - cosine_rows(m1, m2)
         assert (cosine_rows(got, m1) >= np.minimum(COS_GATE, 1.0 - 2.0 * gap - 2e-5)).all(), case["name"]
         checked += 1
-    assert checked >= 4
+    assert checked >= 5
+
+
+@pytest.mark.parametrize("kw", [
+    # EmbeddingGemma 2's structure: hidden 512, 4 query heads over 2 KV heads on sliding layers,
+    # 1 KV head of 512 dims on the global layer, per-layer embeddings
+    dict(n_layers=6, hidden=512, n_heads=4, n_kv_heads=2, global_kv_heads=1, global_head_dim=512, ffn=2048,
+         head_dims=(768,), ple_dim=256),
+    # BASELINE widths with 512-wide global heads (3 query heads, 1 KV head), no PLE
+    dict(n_layers=6, global_head_dim=512),
+])
+def test_global_layers_head_dim_512(gguf_dir, kw):
+    """Global layers with 512-wide heads: the QKV GEMM plus the 512-wide norm/RoPE row kernel,
+    the two-CTA tcgen05 attention, the wider O projection; parity with the oracle and
+    batch == single."""
+    import os
+    cfg = synth.small_config(qk_gain_scale=0.25, **kw)
+    path = synth.ensure_gguf(os.path.join(str(gguf_dir), f"d512_{cfg.hidden}_{cfg.ple_dim}.gguf"), cfg)
+    orc = oracle.OracleModel(path)
+    ids, lens = synth.make_batch(4, 600, orc.vocab, lengths=[600, 513, 64, 1])
+    with GlyprEmbedder.load_gguf(path, [0]) as emb:
+        got = emb.embed_tokens(ids, lens)
+        one = emb.embed_tokens(ids[1:2, : lens[1]], lens[1:2])
+        assert emb.device_status() == 0
+    np.testing.assert_array_equal(one[0], got[1])
+    np.testing.assert_allclose(np.linalg.norm(got, axis=1), 1.0, atol=1e-5)
+    _check_both(got, orc, ids, lens)

@@ -145,21 +145,29 @@ def test_open_accepts_global_kv_heads(tmp_path):
     assert rc == api.GLP_ERR_FORMAT and msg == "head_count must be a multiple of head_count_kv"
 
 
-def test_open_rejects_global_head_dim_512(tmp_path):
-    """The real EmbeddingGemma 2's head_dim-512 global layers: parsed (the oracle runs them) but
-    not supported by the CUDA attention, which holds 256-wide heads."""
+def test_open_accepts_global_head_dim_512(tmp_path):
+    """The real EmbeddingGemma 2's head_dim-512 global layers (config.rs:141-160, 512-wide RoPE
+    at model.rs:279) pass every format and support check; without a GPU the open then stops
+    at the first CUDA call."""
     cfg = synth.small_config(n_layers=6, vocab=256, hidden=512, n_heads=4, n_kv_heads=2, global_kv_heads=1,
                              global_head_dim=512, head_dims=(512,))
     rc, msg = _open(synth.write_gguf(str(tmp_path / "d512.gguf"), cfg))
-    assert rc == api.GLP_ERR_UNSUPPORTED and msg.startswith("per-layer head_dim overrides are not supported")
+    assert rc not in (api.GLP_ERR_UNSUPPORTED, api.GLP_ERR_FORMAT), msg
 
 
-def test_open_rejects_head_dim_override(tmp_path):
+def test_open_rejects_head_dim_other_than_256_or_512(tmp_path):
+    cfg = synth.small_config(n_layers=6, vocab=256, global_head_dim=384)
+    rc, msg = _open(synth.write_gguf(str(tmp_path / "d384.gguf"), cfg))
+    assert rc == api.GLP_ERR_UNSUPPORTED and msg == "head_dim must be 256 (512 is supported on global layers)"
+
+
+def test_open_head_dim_default_512_needs_512_wide_tensors(tmp_path):
     cfg = synth.small_config(n_layers=6, vocab=256)
     p = synth.write_gguf(str(tmp_path / "hd.gguf"), cfg, drop={"gemma-embedding2.attention.key_length"})
-    # key_length defaults to 512 for the global layer (config.rs:143-144): not supported here
+    # key_length defaults to 512 for the global layer (config.rs:143-144); this file's global
+    # layer has 256-wide tensors, so its shapes do not match
     rc, msg = _open(p)
-    assert rc == api.GLP_ERR_UNSUPPORTED and "head_dim" in msg
+    assert rc == api.GLP_ERR_FORMAT and msg == "bad shape for blk.5.attn_q_norm.weight"
 
 
 def test_util_mirrors():
