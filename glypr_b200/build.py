@@ -11,7 +11,7 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libglypr_cuda.so")
 SOURCES = ["glypr_cuda.cu", "gguf.cpp", "engine.cpp", "tokenizer.cpp"]
-HEADERS = ["common.cuh", "gemm.cuh", "q8gemm.cuh", "attention_tc.cuh", "rowops.cuh", "gguf.h", "unicode_case.inc"]
+HEADERS = ["common.cuh", "gemm.cuh", "q8gemm.cuh", "attention_tc.cuh", "attention_d512.cuh", "attention_pair.cuh", "rowops.cuh", "gguf.h", "unicode_case.inc"]
 
 
 def nvcc() -> str:

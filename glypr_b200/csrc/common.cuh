@@ -434,6 +434,16 @@ __device__ __forceinline__ void umma_f16_pair(uint32_t d_tmem, uint64_t adesc, u
       "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
+// The same with A read from tensor memory: each CTA's 128 rows of A in its own tensor memory
+// at column a_tmem (two 16-bit elements per 32-bit column, the lower K index in the low half).
+__device__ __forceinline__ void umma_f16_pair_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                                 uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
 // arrive once on the mbarrier at `cluster_addr` (this CTA's or the peer's) when every pair MMA
 // issued so far by this thread has completed
 __device__ __forceinline__ void umma_commit_pair(uint32_t cluster_addr) {

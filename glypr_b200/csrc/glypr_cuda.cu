@@ -27,6 +27,7 @@
 
 #include "attention_tc.cuh"
 #include "attention_d512.cuh"
+#include "attention_pair.cuh"
 #include "gemm.cuh"
 #include "gguf.h"
 #include "glypr_cuda.h"
@@ -128,6 +129,33 @@ int launch_attention(const __half* qkv, int64_t T, int qkv_width, const int* cu,
     return GLP_OK;
   }
   if (head_dim != glp::kFaD) return fail(GLP_ERR_UNSUPPORTED, "head_dim must be 256 or 512");
+  // 256-wide heads: CTA pairs over 256-query blocks and 128-key tiles (GLP_ATTENTION=single:
+  // the one-CTA kernel over 128-query blocks and 64-key tiles)
+  const char* attn_env = std::getenv("GLP_ATTENTION");  // read per call (A/B measurements)
+  const bool single = attn_env && std::strcmp(attn_env, "single") == 0;
+  if (!single) {
+    CUtensorMap mqv, mk, mo;
+    GLP_TRY(make_map16(&mqv, qkv, T, qkv_width, qkv_width, glp::kFpBQ, true));
+    GLP_TRY(make_map16(&mk, qkv, T, qkv_width, qkv_width, 64, true));
+    GLP_TRY(make_map16(&mo, out, T, static_cast<int64_t>(n_q_heads) * glp::kFaD,
+                       static_cast<int64_t>(n_q_heads) * glp::kFaD, glp::kFaOutBoxRows, true));
+    glp::FaParams fp{};
+    fp.cu_seqlens = cu;
+    fp.cu_base = cu_base;
+    fp.n_seq = n_seq;
+    fp.q_blocks = (max_len + 2 * glp::kFpBQ - 1) / (2 * glp::kFpBQ);
+    fp.n_q_heads = n_q_heads;
+    fp.n_kv_heads = n_kv_heads;
+    fp.window = window;
+    fp.out = out;
+    fp.ld_out = n_q_heads * glp::kFaD;
+    fp.status = status;
+    const int64_t items = static_cast<int64_t>(n_seq) * fp.q_blocks * n_q_heads;
+    const int pairs = static_cast<int>(std::min<int64_t>(items, std::max(1, sm_count() / 2)));
+    glp::flash_attn_pair_kernel<<<2 * pairs, glp::kFaThreads, glp::kFpSmem, st>>>(mqv, mk, mo, fp);
+    GLP_CUDA(cudaGetLastError());
+    return GLP_OK;
+  }
   CUtensorMap mq, mkv, mo;
   GLP_TRY(make_map16(&mq, qkv, T, qkv_width, qkv_width, glp::kFaBQ, true));
   GLP_TRY(make_map16(&mkv, qkv, T, qkv_width, qkv_width, glp::kFaBKV, true));
@@ -190,6 +218,7 @@ int ensure_kernel_attrs() {
   GLP_CUDA(cudaFuncSetAttribute(glp::flash_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 static_cast<int>(glp::kFaSmem)));
   GLP_CUDA(cudaFuncSetAttribute(glp::flash_attn_d512_kernel, A, static_cast<int>(glp::kF5Smem)));
+  GLP_CUDA(cudaFuncSetAttribute(glp::flash_attn_pair_kernel, A, static_cast<int>(glp::kFpSmem)));
   const int q256 = static_cast<int>(glp::Q8PairCfg<256>::SMEM), q128 = static_cast<int>(glp::Q8PairCfg<128>::SMEM);
   GLP_CUDA(cudaFuncSetAttribute(glp::gemm_q8_pair_kernel<glp::kEpiStore16, __nv_bfloat16, 256>, A, q256));
   GLP_CUDA(cudaFuncSetAttribute(glp::gemm_q8_pair_kernel<glp::kEpiStore16, __nv_bfloat16, 128>, A, q128));
@@ -923,7 +952,9 @@ int upload_linear(Device& d, const glp::GgufFile& g, const std::string& name, in
 // epilogue's 32 lanes (consecutive rows = consecutive positions) read one coalesced line.
 // RoPE table, frequency-major with cos and sin of one (frequency, position) side by side:
 // cs[i * max_pos + p] = {cos(p * inv_freq_i), sin(p * inv_freq_i)} (rope.rs:14-76 values)
-int upload_rope(Device& d, double theta, int d_head, int max_pos, float2** cs) {
+// position_major: cs[p * half + i] instead (the 512-wide row kernel reads a lane's 8
+// consecutive frequencies of one position).
+int upload_rope(Device& d, double theta, int d_head, int max_pos, float2** cs, bool position_major = false) {
   const int half = d_head / 2;
   std::vector<float> inv(half);
   std::vector<float2> c(static_cast<size_t>(max_pos) * half);
@@ -931,7 +962,8 @@ int upload_rope(Device& d, double theta, int d_head, int max_pos, float2** cs) {
   for (int i = 0; i < half; ++i)
     for (int p = 0; p < max_pos; ++p) {
       const float f = static_cast<float>(p) * inv[i];
-      c[static_cast<size_t>(i) * max_pos + p] = make_float2(std::cos(f), std::sin(f));
+      const size_t at = position_major ? static_cast<size_t>(p) * half + i : static_cast<size_t>(i) * max_pos + p;
+      c[at] = make_float2(std::cos(f), std::sin(f));
     }
   GLP_TRY(d.alloc(cs, c.size()));
   GLP_CUDA(cudaMemcpy(*cs, c.data(), c.size() * sizeof(float2), cudaMemcpyHostToDevice));
@@ -1138,7 +1170,7 @@ int setup_device(Device& d, const Config& c, const glp::GgufFile& g, int64_t cap
   if (d.head.back().n != c.emb_out) return fail(GLP_ERR_FORMAT, "head output dim != embedding_length_out");
   GLP_TRY(upload_rope(d, c.theta_swa, D, c.max_pos, &d.cs_swa));
   GLP_TRY(upload_rope(d, c.theta_full, D, c.max_pos, &d.cs_full));
-  if (d512) GLP_TRY(upload_rope(d, c.theta_full, 512, c.max_pos, &d.cs_full512));
+  if (d512) GLP_TRY(upload_rope(d, c.theta_full, 512, c.max_pos, &d.cs_full512, true));
 
   // activations for one launch chunk
   d.cap_tokens = cap_tokens;
@@ -1294,7 +1326,7 @@ int run_chunk(const Config& c, Device& d, const int* d_ids_chunk, const int* d_c
         GLP_TRY(prof_launch(d, st, kProfGemmQkv, gemm_flops(Td, W, H), gemm_bytes(Td, W, H, 2.0),
                             [&] { return launch_gemm<__half>(m_x, L.m_qkv, 256, glp::kEpiStore16, p, st, &L.p_qkv); }));
         const int64_t head_rows = static_cast<int64_t>(T) * (c.n_heads + 2 * L.kv);
-        GLP_TRY(prof_launch(d, st, kProfMisc, 0.0, 4.0 * Td * W, [&] {
+        GLP_TRY(prof_launch(d, st, kProfGemmQkv, 0.0, 4.0 * Td * W, [&] {
           glp::qkv_norm_rope512_kernel<<<static_cast<unsigned>((head_rows + 7) / 8), 256, 0, st>>>(
               d.qkv, T, c.n_heads, L.kv, L.q_norm, L.k_norm, d.cs_full512, c.max_pos, d.pos, eps);
           GLP_CUDA(cudaGetLastError());
@@ -2144,11 +2176,11 @@ int glp_q8_0_gemm(const void* d_q8_w, int N, int K, const void* d_x_bf16, int M,
   // into library scratch and the bf16 CTA-pair GEMM runs (M = 131072: 124 vs 170 us; the
   // fused kernel's tensor pipe waits on the dequantisation warps there).  A weight that is not
   // 16-byte aligned (a row slice of a fused weight) always takes the second route.
-  // GLP_Q8_GEMM=fused or =two-pass forces one route (for A/B measurements).
-  static const int route = [] {
+  // GLP_Q8_GEMM=fused or =two-pass forces one route (for A/B measurements; read on every call).
+  const int route = [] {
     const char* e = std::getenv("GLP_Q8_GEMM");
-    if (e && std::string(e) == "two-pass") return 2;
-    if (e && std::string(e) == "fused") return 1;
+    if (e && std::strcmp(e, "two-pass") == 0) return 2;
+    if (e && std::strcmp(e, "fused") == 0) return 1;
     return 0;
   }();
   constexpr int kFusedMaxM = 8192;

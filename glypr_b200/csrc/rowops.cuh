@@ -362,9 +362,9 @@ namespace glp {
 // 256-wide heads have it fused into the GEMM epilogue): qkv [T, (Hq + 2 Hkv) * 512] f16 in
 // place.  One warp per (token, head): lane l holds dims 8l .. 8l + 7 of the lower half and
 // 256 + 8l .. of the upper half, i.e. its 8 RoPE pairs (i, i + 256).  Query heads take
-// q_gain, key heads k_gain (both then rotated with the table cs [256][rope_stride] of
-// {cos, sin}, rope.rs:14-106 values), value heads are normalised without a gain
-// (attention/mod.rs:166-188, model.rs:371-373).
+// q_gain, key heads k_gain (both then rotated with the position-major table cs [pos][256] of
+// {cos, sin}, rope.rs:14-106 values: a lane's 8 frequencies are 64 contiguous bytes), value
+// heads are normalised without a gain (attention/mod.rs:166-188, model.rs:371-373).
 __global__ void qkv_norm_rope512_kernel(__half* __restrict__ qkv, int64_t T, int n_q_heads, int n_kv_heads,
                                         const float* __restrict__ q_gain, const float* __restrict__ k_gain,
                                         const float2* __restrict__ cs, int rope_stride, const int* __restrict__ pos,
@@ -407,7 +407,7 @@ __global__ void qkv_norm_rope512_kernel(__half* __restrict__ qkv, int64_t T, int
         v2 *= __ldg(gain + 256 + i);
       }
       if (is_q || is_k) {  // x cos + rotate_half(x) sin, rotate_half = cat(-x2, x1)
-        const float2 c = __ldg(cs + static_cast<size_t>(i) * rope_stride + p);
+        const float2 c = __ldg(cs + static_cast<size_t>(p) * 256 + i);
         a[u] = v1 * c.x + (-v2) * c.y;
         b[u] = v2 * c.x + v1 * c.y;
       } else {

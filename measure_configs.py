@@ -119,12 +119,17 @@ def config1(torch, emb, report):
 
 
 def config2(torch, report):
+    """glp_q8_0_gemm: the default route and both forced routes (GLP_Q8_GEMM, read per call)."""
     p_t, p_b, src = peaks()
     report.append("## Config 2 — Q8_0 × bf16 GEMM (`glp_q8_0_gemm`, bf16 out)\n")
-    report.append(f"Peaks: {p_t:.0f} TFLOP/s, {p_b:.0f} GB/s ({src}). Time includes the per-call "
-                  "dequantisation of the Q8_0 weight.\n")
-    report.append("| W [N×K] | M | ms | TFLOP/s | GB/s | % of roofline |\n|---|---:|---:|---:|---:|---:|")
+    report.append(f"Peaks: {p_t:.0f} TFLOP/s, {p_b:.0f} GB/s ({src}). Times are per call (CUDA events, "
+                  "median of 10 after 3 warm-ups). Routes: *fused* = one launch streaming the raw Q8_0 rows "
+                  "by TMA and dequantising in shared memory; *two-pass* = dequantise into library scratch, "
+                  "then the bf16 CTA-pair GEMM; *default* = fused up to M = 8,192, two-pass above.\n")
+    report.append("| W [N×K] | M | default ms | % of roofline | fused ms | two-pass ms |\n"
+                  "|---|---:|---:|---:|---:|---:|")
     rng = np.random.default_rng(synth.MASTER_SEED + 22)
+    st = torch.cuda.current_stream().cuda_stream  # the stream the timing events are recorded on
     for n, k in ((768, 768), (256, 768), (1152, 768), (768, 1152)):
         w = (rng.standard_normal((n, k), dtype=np.float32) * np.float32(0.02)).astype(np.float32)
         blocks = synth.quantize_q8_0(w)
@@ -132,15 +137,78 @@ def config2(torch, report):
         for m in (512, 4096, 32768, 131072):
             x = torch.randn((m, k), device="cuda").to(torch.bfloat16)
             y = torch.empty((m, n), device="cuda", dtype=torch.bfloat16)
-            st = torch.cuda.current_stream().cuda_stream  # the stream the timing events are recorded on
-            ms = timed(torch, lambda: api.q8_0_gemm(d_w.data_ptr(), n, k, x.data_ptr(), m, y.data_ptr(), False, st))
+            ms = {}
+            for route in ("default", "fused", "two-pass"):
+                if route == "default":
+                    os.environ.pop("GLP_Q8_GEMM", None)
+                else:
+                    os.environ["GLP_Q8_GEMM"] = route
+                ms[route] = timed(torch, lambda: api.q8_0_gemm(d_w.data_ptr(), n, k, x.data_ptr(), m, y.data_ptr(),
+                                                                 False, st))
+            os.environ.pop("GLP_Q8_GEMM", None)
             flop = 2.0 * m * n * k
             byts = n * k / 32 * 34 + 2.0 * m * k + 2.0 * m * n
             roof_ms = max(flop / (p_t * 1e9), byts / (p_b * 1e6))
-            report.append(f"| {n}×{k} | {m} | {ms:.4f} | {flop / ms / 1e9:.0f} | {byts / ms / 1e6:.0f} | "
-                          f"{100 * roof_ms / ms:.1f} |")
+            report.append(f"| {n}×{k} | {m} | {ms['default']:.4f} | {100 * roof_ms / ms['default']:.1f} | "
+                          f"{ms['fused']:.4f} | {ms['two-pass']:.4f} |")
             del x, y
     report.append("")
+
+
+def attention_ab(torch, report):
+    """glp_flash_attention on the bench's shapes: the CTA-pair kernel (default) against the
+    one-CTA kernel (GLP_ATTENTION=single), same inputs."""
+    p_t, _, src = peaks()
+    report.append("## Attention — CTA-pair kernel vs one-CTA kernel (`glp_flash_attention`, head_dim 256)\n")
+    report.append(f"3 query heads over 1 KV head, f16 qkv with unit-RMS q/k scaled to logit std 16 (the BASELINE "
+                  f"init's spread); median of 10 calls; TFLOP/s of the visible (query, key) pairs, peak {p_t:.0f} ({src}).\n")
+    report.append("| sequences x length | window | pair ms | pair TFLOP/s | single ms | single TFLOP/s |\n"
+                  "|---|---:|---:|---:|---:|---:|")
+    rng = np.random.default_rng(synth.MASTER_SEED + 66)
+    for n_seq, L in ((512, 512), (1, 8192)):
+        t = n_seq * L
+        qkv = rng.standard_normal((t, 5 * 256), dtype=np.float32)
+        d_qkv = torch.from_numpy(qkv.astype(np.float16)).cuda()
+        d_cu = torch.from_numpy(np.arange(0, (n_seq + 1) * L, L, dtype=np.int32)).cuda()
+        out = torch.empty((t, 3 * 256), dtype=torch.float16, device="cuda")
+        st = torch.cuda.current_stream().cuda_stream
+        for window in (0, 512):
+            if window:
+                i = np.arange(L)
+                vis = float((np.minimum(L - 1, i + window) - np.maximum(0, i - window) + 1).sum()) * n_seq
+            else:
+                vis = float(L) * L * n_seq
+            flop = 4.0 * 256 * 3 * vis
+            ms = {}
+            for route in ("pair", "single"):
+                if route == "single":
+                    os.environ["GLP_ATTENTION"] = "single"
+                else:
+                    os.environ.pop("GLP_ATTENTION", None)
+                ms[route] = timed(torch, lambda: api.flash_attention(d_qkv.data_ptr(), d_cu.data_ptr(), n_seq, L, 3, 1,
+                                                                     256, window, out.data_ptr(), st))
+            os.environ.pop("GLP_ATTENTION", None)
+            report.append(f"| {n_seq} x {L} | {window} | {ms['pair']:.3f} | {flop / ms['pair'] / 1e9:.0f} | "
+                          f"{ms['single']:.3f} | {flop / ms['single'] / 1e9:.0f} |")
+        del d_qkv, out
+    report.append("")
+
+
+def q8_one(torch, spec):
+    """One glp_q8_0_gemm shape on one route, 5 calls (a small case for ncu): N,K,M,route."""
+    n, k, m, route = spec.split(",")
+    n, k, m = int(n), int(k), int(m)
+    os.environ["GLP_Q8_GEMM"] = route
+    rng = np.random.default_rng(synth.MASTER_SEED + 22)
+    blocks = synth.quantize_q8_0(rng.standard_normal((n, k), dtype=np.float32) * np.float32(0.02))
+    d_w = torch.from_numpy(blocks.view(np.uint8).reshape(-1).copy()).cuda()
+    x = torch.randn((m, k), device="cuda").to(torch.bfloat16)
+    y = torch.empty((m, n), device="cuda", dtype=torch.bfloat16)
+    st = torch.cuda.current_stream().cuda_stream
+    ms = timed(torch, lambda: api.q8_0_gemm(d_w.data_ptr(), n, k, x.data_ptr(), m, y.data_ptr(), False, st),
+               warm=2, reps=3)
+    print(f"{n}x{k} M={m} {route}: {ms * 1e3:.1f} us, {2.0 * m * n * k / ms / 1e9:.0f} TFLOP/s, "
+          f"status {api.kernel_status(0)}")
 
 
 def config3(torch, emb, report):
@@ -203,7 +271,7 @@ def config4(torch, path, report):
 
 
 EMBEDDINGGEMMA2_SHAPE = synth.EncoderConfig(hidden=512, ffn=2048, n_heads=4, n_kv_heads=2, global_kv_heads=1,
-                                            head_dims=(768,), ple_dim=512)
+                                            head_dims=(768,), ple_dim=512, global_head_dim=512)
 
 
 def ple_config(torch, path, report, n=1024):
@@ -222,8 +290,9 @@ def ple_config(torch, path, report, n=1024):
         emb.profile_enable(False)
     total = sum(v["ms"] for k, v in prof.items() if not k.startswith("_"))
     report.append("## Per-layer embeddings — EmbeddingGemma-2-shaped Q8_0 model, 512-token sequences\n")
-    report.append(f"24 layers, hidden 512, FFN 2048, 4 query heads over 2 KV heads (1 on the global layers), "
-                  f"per-layer inputs of 512, head 512 -> 768, head_dim 256 throughout. {n} sequences: "
+    report.append(f"24 layers, hidden 512, FFN 2048, 4 query heads over 2 KV heads of 256 on the sliding layers "
+                  f"and 1 KV head of 512 on the global layers (EmbeddingGemma 2's widths), per-layer inputs of "
+                  f"512, head 512 -> 768. {n} sequences: "
                   f"{ms:.1f} ms per batch, {n / ms * 1e3:.0f} embeddings/s (device-resident ids).\n")
     report.append("Per kernel (one batch, library CUDA-event profile):\n")
     report.append("| kernel | launches | ms | share | TFLOP/s | GB/s |\n|---|---:|---:|---:|---:|---:|")
@@ -356,9 +425,14 @@ def main(argv=None) -> None:
     ap.add_argument("--model-dir", default=os.environ.get("GLYPR_BENCH_DIR", "/tmp/glypr_models"))
     ap.add_argument("--out", default=None)
     ap.add_argument("--configs", default="1,2,3,4,serving")
+    ap.add_argument("--q8-one", default=None, help="N,K,M,route: one glp_q8_0_gemm case (for ncu), nothing else")
     args = ap.parse_args(argv)
     import torch
     torch.backends.cuda.matmul.allow_tf32 = False
+    if args.q8_one:
+        api.load_library()
+        q8_one(torch, args.q8_one)
+        return
     os.makedirs(args.model_dir, exist_ok=True)
     want = set(int(c) if c.isdigit() else c for c in args.configs.split(","))
     report = [f"# BASELINE configs 1–4 on one {torch.cuda.get_device_name(0)}\n",
@@ -384,6 +458,8 @@ def main(argv=None) -> None:
         text_path(torch, args.model_dir, report)
     if 2 in want:
         config2(torch, report)
+    if "attn" in want:
+        attention_ab(torch, report)
     if "ple" in want:
         pl = synth.ensure_gguf(os.path.join(args.model_dir, "embeddinggemma2_shape_q8_0.gguf"), EMBEDDINGGEMMA2_SHAPE)
         ple_config(torch, pl, report)
