@@ -12,19 +12,26 @@
 // (16 MMAs, both operands in shared memory) and O += P_j V_j is M=256, N=256, K=128 (8 MMAs, P
 // from tensor memory, V MN-major).
 //
-// Per CTA (352 threads): shared memory Q 128 rows x 256 dims (64 KB), K half tiles 64 keys x
-// 256 dims (2 x 32 KB), V half tiles 128 keys x 128 dims (2 x 32 KB), output staging 32 KB;
-// tensor memory S[0] 0-127, S[1] 128-255 (P_j as f16 pairs in the first 64 columns of its slot),
-// O 256-511 (this CTA's 128 rows).
-//   warp 0     TMA producer of Q and the K halves (pair loads completing on the leader's barriers)
-//   warp 10    TMA producer of the V halves
+// Per CTA (480 threads): shared memory Q 128 rows x 256 dims (64 KB), a ring of four 32 KB
+// operand slots that the MMAs consume in issue order (K_0, then per tile j K_{j+1} when there is
+// one, and V_j; a K slot is 64 keys x 256 dims, a V slot 128 keys x 128 dims), and 16 KB of
+// output staging.  Tensor memory: S[0] 0-127, S[1] 128-255 (P_j as f16 pairs in the first 64
+// columns of its slot), O 256-511 (this CTA's 128 rows).
+//   warp 0     TMA producer of the K / V ring (pair loads completing on the leader's barriers)
+//   warp 10    TMA producer of Q: the next item's Q loads as soon as the item's last S completes
 //   warp 1     leader: MMA issuer (commits to both CTAs' barriers); peer: idle
-//   warps 2-9  softmax and output for this CTA's 128 rows: the two warps of a lane quadrant take
-//              64 of the 128 keys of a tile (and 128 of the 256 O columns), exchange row maxima,
-//              rescale O lazily (the reference moves only past 2^12) and write P over their slot.
+//   warps 2-9  softmax for this CTA's 128 rows: the two warps of a lane quadrant take 64 of the
+//              128 keys of a tile (and 128 of the 256 O columns when rescaling), exchange row
+//              maxima, rescale O lazily (the reference moves only past 2^12), write P over
+//              their slot, and at the end of an item hand 1/l of each row to the drain warps
+//   warps 11-14 drain: one per lane quadrant, O of the finished item to global memory while the
+//              softmax warps start the next item
 // The leader's MMA learns that P_j (or a drained O) is ready from its own 8 warps' arrivals and
 // from one 4-byte st.async token per peer warp counted on the same barrier (a remote
-// mbarrier.arrive.release.cluster per warp and tile would stall the peer's warps).
+// mbarrier.arrive.release.cluster per warp and tile would stall the peer's warps).  It waits on
+// those barriers with the plain (CTA-scope) try_wait, as CUTLASS's pair GEMMs do for barriers
+// their peer arrives on: the cluster-scope acquire form cost ~300 cycles per wait on the MMA
+// thread's critical path even when the phase had long completed.
 #pragma once
 #include "attention_tc.cuh"
 
@@ -38,10 +45,14 @@ constexpr uint32_t kFpKChunk = 64 * 128;           // 8 KB: 64 keys x 64 dims
 constexpr uint32_t kFpKBytes = 4 * kFpKChunk;      // 32 KB: this CTA's 64 keys x 256 dims
 constexpr uint32_t kFpVChunk = 128 * 128;          // 16 KB: 128 keys x 64 dims
 constexpr uint32_t kFpVBytes = 2 * kFpVChunk;      // 32 KB: 128 keys x this CTA's 128 dims
-constexpr uint32_t kFpStageBytes = 8 * 4096;
+constexpr uint32_t kFpSlotBytes = 32768;           // one ring slot: a K or a V tile half
+constexpr int kFpSlots = 4;
+constexpr uint32_t kFpStageBytes = 4 * 4096;       // output staging: 32 rows x 128 B per drain warp
+constexpr int kFpThreads = 480;                    // 15 warps (roles below)
+static_assert(kFpKBytes == kFpSlotBytes && kFpVBytes == kFpSlotBytes, "K and V tile halves share the ring");
 constexpr uint32_t kFpBarBytes = 512;              // barriers, then the token slots
-constexpr uint32_t kFpXchBytes = 2 * 2 * 128 * 4;
-constexpr size_t kFpSmem = kFpQBytes + 2 * kFpKBytes + 2 * kFpVBytes + kFpStageBytes + kFpBarBytes + kFpXchBytes;
+constexpr uint32_t kFpXchBytes = 2 * 2 * 128 * 4 + 2 * 128 * 4;  // row maxima / sums, then 1/l per row [2][128]
+constexpr size_t kFpSmem = kFpQBytes + kFpSlots * kFpSlotBytes + kFpStageBytes + kFpBarBytes + kFpXchBytes;
 static_assert(kFpSmem <= 232448, "shared memory per CTA");
 constexpr uint32_t kFpTmemO = 256;
 
@@ -50,17 +61,25 @@ struct FpItem {
   int tok0, len, qp0, q0, qcol, kcol, vcol, t_lo, n_tiles;
 };
 
-// p.q_blocks counts 256-query pair blocks here
-__device__ __forceinline__ FpItem fp_item(const FaParams& p, int item, uint32_t rank) {
+// p.q_blocks counts 256-query pair blocks here.  An item's two cu_seqlens entries are loaded
+// one item ahead (fp_bounds) and only used the next time round (fp_item): anything computed
+// from a load right after issuing it would stall the role for the load's ~1k cycles at every
+// item boundary.
+__device__ __forceinline__ void fp_bounds(const FaParams& p, int item, int& s0, int& s1) {
+  const int b = item / (p.q_blocks * p.n_q_heads);
+  s0 = __ldg(p.cu_seqlens + b);
+  s1 = __ldg(p.cu_seqlens + b + 1);
+}
+
+__device__ __forceinline__ FpItem fp_item(const FaParams& p, int item, uint32_t rank, int seq0, int seq1) {
   FpItem w;
   const int per_seq = p.q_blocks * p.n_q_heads;
   const int b = item / per_seq;
   const int r = item - b * per_seq;
   const int pb = r / p.n_q_heads;
   const int head = r - pb * p.n_q_heads;
-  const int seq0 = __ldg(p.cu_seqlens + b);
   w.tok0 = seq0 - p.cu_base;
-  w.len = __ldg(p.cu_seqlens + b + 1) - seq0;
+  w.len = seq1 - seq0;
   w.qp0 = pb * 2 * kFpBQ;
   w.q0 = w.qp0 + static_cast<int>(rank) * kFpBQ;
   w.valid = w.qp0 < w.len;  // the same for both CTAs of the pair
@@ -78,64 +97,69 @@ __device__ __forceinline__ FpItem fp_item(const FaParams& p, int item, uint32_t 
   return w;
 }
 
-// tmQV: qkv with 64 x 128 boxes (Q rows and V keys), tmK: qkv with 64 x 64 boxes (K keys),
-// tmO: the output [T, Hq * 256] with 64 x 32 boxes.
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFaThreads, 1)
+// tmQV: qkv with 64 x 128 boxes (Q rows and V keys), tmK: qkv with 64 x 64 boxes (K keys).
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFpThreads, 1)
     flash_attn_pair_kernel(const __grid_constant__ CUtensorMap tmQV, const __grid_constant__ CUtensorMap tmK,
-                           const __grid_constant__ CUtensorMap tmO, const FaParams p) {
+                           const FaParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   if (smem_u32(smem_raw) & 1023) {  // the same in both CTAs: both leave before any cluster step
     if (threadIdx.x == 0) record_error(p.status, kErrBadArgs);
     return;
   }
   uint8_t* sQ = smem_raw;
-  uint8_t* sK = sQ + kFpQBytes;            // [2][4][64 x 128 B]
-  uint8_t* sV = sK + 2 * kFpKBytes;        // [2][2][128 x 128 B]
-  uint8_t* sStage = sV + 2 * kFpVBytes;    // [8 warps][32 x 128 B]
+  uint8_t* sRing = sQ + kFpQBytes;  // [5] K slot: [4][64 x 128 B]; V slot: [2][128 x 128 B]
+  uint8_t* sStage = sRing + kFpSlots * kFpSlotBytes;  // [8 warps][32 x 128 B]
   uint64_t* bar = reinterpret_cast<uint64_t*>(sStage + kFpStageBytes);
-  uint64_t* q_full = bar;        // leader: both CTAs' Q
-  uint64_t* q_empty = bar + 1;   // Q buffer free (the item's last S has completed)
-  uint64_t* k_full = bar + 2;    // [2] leader: both K halves
-  uint64_t* k_empty = bar + 4;   // [2]
-  uint64_t* v_full = bar + 6;    // [2] leader: both V halves
-  uint64_t* v_empty = bar + 8;   // [2]
-  uint64_t* s_full = bar + 10;   // [2]
-  uint64_t* p_full = bar + 12;   // [2] leader: 8 local arrivals + 8 peer tokens
-  uint64_t* pv_done = bar + 14;  // [2]
-  uint64_t* o_free = bar + 16;   // leader: O drained in both CTAs (8 local + 8 peer tokens)
+  uint64_t* q_full = bar;            // leader: both CTAs' Q
+  uint64_t* q_empty = bar + 1;       // Q buffer free (the item's last S has completed)
+  uint64_t* ring_full = bar + 2;     // [4] leader: both CTAs' halves of the slot
+  uint64_t* ring_empty = bar + 6;    // [4]
+  uint64_t* s_full = bar + 10;       // [2]
+  uint64_t* p_full = bar + 12;       // [2] leader: 8 local arrivals + 8 peer tokens
+  uint64_t* pv_done = bar + 14;      // [2]
+  uint64_t* o_free = bar + 16;       // leader: O drained in both CTAs (8 local + 8 peer tokens)
   uint64_t* drain = bar + 17;
-  uint64_t* xbar = bar + 18;     // [4]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 22);
+  uint64_t* xbar = bar + 18;         // [4]
+  uint64_t* l_ready = bar + 22;      // [2] per item parity: 1/l of every row written (4 softmax warps)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 24);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   uint32_t* tokens = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(bar) + 256);  // [3][8]: p[0], p[1], o
   float* xch = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bar) + kFpBarBytes);  // [2][2][128]
+  float* inv_l = xch + 2 * 2 * 128;  // [2][128]: 1 / l per row, by item parity
 
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
   const int pair = static_cast<int>(cluster_id_x());
   const int n_pairs = static_cast<int>(n_clusters_x());
   const int n_items = p.n_seq * p.q_blocks * p.n_q_heads;
+  // each pair takes a contiguous run of items: the (query block, head) items of a sequence
+  // follow one another, so its K / V tiles come from HBM for the first of them and from L2
+  // for the rest (with items dealt round-robin, six pairs fetched the same tiles at once and
+  // every one of them waited on HBM)
+  const int item_lo = static_cast<int>(static_cast<int64_t>(pair) * n_items / n_pairs);
+  const int item_hi = static_cast<int>(static_cast<int64_t>(pair + 1) * n_items / n_pairs);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     mbar_init(q_empty, 1);
+    for (int i = 0; i < kFpSlots; ++i) {
+      mbar_init(&ring_full[i], 1);
+      mbar_init(&ring_empty[i], 1);
+    }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&k_full[i], 1);
-      mbar_init(&k_empty[i], 1);
-      mbar_init(&v_full[i], 1);
-      mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 8);
       mbar_init(&pv_done[i], 1);
     }
-    mbar_init(o_free, 8);
+    mbar_init(o_free, 4);
+    mbar_init(&l_ready[0], 4);
+    mbar_init(&l_ready[1], 4);
     mbar_init(drain, 1);
     for (int q = 0; q < 4; ++q) mbar_init(&xbar[q], 2);
     *abort_flag = 0;
     fence_barrier_init();
     tma_prefetch_desc(&tmQV);
     tma_prefetch_desc(&tmK);
-    tma_prefetch_desc(&tmO);
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_slot, 512);
@@ -148,33 +172,48 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFaThreads, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      // ------------------------------------------------------------------ Q / K producer
-      int it = 0;
-      uint32_t g = 0;
+      // ------------------------------------------------------------------ K / V ring producer
+      // slot order per item: K_0, then per tile j: K_{j+1} (if any), V_j -- the MMA order
+      uint32_t r = 0;
       bool ok = true;
-      for (int item = pair; ok && item < n_items; item += n_pairs) {
-        const FpItem w = fp_item(p, item, rank);
-        if (!w.valid) continue;
-        if (!mbar_wait(q_empty, (it & 1) ^ 1, abort_flag)) {
-          ok = false;
-          break;
-        }
-        if (leader) mbar_arrive_expect_tx(q_full, 2 * kFpQBytes);
-        const uint32_t qbar = mapa_shared(smem_u32(q_full), 0);
-        for (int c = 0; c < 4; ++c) tma_load_2d_pair(sQ + c * kFpQChunk, &tmQV, qbar, w.qcol + 64 * c, w.tok0 + w.q0);
-        for (int j = 0; j < w.n_tiles; ++j, ++g) {
-          const int st = g & 1;
-          const int row = w.tok0 + (w.t_lo + j) * kFpBKV + static_cast<int>(rank) * 64;
-          if (!mbar_wait(&k_empty[st], ((g >> 1) & 1) ^ 1, abort_flag)) {
-            ok = false;
-            break;
-          }
-          if (leader) mbar_arrive_expect_tx(&k_full[st], 2 * kFpKBytes);
-          const uint32_t kbar = mapa_shared(smem_u32(&k_full[st]), 0);
+      auto fill = [&](bool is_k, const FpItem& w, int j) -> bool {
+        const int slot = static_cast<int>(r % kFpSlots);
+        if (!mbar_wait(&ring_empty[slot], ((r / kFpSlots) & 1) ^ 1, abort_flag)) return false;
+        if (leader) mbar_arrive_expect_tx(&ring_full[slot], 2 * kFpSlotBytes);
+        const uint32_t fb = mapa_shared(smem_u32(&ring_full[slot]), 0);
+        uint8_t* dst = sRing + slot * kFpSlotBytes;
+        const int key0 = w.tok0 + (w.t_lo + j) * kFpBKV;
+        if (is_k) {
           for (int c = 0; c < 4; ++c)
-            tma_load_2d_pair(sK + st * kFpKBytes + c * kFpKChunk, &tmK, kbar, w.kcol + 64 * c, row);
+            tma_load_2d_pair(dst + c * kFpKChunk, &tmK, fb, w.kcol + 64 * c, key0 + static_cast<int>(rank) * 64);
+        } else {
+          for (int c = 0; c < 2; ++c)
+            tma_load_2d_pair(dst + c * kFpVChunk, &tmQV, fb, w.vcol + static_cast<int>(rank) * 128 + 64 * c, key0);
         }
-        ++it;
+        ++r;
+        return true;
+      };
+      int nb0, nb1;
+      if (item_lo < item_hi) fp_bounds(p, item_lo, nb0, nb1);
+      for (int item = item_lo; ok && item < item_hi; ++item) {
+        const FpItem w = fp_item(p, item, rank, nb0, nb1);
+        if (item + 1 < item_hi) fp_bounds(p, item + 1, nb0, nb1);  // in flight during this item
+        if (!w.valid) continue;
+        ok = fill(true, w, 0);
+        for (int j = 0; ok && j < w.n_tiles; ++j) {
+          if (j + 1 < w.n_tiles) ok = fill(true, w, j + 1);
+          if (ok) ok = fill(false, w, j);
+        }
+        // the next item's first two tiles towards L2 (its start waits on them); this role runs
+        // ahead of the MMAs, so waiting here for the next item's bounds costs nothing
+        FpItem wn{};
+        if (item + 1 < item_hi) wn = fp_item(p, item + 1, rank, nb0, nb1);
+        if (wn.valid)
+          for (int j = 0; j < min(2, wn.n_tiles); ++j) {
+            const int key0 = wn.tok0 + (wn.t_lo + j) * kFpBKV;
+            for (int c = 0; c < 4; ++c) tma_prefetch_l2_2d(&tmK, wn.kcol + 64 * c, key0 + static_cast<int>(rank) * 64);
+            for (int c = 0; c < 2; ++c) tma_prefetch_l2_2d(&tmQV, wn.vcol + static_cast<int>(rank) * 128 + 64 * c, key0);
+          }
       }
       if (!ok) {
         if (!*abort_flag) record_error(p.status, kErrTimeoutProducer);
@@ -183,25 +222,29 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFaThreads, 1)
     }
   } else if (warp == 10) {
     if (lane == 0) {
-      // ------------------------------------------------------------------ V producer
-      uint32_t g = 0;
+      // ------------------------------------------------------------------ Q producer
+      int it = 0;
       bool ok = true;
-      for (int item = pair; ok && item < n_items; item += n_pairs) {
-        const FpItem w = fp_item(p, item, rank);
+      int nb0, nb1;
+      if (item_lo < item_hi) fp_bounds(p, item_lo, nb0, nb1);
+      for (int item = item_lo; ok && item < item_hi; ++item) {
+        const FpItem w = fp_item(p, item, rank, nb0, nb1);
+        if (item + 1 < item_hi) fp_bounds(p, item + 1, nb0, nb1);  // in flight during this item
         if (!w.valid) continue;
-        for (int j = 0; j < w.n_tiles; ++j, ++g) {
-          const int st = g & 1;
-          const int row = w.tok0 + (w.t_lo + j) * kFpBKV;
-          if (!mbar_wait(&v_empty[st], ((g >> 1) & 1) ^ 1, abort_flag)) {
-            ok = false;
-            break;
-          }
-          if (leader) mbar_arrive_expect_tx(&v_full[st], 2 * kFpVBytes);
-          const uint32_t vbar = mapa_shared(smem_u32(&v_full[st]), 0);
-          for (int c = 0; c < 2; ++c)
-            tma_load_2d_pair(sV + st * kFpVBytes + c * kFpVChunk, &tmQV, vbar,
-                             w.vcol + static_cast<int>(rank) * 128 + 64 * c, row);
+        if (!mbar_wait(q_empty, (it & 1) ^ 1, abort_flag)) {
+          ok = false;
+          break;
         }
+        if (leader) mbar_arrive_expect_tx(q_full, 2 * kFpQBytes);
+        const uint32_t qbar = mapa_shared(smem_u32(q_full), 0);
+        for (int c = 0; c < 4; ++c) tma_load_2d_pair(sQ + c * kFpQChunk, &tmQV, qbar, w.qcol + 64 * c, w.tok0 + w.q0);
+        // the next item's Q rows come from HBM (read once): start them towards L2 now, so the
+        // load issued when this item's last S completes does not wait ~2 us on HBM
+        FpItem wn{};
+        if (item + 1 < item_hi) wn = fp_item(p, item + 1, rank, nb0, nb1);
+        if (wn.valid)
+          for (int c = 0; c < 4; ++c) tma_prefetch_l2_2d(&tmQV, wn.qcol + 64 * c, wn.tok0 + wn.q0);
+        ++it;
       }
       if (!ok) {
         if (!*abort_flag) record_error(p.status, kErrTimeoutProducer);
@@ -213,70 +256,107 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFaThreads, 1)
       // ------------------------------------------------------------------ MMA issuer (leader)
       constexpr uint32_t idesc_s = idesc_f16(256, kFpBKV, 0);
       constexpr uint32_t idesc_pv = idesc_f16(256, kFaD, 0) | (1u << 16);  // B (V) MN-major
-      auto commit_both = [&](uint64_t* b) {
-        umma_commit_pair(smem_u32(b));
-        umma_commit_pair(mapa_shared(smem_u32(b), 1));
+      auto commit_both = [&](uint64_t* b) { umma_commit_pair_both(smem_u32(b)); };
+      uint32_t r = 0;  // ring position, in step with the producer
+      auto take_slot = [&](int* slot) -> bool {
+        *slot = static_cast<int>(r % kFpSlots);
+        if (!mbar_wait(&ring_full[*slot], (r / kFpSlots) & 1, abort_flag)) return false;
+        ++r;
+        return true;
       };
-      auto issue_s = [&](uint32_t gx) -> bool {
-        const int st = gx & 1;
-        if (!mbar_wait(&k_full[st], (gx >> 1) & 1, abort_flag)) return false;
-        tc_fence_after();
-        const uint32_t d = tmem + static_cast<uint32_t>(st * kFpBKV);
+      // S_gx = Q K^T into S slot gx & 1; `mid` runs after the first 8 of the 16 MMAs
+      auto issue_s = [&](uint32_t gx, int slot, auto&& mid) {
+        const uint32_t d = tmem + static_cast<uint32_t>((gx & 1) * kFpBKV);
+        uint8_t* sK = sRing + slot * kFpSlotBytes;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           const uint64_t qd = desc_kmajor_sw128(smem_u32(sQ + c * kFpQChunk));
-          const uint64_t kd = desc_kmajor_sw128(smem_u32(sK + st * kFpKBytes + c * kFpKChunk));
+          const uint64_t kd = desc_kmajor_sw128(smem_u32(sK + c * kFpKChunk));
 #pragma unroll
           for (int k = 0; k < 4; ++k) umma_f16_pair(d, qd + 2 * k, kd + 2 * k, idesc_s, (c | k) != 0 ? 1u : 0u);
+          if (c == 1) mid();
         }
-        commit_both(&s_full[st]);
-        commit_both(&k_empty[st]);
-        return true;
       };
+      // Per item: S_0 and S_1, then per tile j one run of MMAs: PV_j, S_{j+2} (into P_j's slot,
+      // which PV_j has read by then: the pipe runs in order).  Only a few MMAs queue ahead of
+      // the pipe, so this thread keeps pace with it, and a wait after a run -- even on a phase
+      // that completed long ago costs ~200 cycles -- leaves the pipe idle.  So in the middle
+      // of each run the thread probes (test_wait, non-blocking) the barriers the next run
+      // needs; when all have completed, the run after it starts without waiting.
       int it = 0;
       uint32_t g = 0;
       bool ok = true;
       bool issued = false;
-      for (int item = pair; ok && item < n_items; item += n_pairs) {
-        const FpItem w = fp_item(p, item, rank);
+      int nb0, nb1;
+      if (item_lo < item_hi) fp_bounds(p, item_lo, nb0, nb1);
+      for (int item = item_lo; ok && item < item_hi; ++item) {
+        const FpItem w = fp_item(p, item, rank, nb0, nb1);
+        if (item + 1 < item_hi) fp_bounds(p, item + 1, nb0, nb1);  // in flight during this item
         if (!w.valid) continue;
-        if (!mbar_wait(q_full, it & 1, abort_flag)) {
+        const int n = w.n_tiles;
+        int ks0, ks1 = -1;
+        if (!mbar_wait(q_full, it & 1, abort_flag) || !take_slot(&ks0) || (n > 1 && !take_slot(&ks1))) {
           ok = false;
           break;
         }
         tc_fence_after();
         issued = true;
-        if (!issue_s(g)) {
-          ok = false;
-          break;
+        auto nothing = [] {};
+        issue_s(g, ks0, nothing);
+        commit_both(&s_full[g & 1]);
+        if (n > 1) {
+          issue_s(g + 1, ks1, nothing);
+          commit_both(&s_full[(g + 1) & 1]);
         }
-        for (int j = 0; j < w.n_tiles; ++j) {
+        if (n <= 2) commit_both(q_empty);  // every S of this item issued: Q is free once they complete
+        commit_both(&ring_empty[ks0]);
+        if (n > 1) commit_both(&ring_empty[ks1]);
+        bool ready = false;  // tile j's barriers found complete by the probe in the previous run
+        for (int j = 0; j < n; ++j) {
           const uint32_t gj = g + j;
           const int st = gj & 1;
-          if (j + 1 < w.n_tiles) {
-            if (!issue_s(gj + 1)) {
-              ok = false;
-              break;
-            }
-          } else {
-            commit_both(q_empty);  // every S of this item issued: Q is free once they complete
+          int vslot, kslot = -1;
+          if (ready) {
+            vslot = static_cast<int>(r++ % kFpSlots);
+            if (j + 2 < n) kslot = static_cast<int>(r++ % kFpSlots);
+          } else if (!take_slot(&vslot) || (j + 2 < n && !take_slot(&kslot)) ||
+                     !mbar_wait(&p_full[st], (gj >> 1) & 1, abort_flag)) {
+            ok = false;
+            break;
           }
-          if (!mbar_wait_cluster(&p_full[st], (gj >> 1) & 1, abort_flag) ||
-              !mbar_wait(&v_full[st], (gj >> 1) & 1, abort_flag) ||
-              (j == 0 && it >= 1 && !mbar_wait_cluster(o_free, (it - 1) & 1, abort_flag))) {
+          if (j == 0 && it >= 1 && !mbar_wait(o_free, (it - 1) & 1, abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
+          // the probe for tile j + 1: its V slot, its K slot (S_{j+3}) and P_{j+1}
+          ready = false;
+          auto probe = [&] {
+            if (j + 1 >= n) return;
+            const uint32_t gn = gj + 1;
+            ready = mbar_test_wait(&ring_full[r % kFpSlots], (r / kFpSlots) & 1) &&
+                    (j + 3 >= n ||
+                     mbar_test_wait(&ring_full[(r + 1) % kFpSlots], ((r + 1) / kFpSlots) & 1)) &&
+                    mbar_test_wait(&p_full[gn & 1], (gn >> 1) & 1);
+          };
+          uint8_t* sV = sRing + vslot * kFpSlotBytes;
 #pragma unroll
           for (int k = 0; k < 8; ++k) {  // 16 keys per step: 16 rows of 128 B in V, 8 TMEM columns of P
-            const uint64_t vd = desc_mnmajor_sw128(smem_u32(sV + st * kFpVBytes + k * 16 * 128), kFpVChunk, 1024);
+            const uint64_t vd = desc_mnmajor_sw128(smem_u32(sV + k * 16 * 128), kFpVChunk, 1024);
             umma_f16_pair_ts(tmem + kFpTmemO, tmem + st * kFpBKV + k * 8, vd, idesc_pv, (j | k) != 0 ? 1u : 0u);
+            if (k == 4 && kslot < 0) probe();
           }
           commit_both(&pv_done[st]);
-          commit_both(&v_empty[st]);
+          commit_both(&ring_empty[vslot]);  // released when PV_j completes: its refill starts a run earlier
+          if (kslot >= 0) {
+            issue_s(gj + 2, kslot, probe);
+            commit_both(&s_full[st]);
+            if (j + 3 == n) commit_both(q_empty);
+            commit_both(&ring_empty[kslot]);
+          }
+          if (ready) tc_fence_after();
         }
-        g += w.n_tiles;
+        g += n;
         ++it;
       }
       if (!ok) {
@@ -299,7 +379,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFaThreads, 1)
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16);
     constexpr float kLog2e = 1.4426950408889634f;
     // readiness for the leader's MMA: local arrival there, a 4-byte token from the peer
-    const uint32_t lead_p0 = mapa_shared(smem_u32(&p_full[0]), 0), lead_o = mapa_shared(smem_u32(o_free), 0);
+    const uint32_t lead_p0 = mapa_shared(smem_u32(&p_full[0]), 0);
     const uint32_t tok0 = mapa_shared(smem_u32(tokens), 0) + static_cast<uint32_t>(ew) * 4u;
     auto signal = [&](uint64_t* local_bar, uint32_t lead_bar, uint32_t slot) {
       if (lane != 0) return;
@@ -322,14 +402,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFaThreads, 1)
       xslot ^= 1u;
       return true;
     };
-    uint8_t* stage = sStage + ew * (kFaOutBoxRows * 128);
-    bool stores_pending = false;
     uint32_t g = 0;
     int it = 0;
     bool ok = true;
     uint32_t sa[32], sb[32];
-    for (int item = pair; ok && item < n_items; item += n_pairs) {
-      const FpItem w = fp_item(p, item, rank);
+    int nb0, nb1;
+    if (item_lo < item_hi) fp_bounds(p, item_lo, nb0, nb1);
+    for (int item = item_lo; ok && item < item_hi; ++item) {
+      const FpItem w = fp_item(p, item, rank, nb0, nb1);
+      if (item + 1 < item_hi) fp_bounds(p, item + 1, nb0, nb1);  // in flight during this item
       if (!w.valid) continue;
       const int i = w.q0 + r;
       float m_ref = -INFINITY, l = 0.f;
@@ -394,31 +475,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFaThreads, 1)
         // 64-key kernel is not needed: the exchange costs little next to 64 keys of work)
         const float mref = m_new == -INFINITY ? 0.f : m_new;
         m_ref = m_new;
-        // O may be rescaled only after P_{j-1} V_{j-1} has landed
-        if (j >= 1 && __any_sync(0xffffffffu, factor != 1.0f)) {
-          const bool wt = mbar_wait(&pv_done[(gj - 1) & 1], ((gj - 1) >> 1) & 1, abort_flag);
-          if (!__all_sync(0xffffffffu, wt)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint64_t f2x = f2(factor, factor);
-#pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
-            uint32_t oa[32];
-            const uint32_t ta = lane_base + kFpTmemO + half * 128 + c * 32;
-            tmem_ld32(ta, oa);
-            tmem_ld_wait_tied(oa);
-#pragma unroll
-            for (int e = 0; e < 32; e += 2) {
-              float a, b;
-              f2_split(f2_mul(f2(u2f(oa[e]), u2f(oa[e + 1])), f2x), a, b);
-              oa[e] = __float_as_uint(a);
-              oa[e + 1] = __float_as_uint(b);
-            }
-            tmem_st32(ta, oa);
-          }
-        }
         // P row r, this warp's 64 keys in two rounds of 32: 16 columns of f16 pairs each, over
         // the first 64 columns of the S slot
         const uint64_t l2e = f2(kLog2e, kLog2e), nmu = f2(-mref, -mref);
@@ -450,6 +506,40 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFaThreads, 1)
           tmem_st16(lane_base + st * kFpBKV + half * 32 + h2 * 16, pk);
         }
         l = l * factor + lsum;
+        // O may be rescaled only after P_{j-1} V_{j-1} has landed.  Done after the exponentials:
+        // PV_{j-1} has mostly finished by then, where waiting for it first stalled this warp
+        // ~1k cycles on most tiles when logits are spread wide (some row of the 32 almost always
+        // moves its maximum past the lazy threshold)
+        if (j >= 1 && __any_sync(0xffffffffu, factor != 1.0f)) {
+          const bool wt = mbar_wait(&pv_done[(gj - 1) & 1], ((gj - 1) >> 1) & 1, abort_flag);
+          if (!__all_sync(0xffffffffu, wt)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t f2x = f2(factor, factor);
+          // 128 columns as two loads of 64 in flight together (sa / sb are free by now)
+#pragma unroll 1
+          for (int c = 0; c < 2; ++c) {
+            const uint32_t ta = lane_base + kFpTmemO + half * 128 + c * 64;
+            tmem_ld32(ta, sa);
+            tmem_ld32(ta + 32, sb);
+            tmem_ld_wait_tied(sa);
+            tmem_ld_wait_tied(sb);
+#pragma unroll
+            for (int e = 0; e < 32; e += 2) {
+              float a, b;
+              f2_split(f2_mul(f2(u2f(sa[e]), u2f(sa[e + 1])), f2x), a, b);
+              sa[e] = __float_as_uint(a);
+              sa[e + 1] = __float_as_uint(b);
+              f2_split(f2_mul(f2(u2f(sb[e]), u2f(sb[e + 1])), f2x), a, b);
+              sb[e] = __float_as_uint(a);
+              sb[e + 1] = __float_as_uint(b);
+            }
+            tmem_st32(ta, sa);
+            tmem_st32(ta + 32, sb);
+          }
+        }
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
@@ -469,40 +559,80 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFaThreads, 1)
         }
       }
       if (!ok) break;
-      // ---- drain O of this item (the next item's Q load and S_0 are already in flight)
-      const uint32_t gl = g + w.n_tiles - 1;
-      const bool wt = mbar_wait(&pv_done[gl & 1], (gl >> 1) & 1, abort_flag);
-      if (!__all_sync(0xffffffffu, wt)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
+      // ---- the row sums to the drain warps (they store O once PV of the last tile lands);
+      // this warp goes straight on to the next item's S_0
       publish(l);
       float l_other;
       if (!collect(&l_other)) {
         ok = false;
         break;
       }
-      const float lt = l + l_other;
-      const float inv = lt > 0.f ? 1.0f / lt : 0.f;
+      if (half == 0) {
+        const float lt = l + l_other;
+        inv_l[(it & 1) * 128 + r] = lt > 0.f ? 1.0f / lt : 0.f;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&l_ready[it & 1]);
+      }
+      g += w.n_tiles;
+      ++it;
+    }
+    if (lane == 0 && !ok) {
+      if (!*abort_flag) record_error(p.status, kErrTimeoutEpilogue);
+      *abort_flag = 1;
+    }
+  } else if (warp >= 11 && warp <= 14) {
+    // -------------------------------------------------------------------- drain of O
+    // Warp (quad q) stores rows 32q.. of this CTA's 128: all 256 columns, 64 at a time, staged
+    // (swizzled) in shared memory and written as 4 rows x 128 contiguous bytes per store.  The
+    // SM writes to L2 at ~32 B/cycle, so the 64 KB of O per item take ~2k cycles: off the
+    // softmax warps, they overlap the next item's S_0, S_1 and first softmax.  O's tensor memory
+    // is released (o_free) once its last columns are in registers.
+    const int quad = warp & 3;
+    const int dw = warp - 11;
+    const int r = quad * 32 + lane;
+    const uint32_t ob_base = tmem + (static_cast<uint32_t>(quad * 32) << 16) + kFpTmemO;
+    const uint32_t lead_o = mapa_shared(smem_u32(o_free), 0);
+    const uint32_t tok = mapa_shared(smem_u32(tokens), 0) + 2u * 32u + static_cast<uint32_t>(dw) * 4u;
+    uint8_t* stage = sStage + dw * 4096;
+    uint32_t g = 0;
+    int it = 0;
+    bool ok = true;
+    int nb0, nb1;
+    if (item_lo < item_hi) fp_bounds(p, item_lo, nb0, nb1);
+    for (int item = item_lo; ok && item < item_hi; ++item) {
+      const FpItem w = fp_item(p, item, rank, nb0, nb1);
+      if (item + 1 < item_hi) fp_bounds(p, item + 1, nb0, nb1);  // in flight during this item
+      if (!w.valid) continue;
+      const uint32_t gl = g + w.n_tiles - 1;
+      const bool wt = mbar_wait(&l_ready[it & 1], (it >> 1) & 1, abort_flag) &&
+                      mbar_wait(&pv_done[gl & 1], (gl >> 1) & 1, abort_flag);
+      if (!__all_sync(0xffffffffu, wt)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const float inv = inv_l[(it & 1) * 128 + r];
       const uint64_t inv2 = f2(inv, inv);
-      const int row0 = w.q0 + quad * kFaOutBoxRows;
-      const bool any_rows = row0 < w.len;
-      const bool bulk = row0 + kFaOutBoxRows <= w.len;
-      const uint32_t ob_base = lane_base + kFpTmemO + half * 128;
+      const int row0 = w.q0 + quad * 32;
+      const int rows = min(32, w.len - row0);  // rows of this warp inside the sequence
 #pragma unroll 1
-      for (int k = 0; k < 2; ++k) {  // two slices of 64 output columns
+      for (int k = 0; k < 4; ++k) {  // four slices of 64 output columns
         uint32_t oa[32], ob[32];
         tmem_ld32(ob_base + k * 64, oa);
         tmem_ld32(ob_base + k * 64 + 32, ob);
-        if (stores_pending) {  // the previous slice's bulk store has read the staging tile
-          if (lane == 0) bulk_wait_read_all();
-          stores_pending = false;
-        }
-        __syncwarp();
         tmem_ld_wait_tied(oa);
         tmem_ld_wait_tied(ob);
-        if (!any_rows) continue;  // every row of this warp lies past the sequence
+        if (k == 3) {  // all of O read: the next item's PV may overwrite it
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            if (leader)
+              mbar_arrive_expect_tx(o_free, 4);
+            else
+              st_async_b32(tok, 1u, lead_o);
+          }
+        }
+        if (rows <= 0) continue;  // every row of this warp lies past the sequence
         uint8_t* srow = stage + lane * 128;
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
@@ -516,39 +646,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFaThreads, 1)
           }
           *reinterpret_cast<uint4*>(srow + ((c ^ (lane & 7)) << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
         }
-        const int col = w.qcol + half * 128 + k * 64;
-        if (bulk) {
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            tma_store_2d(&tmO, stage, col, w.tok0 + row0);
-            bulk_commit();
-          }
-          stores_pending = true;
-        } else {
-          __syncwarp();
-#pragma unroll 1
-          for (int rr = 0; rr < kFaOutBoxRows; rr += 4) {
-            const int row = rr + (lane >> 3), c = lane & 7;
-            const uint4 v = *reinterpret_cast<const uint4*>(stage + row * 128 + ((c ^ (row & 7)) << 4));
-            if (row0 + row < w.len)
-              *reinterpret_cast<uint4*>(p.out + static_cast<size_t>(w.tok0 + row0 + row) * p.ld_out + col + c * 8) = v;
-          }
-          __syncwarp();
+        __syncwarp();
+        const int col = w.qcol + k * 64 + (lane & 7) * 8;
+#pragma unroll
+        for (int rr = 0; rr < 32; rr += 4) {
+          const int row = rr + (lane >> 3), c = lane & 7;
+          const uint4 v = *reinterpret_cast<const uint4*>(stage + row * 128 + ((c ^ (row & 7)) << 4));
+          if (row < rows) *reinterpret_cast<uint4*>(p.out + static_cast<size_t>(w.tok0 + row0 + row) * p.ld_out + col) = v;
         }
+        __syncwarp();
       }
-      tc_fence_before();
-      __syncwarp();
-      signal(o_free, lead_o, 2u);
       g += w.n_tiles;
       ++it;
     }
-    if (lane == 0) {
-      bulk_wait_all();
-      if (!ok) {
-        if (!*abort_flag) record_error(p.status, kErrTimeoutEpilogue);
-        *abort_flag = 1;
-      }
+    if (lane == 0 && !ok) {
+      if (!*abort_flag) record_error(p.status, kErrTimeoutEpilogue);
+      *abort_flag = 1;
     }
   }
 

@@ -134,11 +134,9 @@ int launch_attention(const __half* qkv, int64_t T, int qkv_width, const int* cu,
   const char* attn_env = std::getenv("GLP_ATTENTION");  // read per call (A/B measurements)
   const bool single = attn_env && std::strcmp(attn_env, "single") == 0;
   if (!single) {
-    CUtensorMap mqv, mk, mo;
+    CUtensorMap mqv, mk;
     GLP_TRY(make_map16(&mqv, qkv, T, qkv_width, qkv_width, glp::kFpBQ, true));
     GLP_TRY(make_map16(&mk, qkv, T, qkv_width, qkv_width, 64, true));
-    GLP_TRY(make_map16(&mo, out, T, static_cast<int64_t>(n_q_heads) * glp::kFaD,
-                       static_cast<int64_t>(n_q_heads) * glp::kFaD, glp::kFaOutBoxRows, true));
     glp::FaParams fp{};
     fp.cu_seqlens = cu;
     fp.cu_base = cu_base;
@@ -152,7 +150,7 @@ int launch_attention(const __half* qkv, int64_t T, int qkv_width, const int* cu,
     fp.status = status;
     const int64_t items = static_cast<int64_t>(n_seq) * fp.q_blocks * n_q_heads;
     const int pairs = static_cast<int>(std::min<int64_t>(items, std::max(1, sm_count() / 2)));
-    glp::flash_attn_pair_kernel<<<2 * pairs, glp::kFaThreads, glp::kFpSmem, st>>>(mqv, mk, mo, fp);
+    glp::flash_attn_pair_kernel<<<2 * pairs, glp::kFpThreads, glp::kFpSmem, st>>>(mqv, mk, fp);
     GLP_CUDA(cudaGetLastError());
     return GLP_OK;
   }
