@@ -72,6 +72,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Programmatic dependent launch: a kernel launched with programmatic stream serialization
+// may start before the previous kernel in the stream has finished; griddep_wait() returns once
+// that kernel's writes are visible (immediately for an ordinary launch).  griddep_launch()
+// lets the next such kernel start its prologue now.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // Non-blocking probe: has the phase with the given parity completed?
 __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;

@@ -145,6 +145,9 @@ __device__ __forceinline__ bool gemm_epilogue_tile(const GemmParams& p, uint32_t
     constexpr int SLICE = 128 / ELT;
     constexpr int NSL = BN / 2 / SLICE;
     const int col0 = n_blk * BN + half * (BN / 2);
+    // a last tile past N (N a multiple of 128 but not of BN: the B rows there are the TMA's
+    // zero fill) stores nothing from this warp's half
+    if (col0 >= p.N) return true;
     const size_t ld_bytes = static_cast<size_t>(p.ldc) * ELT;
     uint8_t* dst0 = reinterpret_cast<uint8_t*>(p.C) + (static_cast<size_t>(wrow0) * p.ldc + col0) * ELT;
     const uint32_t tbase = tacc + half * (BN / 2);
@@ -387,6 +390,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 0) {
     if (lane == 0) {
       // ------------------------------------------------------------ TMA producer
+      griddep_wait();  // (see gemm_pair_kernel)
       int s = 0;
       uint32_t ph = 0;
       for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
@@ -598,6 +602,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   if (warp == 0) {
     if (lane == 0) {
       // ------------------------------------------------------------ TMA producer (both CTAs)
+      // Everything this kernel reads or writes in global memory follows the producer's
+      // loads, so this one wait orders it after the previous kernel under a dependent launch.
+      griddep_wait();
       int s = 0;
       uint32_t ph = 0;
       for (int tile = pair; tile < num_tiles && !*abort_flag; tile += n_pairs) {

@@ -363,16 +363,45 @@ int launch_rownorm_gemm(const CUtensorMap& ma, const CUtensorMap& mb_pair, const
 // Launch C = A * B^T with the given epilogue; T is the 16-bit operand type.  `ma` covers
 // A [M, K] (box rows 128), `mb` covers B [N, K] with box rows == bn; `mb_pair` (optional,
 // box rows 128) lets 256-wide tiles run on CTA pairs.
+// One launch of the CTA-pair GEMM; with `dependent` as a programmatic dependent launch (its
+// prologue overlaps the previous kernel, its producer waits for that kernel's writes).
+template <int EPI, typename T>
+cudaError_t launch_pair_gemm(dim3 grid, size_t smem, cudaStream_t st, bool dependent, const CUtensorMap& ma,
+                             const CUtensorMap& mb, const CUtensorMap& mc, const GemmParams& p) {
+  if (!dependent) {
+    glp::gemm_pair_kernel<EPI, T><<<grid, glp::kGemmThreads, smem, st>>>(ma, mb, mc, p);
+    return cudaGetLastError();
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(glp::kGemmThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, glp::gemm_pair_kernel<EPI, T>, ma, mb, mc, p);
+}
+
 template <typename T>
 int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, int bn, int epi, GemmParams p, cudaStream_t st,
-                const CUtensorMap* mb_pair = nullptr, const CUtensorMap* mc = nullptr) {
+                const CUtensorMap* mb_pair = nullptr, const CUtensorMap* mc = nullptr, bool dependent = false) {
   p.m_tiles = (p.M + 127) / 128;
   p.n_tiles = p.N / bn;
   p.k_blocks = p.K / 64;
   if (p.M <= 0) return GLP_OK;
-  if (p.K % 64 || p.N % bn || p.K <= 0) return fail(GLP_ERR_INVALID_ARG, "GEMM needs K % 64 == 0 and N % tile == 0");
+  if (p.K % 64 || p.K <= 0 || p.N % 128) return fail(GLP_ERR_INVALID_ARG, "GEMM needs K % 64 == 0 and N % 128 == 0");
   const bool f16 = std::is_same<T, __half>::value;
-  if (bn == 256 && mb_pair && pair_gemm_for(epi, p.M, p.n_tiles)) {
+  // plain stores with N % 256 == 128 may still take 256-wide pair tiles: the last one's second
+  // half lies past N (zero-filled B rows, nothing stored), which beats 128-wide tiles' 1.5x
+  // operand bytes per MMA once the tiles fill the device
+  const bool store_epi = epi == glp::kEpiStore16 || epi == glp::kEpiF32;
+  const int pair_n_tiles = store_epi ? (p.N + 255) / 256 : p.N / 256;
+  if ((bn == 256 || (store_epi && p.N % 256)) && mb_pair && (store_epi || p.N % 256 == 0) &&
+      pair_gemm_for(epi, p.M, pair_n_tiles)) {
+    p.n_tiles = pair_n_tiles;
     if ((epi == glp::kEpiQkv || epi == glp::kEpiGeglu || epi == glp::kEpiMulGeglu) && !f16)
       return fail(GLP_ERR_INVALID_ARG, "fused epilogues run on f16 operands");
     p.m_tiles = (p.M + 255) / 256;  // 256-row pair tiles
@@ -380,8 +409,8 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, int bn, int epi, G
     const size_t smem = glp::GemmPairCfg::SMEM;
     const dim3 grid(static_cast<unsigned>(2 * pairs));
     switch (epi) {
-      case glp::kEpiStore16: glp::gemm_pair_kernel<glp::kEpiStore16, T><<<grid, glp::kGemmThreads, smem, st>>>(ma, *mb_pair, ma, p); break;
-      case glp::kEpiF32: glp::gemm_pair_kernel<glp::kEpiF32, T><<<grid, glp::kGemmThreads, smem, st>>>(ma, *mb_pair, ma, p); break;
+      case glp::kEpiStore16: GLP_CUDA((launch_pair_gemm<glp::kEpiStore16, T>(grid, smem, st, dependent, ma, *mb_pair, ma, p))); break;
+      case glp::kEpiF32: GLP_CUDA((launch_pair_gemm<glp::kEpiF32, T>(grid, smem, st, dependent, ma, *mb_pair, ma, p))); break;
       case glp::kEpiQkv:
         if (!mc) return fail(GLP_ERR_INVALID_ARG, "the QKV epilogue needs the output's tensor map");
         glp::gemm_pair_kernel<glp::kEpiQkv, __half><<<grid, glp::kGemmThreads, smem, st>>>(ma, *mb_pair, *mc, p);
@@ -395,6 +424,7 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, int bn, int epi, G
     GLP_CUDA(cudaGetLastError());
     return GLP_OK;
   }
+  if (p.N % bn) return fail(GLP_ERR_INVALID_ARG, "GEMM needs N % tile == 0");
   const int tiles = p.m_tiles * p.n_tiles;
   const int grid = std::min(tiles, sm_count());
   if (bn == 256) {
@@ -1791,7 +1821,8 @@ int device_status_word(int dev, int** out) {
   return GLP_OK;
 }
 
-int run_bf16_gemm(const __nv_bfloat16* w, int N, int K, const void* x, int M, void* y, int y_is_f32, cudaStream_t st) {
+int run_bf16_gemm(const __nv_bfloat16* w, int N, int K, const void* x, int M, void* y, int y_is_f32, cudaStream_t st,
+                  bool dependent = false) {
   if (N <= 0 || K <= 0 || M < 0 || N % 128 || K % 64)
     return fail(GLP_ERR_INVALID_ARG, "GEMM needs N % 128 == 0, K % 64 == 0, M >= 0");
   if (!w || !x || !y) return fail(GLP_ERR_INVALID_ARG, "null pointer");
@@ -1813,7 +1844,8 @@ int run_bf16_gemm(const __nv_bfloat16* w, int N, int K, const void* x, int M, vo
   p.C = y;
   p.ldc = N;
   p.status = status;
-  return launch_gemm<__nv_bfloat16>(ma, mb, bn, y_is_f32 ? glp::kEpiF32 : glp::kEpiStore16, p, st, &mbp);
+  return launch_gemm<__nv_bfloat16>(ma, mb, bn, y_is_f32 ? glp::kEpiF32 : glp::kEpiStore16, p, st, &mbp, nullptr,
+                                    dependent);
 }
 
 }  // namespace
@@ -2219,7 +2251,8 @@ int glp_q8_0_gemm(const void* d_q8_w, int N, int K, const void* d_x_bf16, int M,
   glp::q8_0_dequant_rows_kernel<__nv_bfloat16><<<static_cast<unsigned>((nb + 255) / 256), 256, 0, st>>>(
       static_cast<const uint8_t*>(d_q8_w), N, K, w, 0, 0, 0);
   GLP_CUDA(cudaGetLastError());
-  return run_bf16_gemm(w, N, K, d_x_bf16, M, d_y, y_is_f32, st);
+  // the GEMM as the dequantisation's dependent launch: its prologue overlaps that kernel
+  return run_bf16_gemm(w, N, K, d_x_bf16, M, d_y, y_is_f32, st, true);
 }
 
 int glp_bf16_gemm(const void* d_w_bf16, int N, int K, const void* d_x_bf16, int M, void* d_y, int y_is_f32,

@@ -38,6 +38,7 @@ __global__ void q8_0_dequant_f32_kernel(const uint8_t* __restrict__ blocks, int6
 template <typename T>
 __global__ void q8_0_dequant_rows_kernel(const uint8_t* __restrict__ blocks, int n, int k, T* __restrict__ dst,
                                          int row_base, int group, int group_stride) {
+  griddep_launch();  // a GEMM launched after this one as its dependent may start its prologue
   const int nb = k / 32;
   const int64_t b = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (b >= static_cast<int64_t>(n) * nb) return;

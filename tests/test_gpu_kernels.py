@@ -104,12 +104,15 @@ def _gemm_check(blocks, n, k, m, d_w_ptr, f32_out, seed):
     assert np.abs(got - ref).max() <= tol * np.abs(ref).max()
 
 
-@pytest.mark.parametrize("n,k", [(768, 768), (1152, 768), (768, 1152), (256, 64)])
+@pytest.mark.parametrize("n,k", [(768, 768), (1152, 768), (768, 1152), (256, 64), (384, 768)])
 @pytest.mark.parametrize("m", [8192, 8193])
 def test_q8_0_gemm_both_routes(n, k, m):
     """M = 8192 runs the kernel that streams raw Q8_0 rows and dequantises in shared memory
     (every group-row view: K = 768 and 1152 take 1 and 2 rows per TMA row, K = 64 four), M =
-    8193 the dequantise-then-GEMM route; both against bf16(q d) operands with f32 accumulation."""
+    8193 the dequantise-then-GEMM route; both against bf16(q d) operands with f32 accumulation.
+    N = 1152 and 384 (odd multiples of 128) run the second route's CTA-pair GEMM with a last
+    256-wide tile half past N: every output is written (NaN-filled beforehand) and nothing
+    spills into the next row."""
     blocks = _q8_blocks(n, k, seed=n + k + m)
     d_w = _dev(blocks.view(np.uint8).reshape(-1))
     _gemm_check(blocks, n, k, m, d_w.data_ptr(), True, seed=m)
