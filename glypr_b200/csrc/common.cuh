@@ -470,14 +470,16 @@ __device__ __forceinline__ void umma_commit_pair(uint32_t cluster_addr) {
   asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_addr)
                : "memory");
 }
-// The same arriving once on the barrier at this shared-memory offset in both CTAs of the pair
-// (CTA ranks 0 and 1 of the cluster): one instruction instead of one commit per CTA.
-__device__ __forceinline__ void umma_commit_pair_both(uint32_t smem_addr) {
+// The same arriving once on the barrier at this shared-memory offset in each CTA of cta_mask
+// (bit r = cluster rank r): one instruction instead of one commit per CTA.
+__device__ __forceinline__ void umma_commit_pair_mask(uint32_t smem_addr, uint16_t cta_mask) {
   asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
                    smem_addr),
-               "h"(static_cast<uint16_t>(3))
+               "h"(cta_mask)
                : "memory");
 }
+// ... in both CTAs of a cluster of two
+__device__ __forceinline__ void umma_commit_pair_both(uint32_t smem_addr) { umma_commit_pair_mask(smem_addr, 3); }
 
 // ------------------------------------------------------------------------- coalesced row stores
 // Row-per-thread output through a per-warp staging tile: thread `lane` puts its

@@ -644,8 +644,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(ab * Cfg::BN);
         bool ok = true;
+        // Few MMAs queue ahead of the pipe, so this thread issues at the pipe's pace, and a wait
+        // on the next stage after the step's last MMA -- ~200 cycles even for a phase that
+        // completed long ago -- idles the pipe once per K step.  Halfway through each step the
+        // next stage's barrier is probed (non-blocking); when it has completed, the next step
+        // starts without waiting.
+        bool ready = false;
         for (int kb = 0; kb < p.k_blocks; ++kb) {
-          if (!mbar_wait(&full[s], ph, abort_flag)) {
+          if (!ready && !mbar_wait(&full[s], ph, abort_flag)) {
             record_error(p.status, kErrTimeoutMma);
             *abort_flag = 1;
             ok = false;
@@ -654,20 +660,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
           tc_fence_after();
           const uint64_t adesc = desc_kmajor_sw128(smem_u32(sA + s * Cfg::A_BYTES));
           const uint64_t bdesc = desc_kmajor_sw128(smem_u32(sB + s * Cfg::B_BYTES));
+          const int s1 = s + 1 == STAGES ? 0 : s + 1;
+          const uint32_t ph1 = s + 1 == STAGES ? ph ^ 1u : ph;
 #pragma unroll
-          for (int k = 0; k < Cfg::BK / 16; ++k)
+          for (int k = 0; k < Cfg::BK / 16; ++k) {
             umma_f16_pair(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
-          issued = true;
-          umma_commit_pair(smem_u32(&empty[s]));                  // this CTA's stage
-          umma_commit_pair(mapa_shared(smem_u32(&empty[s]), 1));  // the peer's stage
-          if (++s == STAGES) {
-            s = 0;
-            ph ^= 1;
+            if (k == 1) ready = kb + 1 < p.k_blocks && mbar_test_wait(&full[s1], ph1);
           }
+          issued = true;
+          umma_commit_pair_both(smem_u32(&empty[s]));  // the stage in both CTAs
+          s = s1;
+          ph = ph1;
         }
         if (!ok) break;
-        umma_commit_pair(smem_u32(&tfull[ab]));
-        umma_commit_pair(mapa_shared(smem_u32(&tfull[ab]), 1));
+        umma_commit_pair_both(smem_u32(&tfull[ab]));
         ab ^= 1;
         if (ab == 0) aph ^= 1;
       }
@@ -901,7 +907,7 @@ __global__ void __cluster_dims__(2 * NP, 1, 1) __launch_bounds__(kGemmThreads, 1
     if (lane == 0 && leader) {
       // ------------------------------------------------------------ MMA issuer (pair leaders)
       constexpr uint32_t idesc = idesc_f16(256, 256, Half16<T>::kIsBf16);
-      const uint32_t peer = rank | 1u;
+      const uint16_t pair_mask = static_cast<uint16_t>(3u << rank);  // this leader (even rank) and its peer
       int s = 0;
       uint32_t ph = 0;
       int ab = 0;
@@ -916,8 +922,9 @@ __global__ void __cluster_dims__(2 * NP, 1, 1) __launch_bounds__(kGemmThreads, 1
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(ab * 256);
         bool ok = true;
+        bool ready = false;  // the mid-step probe of the next stage (as in gemm_pair_kernel)
         for (int kb = 0; kb < p.k_blocks; ++kb) {
-          if (!mbar_wait(&full[s], ph, abort_flag)) {
+          if (!ready && !mbar_wait(&full[s], ph, abort_flag)) {
             record_error(p.status, kErrTimeoutMma);
             *abort_flag = 1;
             ok = false;
@@ -926,20 +933,20 @@ __global__ void __cluster_dims__(2 * NP, 1, 1) __launch_bounds__(kGemmThreads, 1
           tc_fence_after();
           const uint64_t adesc = desc_kmajor_sw128(smem_u32(sA + s * Cfg::A_BYTES));
           const uint64_t bdesc = desc_kmajor_sw128(smem_u32(sB + s * Cfg::B_BYTES));
+          const int s1 = s + 1 == STAGES ? 0 : s + 1;
+          const uint32_t ph1 = s + 1 == STAGES ? ph ^ 1u : ph;
 #pragma unroll
-          for (int k = 0; k < 4; ++k)
+          for (int k = 0; k < 4; ++k) {
             umma_f16_pair(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
-          issued = true;
-          umma_commit_pair(smem_u32(&empty[s]));
-          umma_commit_pair(mapa_shared(smem_u32(&empty[s]), peer));
-          if (++s == STAGES) {
-            s = 0;
-            ph ^= 1;
+            if (k == 1) ready = kb + 1 < p.k_blocks && mbar_test_wait(&full[s1], ph1);
           }
+          issued = true;
+          umma_commit_pair_mask(smem_u32(&empty[s]), pair_mask);  // the stage in both CTAs of the pair
+          s = s1;
+          ph = ph1;
         }
         if (!ok) break;
-        umma_commit_pair(smem_u32(&tfull[ab]));
-        umma_commit_pair(mapa_shared(smem_u32(&tfull[ab]), peer));
+        umma_commit_pair_mask(smem_u32(&tfull[ab]), pair_mask);
         ab ^= 1;
         if (ab == 0) aph ^= 1;
       }
