@@ -37,7 +37,7 @@ struct GemmParams {
   // kEpiQkv
   const float* q_gain;    // [head_dim]
   const float* k_gain;    // [head_dim]
-  const float2* rope_cs;  // [head_dim/2, rope_stride] {cos, sin}, frequency-major
+  const float2* rope_cs;  // {cos, sin} of two frequencies per position: [head_dim/4, rope_stride] float4
   const int* pos;         // [M] position of each row inside its sequence
   int rope_stride;        // positions per frequency row (the model's context length)
   int n_q_heads, n_kv_heads;
@@ -251,18 +251,20 @@ __device__ __forceinline__ bool gemm_epilogue_tile(const GemmParams& p, uint32_t
     const bool rope = is_q || is_k;
     // positions outside the table read its last row instead of past its end
     const int pos = live ? min(max(p.pos[row], 0), p.rope_stride - 1) : 0;
-    // frequency-major {cos, sin} table: lanes (consecutive rows) read consecutive positions,
-    // one 8-byte load per frequency
-    const float2* tab = p.rope_cs + pos;
+    // frequency-pair-major {cos, sin} table: lanes (consecutive rows) read consecutive
+    // positions, one 16-byte load per two frequencies
+    const float4* tab = reinterpret_cast<const float4*>(p.rope_cs) + pos;
     const size_t fstride = static_cast<size_t>(p.rope_stride);
     const int f0 = half * 64;  // this warp's frequencies [f0, f0 + 64), 8 chunks of 8
     float cva[8], sva[8], cvb[8], svb[8];
     auto load_tab = [&](int k, float (&cv)[8], float (&sv)[8]) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float2 t = __ldg(tab + static_cast<size_t>(f0 + 8 * k + j) * fstride);
+      for (int j = 0; j < 8; j += 2) {
+        const float4 t = __ldg(tab + static_cast<size_t>((f0 + 8 * k + j) >> 1) * fstride);
         cv[j] = t.x;
         sv[j] = t.y;
+        cv[j + 1] = t.z;
+        sv[j + 1] = t.w;
       }
     };
     if (rope) load_tab(0, cva, sva);  // in flight during pass 1

@@ -978,8 +978,10 @@ int upload_linear(Device& d, const glp::GgufFile& g, const std::string& name, in
 // freqs = f32(pos) * inv_freq (f32), cos/sin in f32.  Only the first half is stored (the
 // reference table is cat(freqs, freqs)), frequency-major [half][max_pos] so that the GEMM
 // epilogue's 32 lanes (consecutive rows = consecutive positions) read one coalesced line.
-// RoPE table, frequency-major with cos and sin of one (frequency, position) side by side:
-// cs[i * max_pos + p] = {cos(p * inv_freq_i), sin(p * inv_freq_i)} (rope.rs:14-76 values)
+// RoPE table (rope.rs:14-76 values) with cos and sin of two consecutive frequencies side by
+// side, frequency-pair-major: as float4, cs4[(i / 2) * max_pos + p] = {cos(p f_i), sin(p f_i),
+// cos(p f_i+1), sin(p f_i+1)} for even i, so the QKV epilogue's lanes (consecutive rows =
+// consecutive positions) read two frequencies per 16-byte load and a warp one coalesced 512 B.
 // position_major: cs[p * half + i] instead (the 512-wide row kernel reads a lane's 8
 // consecutive frequencies of one position).
 int upload_rope(Device& d, double theta, int d_head, int max_pos, float2** cs, bool position_major = false) {
@@ -990,7 +992,8 @@ int upload_rope(Device& d, double theta, int d_head, int max_pos, float2** cs, b
   for (int i = 0; i < half; ++i)
     for (int p = 0; p < max_pos; ++p) {
       const float f = static_cast<float>(p) * inv[i];
-      const size_t at = position_major ? static_cast<size_t>(p) * half + i : static_cast<size_t>(i) * max_pos + p;
+      const size_t at = position_major ? static_cast<size_t>(p) * half + i
+                                       : (static_cast<size_t>(i >> 1) * max_pos + p) * 2 + (i & 1);
       c[at] = make_float2(std::cos(f), std::sin(f));
     }
   GLP_TRY(d.alloc(cs, c.size()));
@@ -1797,7 +1800,7 @@ int kernel_rope_table(int dev, double theta, int max_pos, const float2** out) {
   for (int i = 0; i < kHalf; ++i)
     for (int p = 0; p < max_pos; ++p) {
       const float f = static_cast<float>(p) * inv[i];
-      c[static_cast<size_t>(i) * max_pos + p] = make_float2(std::cos(f), std::sin(f));
+      c[(static_cast<size_t>(i >> 1) * max_pos + p) * 2 + (i & 1)] = make_float2(std::cos(f), std::sin(f));
     }
   float2* cs = nullptr;
   GLP_CUDA(cudaMalloc(&cs, c.size() * sizeof(float2)));
