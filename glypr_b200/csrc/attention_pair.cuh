@@ -21,19 +21,18 @@
 //   warp 10    TMA producer of Q: the next item's Q loads as soon as the item's last S completes
 //              (L2 prefetches of the next item's Q and first K / V tiles measured 2.5 % slower:
 //              they added a quarter to the DRAM reads and did not shorten the loads)
-//   warp 1     leader: MMA issuer (commits to both CTAs' barriers); peer: idle
+//   warp 1     leader: MMA issuer (one multicast commit reaches both CTAs' barriers); peer: idle
 //   warps 2-9  softmax for this CTA's 128 rows: the two warps of a lane quadrant take 64 of the
 //              128 keys of a tile (and 128 of the 256 O columns when rescaling), exchange row
 //              maxima, rescale O lazily (the reference moves only past 2^12), write P over
 //              their slot, and at the end of an item hand 1/l of each row to the drain warps
 //   warps 11-14 drain: one per lane quadrant, O of the finished item to global memory while the
 //              softmax warps start the next item
-// The leader's MMA learns that P_j (or a drained O) is ready from its own 8 warps' arrivals and
+// The leader's MMA learns that P_j (or a drained O) is ready from its own warps' arrivals and
 // from one 4-byte st.async token per peer warp counted on the same barrier (a remote
 // mbarrier.arrive.release.cluster per warp and tile would stall the peer's warps).  It waits on
 // those barriers with the plain (CTA-scope) try_wait, as CUTLASS's pair GEMMs do for barriers
-// their peer arrives on: the cluster-scope acquire form cost ~300 cycles per wait on the MMA
-// thread's critical path even when the phase had long completed.
+// their peer arrives on.
 #pragma once
 #include "attention_tc.cuh"
 
