@@ -47,6 +47,11 @@ constexpr uint32_t kFpKBytes = 4 * kFpKChunk;      // 32 KB: this CTA's 64 keys 
 constexpr uint32_t kFpVChunk = 128 * 128;          // 16 KB: 128 keys x 64 dims
 constexpr uint32_t kFpVBytes = 2 * kFpVChunk;      // 32 KB: 128 keys x this CTA's 128 dims
 constexpr uint32_t kFpSlotBytes = 32768;           // one ring slot: a K or a V tile half
+// 2^x pairs of a softmax round taken by the FMA-pipe polynomial instead of MUFU ex2: none.  The
+// one-CTA kernel's split (6 of 16) measured 3 % slower here (0.424 vs 0.412 ms on 512 x
+// 512-token sequences; 4 of 16: 0.419, 8: 0.432) -- these softmax warps are bound by issue
+// slots, not by the special-function unit.
+constexpr uint32_t kFpPolyPairs = 0;
 constexpr int kFpSlots = 4;
 constexpr uint32_t kFpStageBytes = 4 * 4096;       // output staging: 32 rows x 128 B per drain warp
 constexpr int kFpThreads = 480;                    // 15 warps (roles below)
@@ -473,7 +478,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFpThreads, 1)
           for (int e = 0; e < 16; ++e) {
             const uint64_t x = f2_fma(f2(u2f(sx[2 * e]), u2f(sx[2 * e + 1])), l2e, nmu);
             uint64_t ev;
-            if ((kFaPolyPairs >> e) & 1u) {
+            if ((kFpPolyPairs >> e) & 1u) {
               ev = exp2_poly_pair(x);
             } else {
               float a, b;
