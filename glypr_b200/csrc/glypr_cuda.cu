@@ -23,6 +23,7 @@
 #include <string>
 #include <thread>
 #include <type_traits>
+#include <unordered_map>
 #include <vector>
 
 #include "attention_tc.cuh"
@@ -78,6 +79,44 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
+// Encoded maps by their arguments.  A map holds the address, shape, strides, box and layout and
+// nothing of the data, so the map made for the same arguments stays valid (also for memory
+// freed and allocated again at the same address); the standalone entry points build the same
+// few maps on every call, and a lookup costs less than an encode.  Bounded: emptied when full.
+struct MapKey {
+  const void* base;
+  int64_t a, b, c;
+  int box, kind;
+  bool operator==(const MapKey& o) const {
+    return base == o.base && a == o.a && b == o.b && c == o.c && box == o.box && kind == o.kind;
+  }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    size_t h = std::hash<const void*>()(k.base);
+    for (int64_t v : {k.a, k.b, k.c, static_cast<int64_t>(k.box), static_cast<int64_t>(k.kind)})
+      h = h * 1000003u ^ std::hash<int64_t>()(v);
+    return h;
+  }
+};
+struct MapCache {
+  std::mutex mu;
+  std::unordered_map<MapKey, CUtensorMap, MapKeyHash> maps;
+  bool get(const MapKey& k, CUtensorMap* out) {
+    std::lock_guard<std::mutex> lk(mu);
+    const auto it = maps.find(k);
+    if (it == maps.end()) return false;
+    *out = it->second;
+    return true;
+  }
+  void put(const MapKey& k, const CUtensorMap& m) {
+    std::lock_guard<std::mutex> lk(mu);
+    if (maps.size() >= 1024) maps.clear();
+    maps.emplace(k, m);
+  }
+};
+MapCache g_maps;
+
 // 2-D 16-bit row-major [rows, cols] tensor, box = 64 columns (one 128-byte swizzle row) x
 // box_rows rows, 128B swizzle, out-of-bounds rows read as zero.  f16 = true for the model
 // path's operands, false for bf16.
@@ -86,6 +125,8 @@ int make_map16(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int
   if (!fn) return fail(GLP_ERR_CUDA, "cuTensorMapEncodeTiled unavailable (driver too old?)");
   if ((reinterpret_cast<uintptr_t>(base) & 15) || (ld_elems * 2) % 16 || cols % 64)
     return fail(GLP_ERR_INVALID_ARG, "TMA operand must be 16-byte aligned with K % 64 == 0");
+  const MapKey key{base, rows, cols, ld_elems, box_rows, f16 ? 1 : 0};
+  if (g_maps.get(key, m)) return GLP_OK;
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld_elems * 2)};
   const cuuint32_t box[2] = {64u, static_cast<cuuint32_t>(box_rows)};
@@ -95,6 +136,7 @@ int make_map16(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int
                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(GLP_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string(r));
+  g_maps.put(key, *m);
   return GLP_OK;
 }
 
@@ -227,10 +269,14 @@ int ensure_kernel_attrs() {
 }
 
 int sm_count() {
+  static std::array<std::atomic<int>, 64> cached{};  // per device, read once
   int dev = 0, n = 0;
   cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && (n = cached[dev].load(std::memory_order_relaxed)) > 0) return n;
   cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-  return n > 0 ? n : 148;
+  n = n > 0 ? n : 148;
+  if (dev >= 0 && dev < 64) cached[dev].store(n, std::memory_order_relaxed);
+  return n;
 }
 
 int bn_for(int n) { return n % 256 == 0 ? 256 : 128; }
@@ -481,6 +527,8 @@ int make_map_q8_raw(CUtensorMap* m, const void* base, int N, int K, int box_rows
   const int G = q8_raw_group(K);
   if (!G || N % G) return fail(GLP_ERR_INVALID_ARG, "Q8_0 GEMM needs K % 64 == 0");
   if (reinterpret_cast<uintptr_t>(base) & 15) return fail(GLP_ERR_INVALID_ARG, "Q8_0 weight must be 16-byte aligned");
+  const MapKey key{base, N, K, 0, box_rows, 2};
+  if (g_maps.get(key, m)) return GLP_OK;
   const uint64_t row = static_cast<uint64_t>(G) * (K / 32) * 34;
   const cuuint64_t dims[2] = {row, static_cast<cuuint64_t>(N / G)};
   const cuuint64_t strides[1] = {row};
@@ -490,6 +538,7 @@ int make_map_q8_raw(CUtensorMap* m, const void* base, int N, int K, int box_rows
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(GLP_ERR_CUDA, "cuTensorMapEncodeTiled (raw Q8_0) failed: " + std::to_string(r));
+  g_maps.put(key, *m);
   return GLP_OK;
 }
 
