@@ -461,8 +461,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFpThreads, 1)
         const float joint = fmaxf(mine, other);
         const float m_new = joint > m_ref + kFaRescaleLog2 ? joint : m_ref;
         const float factor = (m_ref == -INFINITY || m_new == m_ref) ? 1.f : fast_exp2(m_ref - m_new);
-        // exponentials against the final reference directly (the speculative form of the
-        // 64-key kernel is not needed: the exchange costs little next to 64 keys of work)
+        // exponentials against the final reference directly.  The speculative form (against
+        // this warp's own choice while the partner's maximum is in flight, scaled afterwards
+        // where the joint choice differs) measured 10 % slower here: 0.60 vs 0.55 ms per
+        // 262,144-token launch, the values held in f32 across the exchange and packed after it
         const float mref = m_new == -INFINITY ? 0.f : m_new;
         m_ref = m_new;
         // P row r, this warp's 64 keys in two rounds of 32: 16 columns of f16 pairs each, over
